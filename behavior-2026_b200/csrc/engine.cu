@@ -1,0 +1,1218 @@
+// engine.cu — host side of the pi0.5 engine: weight arena, activation buffers, launch planning,
+// CUDA-graph capture, and the C ABI declared in include/pi05.h.
+//
+// Reference boundary replaced: include/pi05_batch.h of the deleted engine
+// (docs/archive/windows/π05_네이티브엔진.md:288-303).  The reference captured the per-board prefix as
+// one CUDA graph and ran the denoise for all boards at once (:298); here both the prefill and the
+// 10-step denoise of a batch are captured once per batch size and replayed.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/pi05.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "kernels.cuh"
+
+using namespace p5;
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct Tensor {
+  std::string name;
+  bf16* ptr;
+  long rows;
+  int cols;
+};
+
+struct SigLayer {
+  bf16 *ln1s, *ln1b, *wqkv, *bqkv, *wo, *bo, *ln2s, *ln2b, *w1, *b1, *w2, *b2;
+};
+struct GemLayer {
+  bf16 *rms1, *wqkv, *wo, *rms2, *wgu, *wd;
+};
+struct ExpLayer {
+  bf16 *wqkv, *wo, *wgu, *wd;
+};
+
+struct Acts {
+  uint8_t* images;
+  int32_t* tokens;
+  bf16 *patches, *sx, *sy, *sqkv, *so, *sh;
+  bf16 *px, *ph, *pqkv, *po, *pact, *kcache, *vcache;
+  bf16 *ex, *eh, *eqkv, *eo, *eact, *ek, *ev;
+  float *xt, *noise, *actions;
+};
+
+}  // namespace
+
+struct pi05_engine {
+  pi05_config cfg;
+  int device = 0, max_batch = 1, P = 968, NM = 37;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  int* d_status = nullptr;
+  EncodeTiledFn encode = nullptr;
+  int num_sms = 148;
+  bool pdl = true;
+
+  std::vector<void*> allocs;
+  char* warena = nullptr;
+  size_t wbytes = 0, wused = 0;
+  std::vector<Tensor> tensors;
+
+  // weights
+  bf16 *sig_stem_w, *sig_stem_b, *sig_posemb, *sig_post_s, *sig_post_b, *sig_head_w, *sig_head_b;
+  std::vector<SigLayer> sig;
+  bf16* embed;
+  std::vector<GemLayer> gem;
+  std::vector<ExpLayer> ex;
+  bf16 *ada_w, *ada_b, *ain_w, *ain_b, *aout_w, *aout_b, *tin_w, *tin_b, *tout_w, *tout_b;
+
+  Acts A;
+  float *d_cos = nullptr, *d_sin = nullptr;
+  bf16* mods = nullptr;  // [steps][NM*3*1024]
+  float* gemm_ws = nullptr;
+  size_t gemm_ws_bytes = 0;
+  int* counters = nullptr;
+  int n_counters = 0;
+  float *attn_ws_o = nullptr, *attn_ws_ml = nullptr;
+  size_t attn_ws_rows = 0;
+
+  bool weights_ready = false;
+  int prefix_n = 0;  // batch whose prefix cache is valid
+  std::map<int, cudaGraphExec_t> denoise_graphs, prefill_graphs;
+  std::map<int, long> denoise_launches, prefill_launches;
+  long launches = 0;  // kernels enqueued (counted at capture time)
+};
+
+namespace {
+
+bool set_err(pi05_engine* e, const std::string& s) {
+  e->err = s;
+  return false;
+}
+#define CK(call)                                                                              \
+  do {                                                                                        \
+    cudaError_t _e = (call);                                                                  \
+    if (_e != cudaSuccess) {                                                                  \
+      set_err(e, std::string(#call) + ": " + cudaGetErrorString(_e) + " @" + std::to_string(__LINE__)); \
+      return false;                                                                           \
+    }                                                                                         \
+  } while (0)
+
+bool dalloc(pi05_engine* e, void** p, size_t bytes) {
+  CK(cudaMalloc(p, bytes));
+  CK(cudaMemsetAsync(*p, 0, bytes, e->stream));
+  e->allocs.push_back(*p);
+  return true;
+}
+
+bf16* wtake(pi05_engine* e, const std::string& name, long rows, int cols) {
+  const size_t bytes = ((size_t)rows * cols * 2 + 255) & ~(size_t)255;
+  if (e->warena && e->wused + bytes > e->wbytes) return nullptr;
+  bf16* p = e->warena ? reinterpret_cast<bf16*>(e->warena + e->wused) : nullptr;
+  e->wused += bytes;
+  if (e->warena) e->tensors.push_back({name, p, rows, cols});
+  return p;
+}
+
+// Lay out every weight tensor (called twice: once to size the arena, once to assign pointers).
+void layout_weights(pi05_engine* e) {
+  const pi05_config& c = e->cfg;
+  e->wused = 0;
+  e->tensors.clear();
+  e->sig_stem_w = wtake(e, "sig.stem.w", P5_SIG_W, P5_SIG_KPAD);
+  e->sig_stem_b = wtake(e, "sig.stem.b", 1, P5_SIG_W);
+  e->sig_posemb = wtake(e, "sig.posemb", 256, P5_SIG_W);
+  e->sig.resize(c.siglip_layers);
+  for (int l = 0; l < c.siglip_layers; ++l) {
+    SigLayer& s = e->sig[l];
+    const std::string p = "sig.l" + std::to_string(l) + ".";
+    s.ln1s = wtake(e, p + "ln1.s", 1, P5_SIG_W);
+    s.ln1b = wtake(e, p + "ln1.b", 1, P5_SIG_W);
+    s.wqkv = wtake(e, p + "qkv.w", P5_SIG_QKV, P5_SIG_W);
+    s.bqkv = wtake(e, p + "qkv.b", 1, P5_SIG_QKV);
+    s.wo = wtake(e, p + "o.w", P5_SIG_W, P5_SIG_W);
+    s.bo = wtake(e, p + "o.b", 1, P5_SIG_W);
+    s.ln2s = wtake(e, p + "ln2.s", 1, P5_SIG_W);
+    s.ln2b = wtake(e, p + "ln2.b", 1, P5_SIG_W);
+    s.w1 = wtake(e, p + "mlp1.w", P5_SIG_MLP, P5_SIG_W);
+    s.b1 = wtake(e, p + "mlp1.b", 1, P5_SIG_MLP);
+    s.w2 = wtake(e, p + "mlp2.w", P5_SIG_W, P5_SIG_MLP);
+    s.b2 = wtake(e, p + "mlp2.b", 1, P5_SIG_W);
+  }
+  e->sig_post_s = wtake(e, "sig.post.s", 1, P5_SIG_W);
+  e->sig_post_b = wtake(e, "sig.post.b", 1, P5_SIG_W);
+  e->sig_head_w = wtake(e, "sig.head.w", P5_GEM_W, P5_SIG_W);
+  e->sig_head_b = wtake(e, "sig.head.b", 1, P5_GEM_W);
+  e->embed = wtake(e, "gem.embed", P5_VOCAB, P5_GEM_W);
+  e->gem.resize(c.gemma_layers);
+  for (int l = 0; l < c.gemma_layers; ++l) {
+    GemLayer& g = e->gem[l];
+    const std::string p = "gem.l" + std::to_string(l) + ".";
+    g.rms1 = wtake(e, p + "rms1", 1, P5_GEM_W);
+    g.wqkv = wtake(e, p + "qkv.w", P5_QKV, P5_GEM_W);
+    g.wo = wtake(e, p + "o.w", P5_GEM_W, P5_QDIM);
+    g.rms2 = wtake(e, p + "rms2", 1, P5_GEM_W);
+    g.wgu = wtake(e, p + "gu.w", 2 * P5_GEM_MLP, P5_GEM_W);
+    g.wd = wtake(e, p + "down.w", P5_GEM_W, P5_GEM_MLP);
+  }
+  e->ex.resize(c.expert_layers);
+  for (int l = 0; l < c.expert_layers; ++l) {
+    ExpLayer& x = e->ex[l];
+    const std::string p = "exp.l" + std::to_string(l) + ".";
+    x.wqkv = wtake(e, p + "qkv.w", P5_QKV, P5_EXP_W);
+    x.wo = wtake(e, p + "o.w", P5_EXP_W, P5_QDIM);
+    x.wgu = wtake(e, p + "gu.w", 2 * P5_EXP_MLP, P5_EXP_W);
+    x.wd = wtake(e, p + "down.w", P5_EXP_W, P5_EXP_MLP);
+  }
+  e->ada_w = wtake(e, "exp.ada.w", (long)e->NM * 3 * P5_EXP_W, P5_EXP_W);
+  e->ada_b = wtake(e, "exp.ada.b", 1, e->NM * 3 * P5_EXP_W);
+  e->ain_w = wtake(e, "action_in.w", P5_EXP_W, P5_ACT_D);
+  e->ain_b = wtake(e, "action_in.b", 1, P5_EXP_W);
+  e->aout_w = wtake(e, "action_out.w", P5_ACT_D, P5_EXP_W);
+  e->aout_b = wtake(e, "action_out.b", 1, P5_ACT_D);
+  e->tin_w = wtake(e, "time_in.w", P5_EXP_W, P5_EXP_W);
+  e->tin_b = wtake(e, "time_in.b", 1, P5_EXP_W);
+  e->tout_w = wtake(e, "time_out.w", P5_EXP_W, P5_EXP_W);
+  e->tout_b = wtake(e, "time_out.b", 1, P5_EXP_W);
+}
+
+// ------------------------------------------------------------------ launch helpers
+template <typename... KArgs, typename... Args>
+bool launch(pi05_engine* e, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = e->stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = (pdl && e->pdl) ? 1 : 0;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&lc, kern, std::forward<Args>(args)...));
+  e->launches++;
+  return true;
+}
+
+bool make_tmap(pi05_engine* e, CUtensorMap* m, const bf16* base, long rows, int K, int ld, int box_rows) {
+  if (((uintptr_t)base & 15) || (ld * 2) % 16) return set_err(e, "tensor map: misaligned operand");
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = e->encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16*>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_err(e, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return true;
+}
+
+// One linear layer y = x W^T with a fused epilogue.  x: [T][K] (ld ldx), W: [F][K] (ld ldw).
+struct Lin {
+  const bf16* x;
+  int ldx, T;
+  const bf16* w;
+  int ldw, F, K;
+  int epi = EPI_STORE;
+  bf16* out = nullptr;
+  int ld_out = 0;
+  float* out_f32 = nullptr;
+  int ld_out_f32 = 0;
+  const bf16* bias = nullptr;
+  const bf16* res = nullptr;
+  int ld_res = 0;
+  const bf16* gate = nullptr;
+  int ld_gate = 0, gate_div = 1;
+  float out_scale = 1.0f;
+  const bf16* addend = nullptr;
+  int add_ld = 0, add_mod = 1;
+};
+
+template <int BN>
+bool launch_gemm_bn(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga) {
+  dim3 grid(ga.tiles_m * ga.tiles_n, ga.splits);
+  return launch(e, gemm_tc_kernel<BN>, grid, dim3(256), (size_t)GemmCfg<BN>::SMEM, ga.pdl != 0, ta, tb, ga);
+}
+
+bool linear(pi05_engine* e, const Lin& L) {
+  GemmArgs ga = {};
+  const bool swap = L.T <= 128;
+  int BN;
+  CUtensorMap ta, tb;
+  const int kt = (L.K + 63) / 64;
+  if (swap) {
+    BN = L.T <= 64 ? 64 : 128;
+    ga.M = L.F;
+    ga.N = L.T;
+    ga.tiles_m = (L.F + 127) / 128;
+    ga.tiles_n = 1;
+    if (!make_tmap(e, &ta, L.w, L.F, L.K, L.ldw, 128) || !make_tmap(e, &tb, L.x, L.T, L.K, L.ldx, BN)) return false;
+  } else {
+    const int tm = (L.T + 127) / 128;
+    BN = (tm * ((L.F + 255) / 256) >= 2 * e->num_sms) ? 256 : 128;
+    ga.M = L.T;
+    ga.N = L.F;
+    ga.tiles_m = tm;
+    ga.tiles_n = (L.F + BN - 1) / BN;
+    if (!make_tmap(e, &ta, L.x, L.T, L.K, L.ldx, 128) || !make_tmap(e, &tb, L.w, L.F, L.K, L.ldw, BN)) return false;
+  }
+  ga.K = L.K;
+  ga.swap = swap;
+  ga.group_m = swap ? 1 : 16;
+  const int tiles = ga.tiles_m * ga.tiles_n;
+  int splits = 1;
+  if (tiles < e->num_sms && kt >= 4) {
+    splits = std::max(1, std::min(e->num_sms / tiles, kt / 2));
+    const size_t need = (size_t)splits * tiles * 128 * BN * 4;
+    while (splits > 1 && ((size_t)splits * tiles * 128 * BN * 4 > e->gemm_ws_bytes || tiles > e->n_counters)) --splits;
+    (void)need;
+  }
+  int kper = (kt + splits - 1) / splits;
+  splits = (kt + kper - 1) / kper;  // no empty split
+  ga.splits = splits;
+  ga.kt_per_split = kper;
+  ga.epi = L.epi;
+  ga.out = L.out;
+  ga.ld_out = L.ld_out;
+  ga.out_f32 = L.out_f32;
+  ga.ld_out_f32 = L.ld_out_f32;
+  ga.bias = L.bias;
+  ga.res = L.res;
+  ga.ld_res = L.ld_res;
+  ga.gate = L.gate;
+  ga.ld_gate = L.ld_gate;
+  ga.gate_div = L.gate_div;
+  ga.out_scale = L.out_scale;
+  ga.addend = L.addend;
+  ga.add_ld = L.add_ld;
+  ga.add_mod = L.add_mod;
+  ga.ws = e->gemm_ws;
+  ga.counters = e->counters;
+  ga.status = e->d_status;
+  ga.pdl = e->pdl ? 1 : 0;
+  if (BN == 64) return launch_gemm_bn<64>(e, ta, tb, ga);
+  if (BN == 128) return launch_gemm_bn<128>(e, ta, tb, ga);
+  return launch_gemm_bn<256>(e, ta, tb, ga);
+}
+
+bool attention(pi05_engine* e, const AttnArgs& a0, int batch, int hd) {
+  AttnArgs a = a0;
+  a.pdl = e->pdl ? 1 : 0;
+  const int rows = a.T * a.G;
+  const int total = a.len1 + a.len2;
+  if (a.splits < 1) a.splits = 1;
+  a.keys_per_split = ((total + a.splits - 1) / a.splits + 63) / 64 * 64;
+  a.splits = (total + a.keys_per_split - 1) / a.keys_per_split;
+  if (a.splits > 1) {
+    if ((size_t)batch * a.splits * rows > e->attn_ws_rows) {
+      a.splits = 1;
+      a.keys_per_split = total;
+    } else {
+      a.ws_o = e->attn_ws_o;
+      a.ws_ml = e->attn_ws_ml;
+    }
+  }
+  const int heads = a.G == 1 ? (hd == P5_SIG_HD ? P5_SIG_HEADS : 1) : 1;
+  dim3 grid((rows + 63) / 64, heads, batch * a.splits);
+  if (hd == P5_HD) {
+    if (!launch(e, attn_kernel<P5_HD>, grid, dim3(128), (size_t)AttnCfg<P5_HD>::SMEM, true, a)) return false;
+    if (a.splits > 1) {
+      const long n = (long)batch * rows * (P5_HD / 2);
+      if (!launch(e, attn_combine_kernel<P5_HD>, dim3((n + 255) / 256), dim3(256), 0, true, a, batch)) return false;
+    }
+    return true;
+  }
+  return launch(e, attn_kernel<P5_SIG_HD>, grid, dim3(128), (size_t)AttnCfg<P5_SIG_HD>::SMEM, true, a);
+}
+
+int rows_grid(long rows_warps) { return (int)((rows_warps * 32 + 255) / 256); }
+
+// ------------------------------------------------------------------ forward passes
+bool run_siglip(pi05_engine* e, int n) {
+  const int T = n * e->cfg.n_cameras * P5_SIG_TOK, D = P5_SIG_W;
+  Acts& A = e->A;
+  {
+    const long tot = (long)T * P5_SIG_KPAD;
+    if (!launch(e, patchify_kernel, dim3((unsigned)std::min<long>((tot + 255) / 256, 65535)), dim3(256), 0, false,
+                A.images, A.patches, n * e->cfg.n_cameras))
+      return false;
+  }
+  {
+    Lin L{A.patches, P5_SIG_KPAD, T, e->sig_stem_w, P5_SIG_KPAD, D, P5_SIG_KPAD};
+    L.out = A.sx;
+    L.ld_out = D;
+    L.bias = e->sig_stem_b;
+    L.out_scale = 1.0f / 255.0f;
+    L.addend = e->sig_posemb;
+    L.add_ld = D;
+    L.add_mod = 256;
+    if (!linear(e, L)) return false;
+  }
+  for (int l = 0; l < e->cfg.siglip_layers; ++l) {
+    const SigLayer& s = e->sig[l];
+    if (!launch(e, layernorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.sx, A.sy, s.ln1s, s.ln1b, T, D))
+      return false;
+    Lin q{A.sy, D, T, s.wqkv, D, P5_SIG_QKV, D};
+    q.out = A.sqkv;
+    q.ld_out = P5_SIG_QKV;
+    q.bias = s.bqkv;
+    if (!linear(e, q)) return false;
+    AttnArgs at = {};
+    at.q = A.sqkv;
+    at.ldq = P5_SIG_QKV;
+    at.q_bstride = (long)256 * P5_SIG_QKV;
+    at.out = A.so;
+    at.ldo = D;
+    at.o_bstride = (long)256 * D;
+    at.k1 = A.sqkv + D;
+    at.v1 = A.sqkv + 2 * D;
+    at.ld1 = P5_SIG_QKV;
+    at.len1 = 256;
+    at.b1stride = (long)256 * P5_SIG_QKV;
+    at.k2 = at.k1;
+    at.v2 = at.v1;
+    at.T = 256;
+    at.G = 1;
+    at.qdiv = P5_SIG_QDIV;
+    at.splits = 1;
+    if (!attention(e, at, n * e->cfg.n_cameras, P5_SIG_HD)) return false;
+    Lin o{A.so, D, T, s.wo, D, D, D};
+    o.epi = EPI_RESID;
+    o.out = A.sx;
+    o.ld_out = D;
+    o.bias = s.bo;
+    o.res = A.sx;
+    o.ld_res = D;
+    if (!linear(e, o)) return false;
+    if (!launch(e, layernorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.sx, A.sy, s.ln2s, s.ln2b, T, D))
+      return false;
+    Lin m1{A.sy, D, T, s.w1, D, P5_SIG_MLP, D};
+    m1.epi = EPI_GELU;
+    m1.out = A.sh;
+    m1.ld_out = P5_SIG_MLP;
+    m1.bias = s.b1;
+    if (!linear(e, m1)) return false;
+    Lin m2{A.sh, P5_SIG_MLP, T, s.w2, P5_SIG_MLP, D, P5_SIG_MLP};
+    m2.epi = EPI_RESID;
+    m2.out = A.sx;
+    m2.ld_out = D;
+    m2.bias = s.b2;
+    m2.res = A.sx;
+    m2.ld_res = D;
+    if (!linear(e, m2)) return false;
+  }
+  if (!launch(e, layernorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.sx, A.sy, e->sig_post_s, e->sig_post_b,
+              T, D))
+    return false;
+  // projector 1152 -> 2048 straight into the image rows of each sample's prefix
+  const int img_tok = e->cfg.n_cameras * P5_SIG_TOK;
+  for (int b = 0; b < n; ++b) {
+    Lin h{A.sy + (size_t)b * img_tok * D, D, img_tok, e->sig_head_w, D, P5_GEM_W, D};
+    h.out = A.px + (size_t)b * e->P * P5_GEM_W;
+    h.ld_out = P5_GEM_W;
+    h.bias = e->sig_head_b;
+    if (!linear(e, h)) return false;
+  }
+  return true;
+}
+
+bool run_gemma(pi05_engine* e, int n) {
+  const int P = e->P, T = n * P, D = P5_GEM_W;
+  Acts& A = e->A;
+  const size_t cache_layer = (size_t)e->max_batch * P * P5_HD;
+  for (int l = 0; l < e->cfg.gemma_layers; ++l) {
+    const GemLayer& g = e->gem[l];
+    if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.px, A.ph, g.rms1, (const bf16*)nullptr,
+                T, D, 1, 0))
+      return false;
+    Lin q{A.ph, D, T, g.wqkv, D, P5_QKV, D};
+    q.out = A.pqkv;
+    q.ld_out = P5_QKV;
+    if (!linear(e, q)) return false;
+    bf16* kc = A.kcache + l * cache_layer;
+    bf16* vc = A.vcache + l * cache_layer;
+    if (!launch(e, rope_qkv_kernel, dim3(T), dim3(256), 0, true, A.pqkv, T, P, 0, kc, vc, (const float*)e->d_cos,
+                (const float*)e->d_sin))
+      return false;
+    if (l == e->cfg.gemma_layers - 1) break;  // later outputs of the last layer feed nothing
+    AttnArgs at = {};
+    at.q = A.pqkv;
+    at.ldq = P5_QKV;
+    at.q_bstride = (long)P * P5_QKV;
+    at.out = A.po;
+    at.ldo = P5_QDIM;
+    at.o_bstride = (long)P * P5_QDIM;
+    at.k1 = kc;
+    at.v1 = vc;
+    at.ld1 = P5_HD;
+    at.len1 = P;
+    at.b1stride = (long)P * P5_HD;
+    at.k2 = kc;
+    at.v2 = vc;
+    at.T = P;
+    at.G = P5_NH;
+    at.qdiv = 1.0f;
+    at.splits = 1;
+    if (!attention(e, at, n, P5_HD)) return false;
+    Lin o{A.po, P5_QDIM, T, g.wo, P5_QDIM, D, P5_QDIM};
+    o.epi = EPI_RESID;
+    o.out = A.px;
+    o.ld_out = D;
+    o.res = A.px;
+    o.ld_res = D;
+    if (!linear(e, o)) return false;
+    if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.px, A.ph, g.rms2, (const bf16*)nullptr,
+                T, D, 1, 0))
+      return false;
+    Lin gu{A.ph, D, T, g.wgu, D, 2 * P5_GEM_MLP, D};
+    gu.epi = EPI_GEGLU;
+    gu.out = A.pact;
+    gu.ld_out = P5_GEM_MLP;
+    if (!linear(e, gu)) return false;
+    Lin dn{A.pact, P5_GEM_MLP, T, g.wd, P5_GEM_MLP, D, P5_GEM_MLP};
+    dn.epi = EPI_RESID;
+    dn.out = A.px;
+    dn.ld_out = D;
+    dn.res = A.px;
+    dn.ld_res = D;
+    if (!linear(e, dn)) return false;
+  }
+  return true;
+}
+
+bool run_prefill_body(pi05_engine* e, int n) {
+  if (!run_siglip(e, n)) return false;
+  if (e->cfg.n_text > 0 &&
+      !launch(e, embed_text_kernel, dim3(e->cfg.n_text, n), dim3(256), 0, true, (const int32_t*)e->A.tokens,
+              (const bf16*)e->embed, e->A.px, e->cfg.n_text, e->P, e->cfg.n_cameras * P5_SIG_TOK))
+    return false;
+  return run_gemma(e, n);
+}
+
+bool run_denoise_body(pi05_engine* e, int n) {
+  const int H = e->cfg.horizon, T = n * H, D = P5_EXP_W, P = e->P;
+  Acts& A = e->A;
+  const size_t cache_layer = (size_t)e->max_batch * P * P5_HD;
+  const int MW = e->NM * 3 * D;  // modulation row width
+  const float dtb = p5_dt_bf16(e->cfg.num_steps);
+  const int attn_splits = n <= 4 ? 8 : 1;
+  for (int s = 0; s < e->cfg.num_steps; ++s) {
+    const bf16* mrow = e->mods + (size_t)s * MW;
+    if (!launch(e, action_in_kernel, dim3((T * D + 255) / 256), dim3(256), 0, true, (const float*)A.xt,
+                (const bf16*)e->ain_w, (const bf16*)e->ain_b, A.ex, T, D))
+      return false;
+    for (int l = 0; l < e->cfg.expert_layers; ++l) {
+      const ExpLayer& x = e->ex[l];
+      const bf16* m1 = mrow + (size_t)(2 * l) * 3 * D;
+      const bf16* m2 = mrow + (size_t)(2 * l + 1) * 3 * D;
+      if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m1, m1 + D, T, D, 1, 0))
+        return false;
+      Lin q{A.eh, D, T, x.wqkv, D, P5_QKV, D};
+      q.out = A.eqkv;
+      q.ld_out = P5_QKV;
+      if (!linear(e, q)) return false;
+      if (!launch(e, rope_qkv_kernel, dim3(T), dim3(256), 0, true, A.eqkv, T, H, P, A.ek, A.ev, (const float*)e->d_cos,
+                  (const float*)e->d_sin))
+        return false;
+      AttnArgs at = {};
+      at.q = A.eqkv;
+      at.ldq = P5_QKV;
+      at.q_bstride = (long)H * P5_QKV;
+      at.out = A.eo;
+      at.ldo = P5_QDIM;
+      at.o_bstride = (long)H * P5_QDIM;
+      at.k1 = A.kcache + l * cache_layer;
+      at.v1 = A.vcache + l * cache_layer;
+      at.ld1 = P5_HD;
+      at.len1 = P;
+      at.b1stride = (long)P * P5_HD;
+      at.k2 = A.ek;
+      at.v2 = A.ev;
+      at.ld2 = P5_HD;
+      at.len2 = H;
+      at.b2stride = (long)H * P5_HD;
+      at.T = H;
+      at.G = P5_NH;
+      at.qdiv = 1.0f;
+      at.splits = attn_splits;
+      if (!attention(e, at, n, P5_HD)) return false;
+      Lin o{A.eo, P5_QDIM, T, x.wo, P5_QDIM, D, P5_QDIM};
+      o.epi = EPI_GATED;
+      o.out = A.ex;
+      o.ld_out = D;
+      o.res = A.ex;
+      o.ld_res = D;
+      o.gate = m1 + 2 * D;
+      o.ld_gate = 0;
+      o.gate_div = 1;
+      if (!linear(e, o)) return false;
+      if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m2, m2 + D, T, D, 1, 0))
+        return false;
+      Lin gu{A.eh, D, T, x.wgu, D, 2 * P5_EXP_MLP, D};
+      gu.epi = EPI_GEGLU;
+      gu.out = A.eact;
+      gu.ld_out = P5_EXP_MLP;
+      if (!linear(e, gu)) return false;
+      Lin dn{A.eact, P5_EXP_MLP, T, x.wd, P5_EXP_MLP, D, P5_EXP_MLP};
+      dn.epi = EPI_GATED;
+      dn.out = A.ex;
+      dn.ld_out = D;
+      dn.res = A.ex;
+      dn.ld_res = D;
+      dn.gate = m2 + 2 * D;
+      dn.ld_gate = 0;
+      dn.gate_div = 1;
+      if (!linear(e, dn)) return false;
+    }
+    const bf16* mf = mrow + (size_t)(e->NM - 1) * 3 * D;
+    if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, mf, mf + D, T, D, 1, 0))
+      return false;
+    if (!launch(e, action_out_euler_kernel, dim3(rows_grid((long)T * P5_ACT_D)), dim3(256), 0, true,
+                (const bf16*)A.eh, (const bf16*)e->aout_w, (const bf16*)e->aout_b, A.xt, (float*)nullptr, T, D, dtb))
+      return false;
+  }
+  return true;
+}
+
+// Capture `body` once per batch size and replay it.
+bool run_graph(pi05_engine* e, std::map<int, cudaGraphExec_t>& cache, std::map<int, long>& counts, int n,
+               bool (*body)(pi05_engine*, int)) {
+  auto it = cache.find(n);
+  if (it == cache.end()) {
+    cudaGraph_t g = nullptr;
+    const long before = e->launches;
+    CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    const bool ok = body(e, n);
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+    if (!ok) {
+      if (g) cudaGraphDestroy(g);
+      return false;
+    }
+    if (ce != cudaSuccess) return set_err(e, std::string("graph capture: ") + cudaGetErrorString(ce));
+    cudaGraphExec_t ex = nullptr;
+    ce = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return set_err(e, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+    counts[n] = e->launches - before;
+    it = cache.emplace(n, ex).first;
+  }
+  CK(cudaGraphLaunch(it->second, e->stream));
+  return true;
+}
+
+bool is_device_ptr(const void* p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+bool copy_in(pi05_engine* e, void* dst, const void* src, size_t bytes) {
+  CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, e->stream));
+  return true;
+}
+
+bool check_status(pi05_engine* e) {
+  int st = 0;
+  CK(cudaMemcpy(&st, e->d_status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (st != 0) {
+    CK(cudaMemset(e->d_status, 0, sizeof(int)));
+    return set_err(e, "device-side wait gave up (status " + std::to_string(st) + ")");
+  }
+  return true;
+}
+
+int fail_code(pi05_engine* e) {
+  return e->err.rfind("device-side", 0) == 0 ? PI05_ERR_DEVICE : PI05_ERR_CUDA;
+}
+
+// time conditioning -> modulation table for every step (depends only on the fixed schedule)
+bool build_mods(pi05_engine* e) {
+  const int S = e->cfg.num_steps, D = P5_EXP_W;
+  std::vector<float> ts(S), emb((size_t)S * D);
+  p5_time_schedule(S, ts.data());
+  for (int s = 0; s < S; ++s) p5_time_embedding(ts[s], D, emb.data() + (size_t)s * D);
+  float *d_emb, *d_c1, *d_c2;
+  bf16* d_cbf;
+  CK(cudaMalloc(&d_emb, (size_t)S * D * 4));
+  CK(cudaMalloc(&d_c1, (size_t)S * D * 4));
+  CK(cudaMalloc(&d_c2, (size_t)S * D * 4));
+  CK(cudaMalloc(&d_cbf, (size_t)S * D * 2));
+  CK(cudaMemcpyAsync(d_emb, emb.data(), (size_t)S * D * 4, cudaMemcpyHostToDevice, e->stream));
+  const int warps = S * D;
+  linear_swish_f32_kernel<<<(warps * 32 + 255) / 256, 256, 0, e->stream>>>(d_emb, e->tin_w, e->tin_b, d_c1,
+                                                                          (bf16*)nullptr, S, D);
+  linear_swish_f32_kernel<<<(warps * 32 + 255) / 256, 256, 0, e->stream>>>(d_c1, e->tout_w, e->tout_b, d_c2, d_cbf,
+                                                                          S, D);
+  CK(cudaGetLastError());
+  Lin m{d_cbf, D, S, e->ada_w, D, e->NM * 3 * D, D};
+  m.out = e->mods;
+  m.ld_out = e->NM * 3 * D;
+  m.bias = e->ada_b;
+  const bool ok = linear(e, m);
+  CK(cudaStreamSynchronize(e->stream));
+  cudaFree(d_emb);
+  cudaFree(d_c1);
+  cudaFree(d_c2);
+  cudaFree(d_cbf);
+  return ok && check_status(e);
+}
+
+struct Fill {
+  bf16* dst;
+  long rows;
+  int cols, ld;
+  long row_off;
+  int row_step;
+  int kind, sub;
+  double stdv;
+};
+
+bool fill(pi05_engine* e, uint64_t seed, const Fill& f) {
+  const uint64_t key = p5_key(seed, (uint32_t)f.kind, (uint32_t)f.sub);
+  const float sc = p5_scale_for_std(f.stdv);
+  const float base = p5_kind_has_unit_base(f.kind) ? 1.0f : 0.0f;
+  const long n = f.rows * f.cols;
+  const unsigned blocks = (unsigned)std::min<long>((n + 255) / 256, 148L * 64);
+  fill_param_kernel<<<blocks, 256, 0, e->stream>>>(f.dst, f.rows, f.cols, f.ld, f.row_off, f.row_step, key, sc, base);
+  CK(cudaGetLastError());
+  return true;
+}
+
+bool init_random(pi05_engine* e, uint64_t seed) {
+  const pi05_config& c = e->cfg;
+  const double S = P5_W_STD;
+  CK(cudaMemsetAsync(e->warena, 0, e->wbytes, e->stream));
+  std::vector<Fill> F;
+  const int D = P5_SIG_W;
+  F.push_back({e->sig_stem_w, D, P5_SIG_K, P5_SIG_KPAD, 0, 1, K_SIG_STEM_W, 0, S});
+  F.push_back({e->sig_stem_b, 1, D, D, 0, 1, K_SIG_STEM_B, 0, S});
+  F.push_back({e->sig_posemb, 256, D, D, 0, 1, K_SIG_POSEMB, 0, S});
+  for (int l = 0; l < c.siglip_layers; ++l) {
+    const SigLayer& s = e->sig[l];
+    F.push_back({s.ln1s, 1, D, D, 0, 1, K_SIG_LN1_S, l, S});
+    F.push_back({s.ln1b, 1, D, D, 0, 1, K_SIG_LN1_B, l, S});
+    F.push_back({s.wqkv, D, D, D, 0, 1, K_SIG_WQ, l, S});
+    F.push_back({s.wqkv, D, D, D, D, 1, K_SIG_WK, l, S});
+    F.push_back({s.wqkv, D, D, D, 2 * D, 1, K_SIG_WV, l, S});
+    F.push_back({s.bqkv, 1, D, D, 0, 1, K_SIG_BQ, l, S});
+    F.push_back({s.bqkv + D, 1, D, D, 0, 1, K_SIG_BK, l, S});
+    F.push_back({s.bqkv + 2 * D, 1, D, D, 0, 1, K_SIG_BV, l, S});
+    F.push_back({s.wo, D, D, D, 0, 1, K_SIG_WO, l, S});
+    F.push_back({s.bo, 1, D, D, 0, 1, K_SIG_BO, l, S});
+    F.push_back({s.ln2s, 1, D, D, 0, 1, K_SIG_LN2_S, l, S});
+    F.push_back({s.ln2b, 1, D, D, 0, 1, K_SIG_LN2_B, l, S});
+    F.push_back({s.w1, P5_SIG_MLP, D, D, 0, 1, K_SIG_W1, l, S});
+    F.push_back({s.b1, 1, P5_SIG_MLP, P5_SIG_MLP, 0, 1, K_SIG_B1, l, S});
+    F.push_back({s.w2, D, P5_SIG_MLP, P5_SIG_MLP, 0, 1, K_SIG_W2, l, S});
+    F.push_back({s.b2, 1, D, D, 0, 1, K_SIG_B2, l, S});
+  }
+  F.push_back({e->sig_post_s, 1, D, D, 0, 1, K_SIG_POST_S, 0, S});
+  F.push_back({e->sig_post_b, 1, D, D, 0, 1, K_SIG_POST_B, 0, S});
+  F.push_back({e->sig_head_w, P5_GEM_W, D, D, 0, 1, K_SIG_HEAD_W, 0, S});
+  F.push_back({e->sig_head_b, 1, P5_GEM_W, P5_GEM_W, 0, 1, K_SIG_HEAD_B, 0, S});
+  F.push_back({e->embed, P5_VOCAB, P5_GEM_W, P5_GEM_W, 0, 1, K_GEM_EMBED, 0, S});
+  const int G = P5_GEM_W;
+  for (int l = 0; l < c.gemma_layers; ++l) {
+    const GemLayer& g = e->gem[l];
+    F.push_back({g.rms1, 1, G, G, 0, 1, K_GEM_RMS1, l, S});
+    F.push_back({g.wqkv, P5_QDIM, G, G, 0, 1, K_GEM_WQ, l, S});
+    F.push_back({g.wqkv, P5_HD, G, G, P5_QDIM, 1, K_GEM_WK, l, S});
+    F.push_back({g.wqkv, P5_HD, G, G, P5_QDIM + P5_HD, 1, K_GEM_WV, l, S});
+    F.push_back({g.wo, G, P5_QDIM, P5_QDIM, 0, 1, K_GEM_WO, l, S});
+    F.push_back({g.rms2, 1, G, G, 0, 1, K_GEM_RMS2, l, S});
+    F.push_back({g.wgu, P5_GEM_MLP, G, G, 0, 2, K_GEM_WG, l, S});  // gate rows even
+    F.push_back({g.wgu, P5_GEM_MLP, G, G, 1, 2, K_GEM_WU, l, S});  // up rows odd
+    F.push_back({g.wd, G, P5_GEM_MLP, P5_GEM_MLP, 0, 1, K_GEM_WD, l, S});
+  }
+  const int X = P5_EXP_W;
+  for (int l = 0; l < c.expert_layers; ++l) {
+    const ExpLayer& x = e->ex[l];
+    F.push_back({x.wqkv, P5_QDIM, X, X, 0, 1, K_EXP_WQ, l, S});
+    F.push_back({x.wqkv, P5_HD, X, X, P5_QDIM, 1, K_EXP_WK, l, S});
+    F.push_back({x.wqkv, P5_HD, X, X, P5_QDIM + P5_HD, 1, K_EXP_WV, l, S});
+    F.push_back({x.wo, X, P5_QDIM, P5_QDIM, 0, 1, K_EXP_WO, l, S});
+    F.push_back({x.wgu, P5_EXP_MLP, X, X, 0, 2, K_EXP_WG, l, S});
+    F.push_back({x.wgu, P5_EXP_MLP, X, X, 1, 2, K_EXP_WU, l, S});
+    F.push_back({x.wd, X, P5_EXP_MLP, P5_EXP_MLP, 0, 1, K_EXP_WD, l, S});
+  }
+  for (int m = 0; m < e->NM; ++m) {
+    const bool fin = m == e->NM - 1;
+    const int kw = fin ? K_EXP_FINAL_W : ((m & 1) ? K_EXP_ADA2_W : K_EXP_ADA1_W);
+    const int l = fin ? 0 : m / 2;
+    F.push_back({e->ada_w, 3 * X, X, X, (long)m * 3 * X, 1, kw, l, S});
+    F.push_back({e->ada_b + (size_t)m * 3 * X, 1, 3 * X, 3 * X, 0, 1, kw + 1, l, S});
+  }
+  F.push_back({e->ain_w, X, P5_ACT_D, P5_ACT_D, 0, 1, K_AIN_W, 0, S});
+  F.push_back({e->ain_b, 1, X, X, 0, 1, K_AIN_B, 0, S});
+  F.push_back({e->aout_w, P5_ACT_D, X, X, 0, 1, K_AOUT_W, 0, S});
+  F.push_back({e->aout_b, 1, P5_ACT_D, P5_ACT_D, 0, 1, K_AOUT_B, 0, S});
+  F.push_back({e->tin_w, X, X, X, 0, 1, K_TIN_W, 0, S});
+  F.push_back({e->tin_b, 1, X, X, 0, 1, K_TIN_B, 0, S});
+  F.push_back({e->tout_w, X, X, X, 0, 1, K_TOUT_W, 0, S});
+  F.push_back({e->tout_b, 1, X, X, 0, 1, K_TOUT_B, 0, S});
+  for (const Fill& f : F)
+    if (!fill(e, seed, f)) return false;
+  CK(cudaStreamSynchronize(e->stream));
+  return build_mods(e);
+}
+
+bool create(pi05_engine* e) {
+  const pi05_config& c = e->cfg;
+  CK(cudaSetDevice(e->device));
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, e->device));
+  if (prop.major != 10) return set_err(e, "this engine is built for sm_100a (B200); device is sm_" +
+                                              std::to_string(prop.major) + std::to_string(prop.minor));
+  e->num_sms = prop.multiProcessorCount;
+  CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (!fn || q != cudaDriverEntryPointSuccess) return set_err(e, "cuTensorMapEncodeTiled unavailable");
+  e->encode = reinterpret_cast<EncodeTiledFn>(fn);
+
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<64>::SMEM));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<128>::SMEM));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<256>::SMEM));
+  CK(cudaFuncSetAttribute(attn_kernel<P5_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<P5_HD>::SMEM));
+  CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          AttnCfg<P5_SIG_HD>::SMEM));
+
+  // weights
+  e->warena = nullptr;
+  layout_weights(e);
+  e->wbytes = e->wused;
+  void* p;
+  if (!dalloc(e, &p, e->wbytes)) return false;
+  e->warena = (char*)p;
+  layout_weights(e);
+
+  // activations
+  const int B = e->max_batch, P = e->P, H = c.horizon;
+  const long Ts = (long)B * c.n_cameras * P5_SIG_TOK, Tp = (long)B * P, Te = (long)B * H;
+  Acts& A = e->A;
+  auto al = [&](void** dst, size_t bytes) { return dalloc(e, dst, bytes); };
+  if (!al((void**)&A.images, (size_t)B * c.n_cameras * P5_IMG * P5_IMG * 3) ||
+      !al((void**)&A.tokens, (size_t)B * std::max(1, c.n_text) * 4) ||
+      !al((void**)&A.patches, (size_t)Ts * P5_SIG_KPAD * 2) || !al((void**)&A.sx, (size_t)Ts * P5_SIG_W * 2) ||
+      !al((void**)&A.sy, (size_t)Ts * P5_SIG_W * 2) || !al((void**)&A.sqkv, (size_t)Ts * P5_SIG_QKV * 2) ||
+      !al((void**)&A.so, (size_t)Ts * P5_SIG_W * 2) || !al((void**)&A.sh, (size_t)Ts * P5_SIG_MLP * 2) ||
+      !al((void**)&A.px, (size_t)Tp * P5_GEM_W * 2) || !al((void**)&A.ph, (size_t)Tp * P5_GEM_W * 2) ||
+      !al((void**)&A.pqkv, (size_t)Tp * P5_QKV * 2) || !al((void**)&A.po, (size_t)Tp * P5_QDIM * 2) ||
+      !al((void**)&A.pact, (size_t)Tp * P5_GEM_MLP * 2) ||
+      !al((void**)&A.kcache, (size_t)c.gemma_layers * Tp * P5_HD * 2) ||
+      !al((void**)&A.vcache, (size_t)c.gemma_layers * Tp * P5_HD * 2) ||
+      !al((void**)&A.ex, (size_t)Te * P5_EXP_W * 2) || !al((void**)&A.eh, (size_t)Te * P5_EXP_W * 2) ||
+      !al((void**)&A.eqkv, (size_t)Te * P5_QKV * 2) || !al((void**)&A.eo, (size_t)Te * P5_QDIM * 2) ||
+      !al((void**)&A.eact, (size_t)Te * P5_EXP_MLP * 2) || !al((void**)&A.ek, (size_t)Te * P5_HD * 2) ||
+      !al((void**)&A.ev, (size_t)Te * P5_HD * 2) || !al((void**)&A.xt, (size_t)Te * P5_ACT_D * 4) ||
+      !al((void**)&A.noise, (size_t)Te * P5_ACT_D * 4) || !al((void**)&A.actions, (size_t)Te * P5_ACT_D * 4))
+    return false;
+  // RoPE table, modulation table, GEMM and attention workspaces, status word
+  const int npos = P + H + 8;
+  std::vector<float> cs((size_t)npos * 128), sn((size_t)npos * 128);
+  p5_rope_table(npos, cs.data(), sn.data());
+  if (!al((void**)&e->d_cos, cs.size() * 4) || !al((void**)&e->d_sin, sn.size() * 4)) return false;
+  CK(cudaMemcpyAsync(e->d_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, e->stream));
+  CK(cudaMemcpyAsync(e->d_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, e->stream));
+  if (!al((void**)&e->mods, (size_t)c.num_steps * e->NM * 3 * P5_EXP_W * 2)) return false;
+  e->gemm_ws_bytes = (size_t)64 << 20;
+  e->n_counters = 1 << 16;
+  if (!al((void**)&e->gemm_ws, e->gemm_ws_bytes) || !al((void**)&e->counters, (size_t)e->n_counters * 4)) return false;
+  e->attn_ws_rows = (size_t)4 * 16 * H * P5_NH;
+  if (!al((void**)&e->attn_ws_o, e->attn_ws_rows * P5_HD * 4) || !al((void**)&e->attn_ws_ml, e->attn_ws_rows * 2 * 4))
+    return false;
+  if (!al((void**)&e->d_status, 64)) return false;
+  CK(cudaStreamSynchronize(e->stream));
+  return true;
+}
+
+}  // namespace
+
+// ===================================================================== C ABI
+extern "C" {
+
+void pi05_default_config(pi05_config* c) {
+  if (!c) return;
+  c->siglip_layers = 27;
+  c->gemma_layers = 18;
+  c->expert_layers = 18;
+  c->num_steps = 10;
+  c->n_cameras = 3;
+  c->n_text = 200;
+  c->horizon = 50;
+}
+
+pi05_engine* pi05_create(const pi05_config* c, int device, int max_batch, char* err, size_t err_len) {
+  auto fail = [&](const std::string& m) -> pi05_engine* {
+    if (err && err_len) snprintf(err, err_len, "%s", m.c_str());
+    return nullptr;
+  };
+  pi05_config cfg;
+  pi05_default_config(&cfg);
+  if (c) cfg = *c;
+  if (cfg.siglip_layers < 0 || cfg.gemma_layers < 1 || cfg.expert_layers != cfg.gemma_layers || cfg.num_steps < 1 ||
+      cfg.n_cameras < 1 || cfg.n_text < 0 || cfg.horizon < 1 || cfg.horizon > 128 || max_batch < 1)
+    return fail("pi05_create: invalid configuration");
+  pi05_engine* e = new pi05_engine();
+  e->cfg = cfg;
+  e->device = device;
+  e->max_batch = max_batch;
+  e->P = cfg.n_cameras * P5_SIG_TOK + cfg.n_text;
+  e->NM = 2 * cfg.expert_layers + 1;
+  if (!create(e)) {
+    std::string m = e->err;
+    pi05_destroy(e);
+    return fail("pi05_create: " + m);
+  }
+  return e;
+}
+
+void pi05_destroy(pi05_engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (auto& kv : e->denoise_graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : e->prefill_graphs) cudaGraphExecDestroy(kv.second);
+  for (void* p : e->allocs) cudaFree(p);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+const char* pi05_last_error(const pi05_engine* e) { return e ? e->err.c_str() : "null engine"; }
+
+int pi05_prefix_len(const pi05_engine* e) { return e ? e->P : 0; }
+
+void* pi05_stream(pi05_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+int pi05_sync(pi05_engine* e) {
+  if (!e) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  cudaError_t ce = cudaStreamSynchronize(e->stream);
+  if (ce != cudaSuccess) {
+    e->err = std::string("cudaStreamSynchronize: ") + cudaGetErrorString(ce);
+    return PI05_ERR_CUDA;
+  }
+  if (!check_status(e)) return fail_code(e);
+  return PI05_OK;
+}
+
+int pi05_init_random_weights(pi05_engine* e, uint64_t seed) {
+  if (!e) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  if (!init_random(e, seed)) return fail_code(e);
+  e->weights_ready = true;
+  e->prefix_n = 0;
+  return PI05_OK;
+}
+
+int pi05_save_weights(pi05_engine* e, const char* path) {
+  if (!e || !path) return PI05_ERR_ARG;
+  if (!e->weights_ready) {
+    e->err = "no weights";
+    return PI05_ERR_STATE;
+  }
+  cudaSetDevice(e->device);
+  FILE* f = fopen(path, "wb");
+  if (!f) {
+    e->err = std::string("cannot open ") + path;
+    return PI05_ERR_ARG;
+  }
+  std::string man = "pi05w 1\n";
+  const pi05_config& c = e->cfg;
+  man += "cfg siglip_layers " + std::to_string(c.siglip_layers) + "\ncfg gemma_layers " +
+         std::to_string(c.gemma_layers) + "\ncfg expert_layers " + std::to_string(c.expert_layers) +
+         "\ncfg num_steps " + std::to_string(c.num_steps) + "\ncfg n_cameras " + std::to_string(c.n_cameras) +
+         "\ncfg n_text " + std::to_string(c.n_text) + "\ncfg horizon " + std::to_string(c.horizon) + "\n";
+  size_t off = 0;
+  for (const Tensor& t : e->tensors) {
+    const size_t bytes = (size_t)t.rows * t.cols * 2;
+    man += "t " + t.name + " bf16 " + std::to_string(off) + " " + std::to_string(bytes) + " " +
+           std::to_string(t.rows) + " " + std::to_string(t.cols) + "\n";
+    off += (bytes + 255) & ~(size_t)255;
+  }
+  man += "end\n";
+  const size_t hdr = (man.size() + 255) & ~(size_t)255;
+  man.resize(hdr, '\n');
+  fwrite(man.data(), 1, hdr, f);
+  std::vector<char> buf;
+  for (const Tensor& t : e->tensors) {
+    const size_t bytes = (size_t)t.rows * t.cols * 2, padded = (bytes + 255) & ~(size_t)255;
+    buf.assign(padded, 0);
+    if (cudaMemcpy(buf.data(), t.ptr, bytes, cudaMemcpyDeviceToHost) != cudaSuccess) {
+      fclose(f);
+      e->err = "device read failed";
+      return PI05_ERR_CUDA;
+    }
+    fwrite(buf.data(), 1, padded, f);
+  }
+  fclose(f);
+  return PI05_OK;
+}
+
+int pi05_load_weights(pi05_engine* e, const char* path) {
+  if (!e || !path) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  FILE* f = fopen(path, "rb");
+  if (!f) {
+    e->err = std::string("cannot open ") + path;
+    return PI05_ERR_ARG;
+  }
+  std::vector<std::string> lines;
+  std::string cur;
+  size_t consumed = 0;
+  int ch;
+  while ((ch = fgetc(f)) != EOF) {
+    ++consumed;
+    if (ch == '\n') {
+      if (cur == "end") break;
+      lines.push_back(cur);
+      cur.clear();
+    } else {
+      cur.push_back((char)ch);
+    }
+  }
+  const size_t hdr = (consumed + 255) & ~(size_t)255;
+  if (lines.empty() || lines[0] != "pi05w 1") {
+    fclose(f);
+    e->err = "not a pi05w file";
+    return PI05_ERR_ARG;
+  }
+  std::map<std::string, std::pair<size_t, size_t>> ent;
+  for (const std::string& L : lines) {
+    char name[256];
+    size_t off, bytes;
+    if (sscanf(L.c_str(), "t %255s bf16 %zu %zu", name, &off, &bytes) == 3) ent[name] = {off, bytes};
+  }
+  std::vector<char> buf;
+  for (const Tensor& t : e->tensors) {
+    auto it = ent.find(t.name);
+    const size_t bytes = (size_t)t.rows * t.cols * 2;
+    if (it == ent.end() || it->second.second != bytes) {
+      fclose(f);
+      e->err = "weight file lacks tensor " + t.name + " of the configured shape";
+      return PI05_ERR_ARG;
+    }
+    buf.resize(bytes);
+    if (fseek(f, (long)(hdr + it->second.first), SEEK_SET) != 0 || fread(buf.data(), 1, bytes, f) != bytes) {
+      fclose(f);
+      e->err = "short read for " + t.name;
+      return PI05_ERR_ARG;
+    }
+    if (cudaMemcpy(t.ptr, buf.data(), bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+      fclose(f);
+      e->err = "device write failed";
+      return PI05_ERR_CUDA;
+    }
+  }
+  fclose(f);
+  if (!build_mods(e)) return fail_code(e);
+  e->weights_ready = true;
+  e->prefix_n = 0;
+  return PI05_OK;
+}
+
+int pi05_prefill(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens) {
+  if (!e || n < 1 || n > e->max_batch || !images || (e->cfg.n_text > 0 && !tokens)) {
+    if (e) e->err = "pi05_prefill: bad arguments";
+    return PI05_ERR_ARG;
+  }
+  if (!e->weights_ready) {
+    e->err = "pi05_prefill: weights not loaded";
+    return PI05_ERR_STATE;
+  }
+  cudaSetDevice(e->device);
+  const size_t ib = (size_t)n * e->cfg.n_cameras * P5_IMG * P5_IMG * 3;
+  if (!copy_in(e, e->A.images, images, ib)) return PI05_ERR_CUDA;
+  if (e->cfg.n_text > 0 && !copy_in(e, e->A.tokens, tokens, (size_t)n * e->cfg.n_text * 4)) return PI05_ERR_CUDA;
+  if (!run_graph(e, e->prefill_graphs, e->prefill_launches, n, run_prefill_body)) return fail_code(e);
+  e->prefix_n = n;
+  return PI05_OK;
+}
+
+int pi05_set_prefix_cache(pi05_engine* e, int n, const uint16_t* k, const uint16_t* v) {
+  if (!e || n < 1 || n > e->max_batch || !k || !v) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  const size_t per = (size_t)e->P * P5_HD;  // one layer of one sample
+  const size_t layer = (size_t)e->max_batch * per;
+  for (int l = 0; l < e->cfg.gemma_layers; ++l)
+    for (int b = 0; b < n; ++b) {
+      const size_t src = ((size_t)b * e->cfg.gemma_layers + l) * per;
+      if (!copy_in(e, e->A.kcache + l * layer + b * per, k + src, per * 2) ||
+          !copy_in(e, e->A.vcache + l * layer + b * per, v + src, per * 2))
+        return PI05_ERR_CUDA;
+    }
+  if (!is_device_ptr(k) && cudaStreamSynchronize(e->stream) != cudaSuccess) return PI05_ERR_CUDA;
+  e->prefix_n = n;
+  return PI05_OK;
+}
+
+int pi05_synth_prefix_cache(pi05_engine* e, int n, uint64_t seed) {
+  if (!e || n < 1 || n > e->max_batch) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  const size_t per = (size_t)e->P * P5_HD;
+  const size_t layer = (size_t)e->max_batch * per;
+  const float sc = p5_scale_for_std(1.0);
+  for (int b = 0; b < n; ++b) {
+    // stream per sample, logical index (l * P + p) * 256 + d, as the host generator lays it out
+    const uint64_t kk = p5_key(seed, K_IN_KCACHE, (uint32_t)b), kv = p5_key(seed, K_IN_VCACHE, (uint32_t)b);
+    for (int l = 0; l < e->cfg.gemma_layers; ++l) {
+      // generate the [P][256] block of layer l: logical offset l*per
+      fill_normal_bf16_kernel<<<148, 256, 0, e->stream>>>(e->A.kcache + l * layer + b * per, (long)per, kk, sc,
+                                                          (long)(l * per));
+      fill_normal_bf16_kernel<<<148, 256, 0, e->stream>>>(e->A.vcache + l * layer + b * per, (long)per, kv, sc,
+                                                          (long)(l * per));
+    }
+  }
+  e->prefix_n = n;
+  return cudaGetLastError() == cudaSuccess ? PI05_OK : PI05_ERR_CUDA;
+}
+
+int pi05_get_prefix_cache(pi05_engine* e, int sample, int layer, uint16_t* k, uint16_t* v) {
+  if (!e || sample < 0 || sample >= e->max_batch || layer < 0 || layer >= e->cfg.gemma_layers) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  const size_t per = (size_t)e->P * P5_HD;
+  const size_t off = (size_t)layer * e->max_batch * per + (size_t)sample * per;
+  if (cudaMemcpyAsync(k, e->A.kcache + off, per * 2, cudaMemcpyDefault, e->stream) != cudaSuccess ||
+      cudaMemcpyAsync(v, e->A.vcache + off, per * 2, cudaMemcpyDefault, e->stream) != cudaSuccess)
+    return PI05_ERR_CUDA;
+  return pi05_sync(e);
+}
+
+int pi05_denoise(pi05_engine* e, int n, const float* noise, float* actions) {
+  if (!e || n < 1 || n > e->max_batch || !noise || !actions) return PI05_ERR_ARG;
+  if (!e->weights_ready || e->prefix_n < n) {
+    e->err = "pi05_denoise: no prefix cache for this batch (call pi05_prefill first)";
+    return PI05_ERR_STATE;
+  }
+  cudaSetDevice(e->device);
+  const size_t bytes = (size_t)n * e->cfg.horizon * P5_ACT_D * 4;
+  if (!copy_in(e, e->A.xt, noise, bytes)) return PI05_ERR_CUDA;
+  if (!run_graph(e, e->denoise_graphs, e->denoise_launches, n, run_denoise_body)) return fail_code(e);
+  if (cudaMemcpyAsync(actions, e->A.xt, bytes, cudaMemcpyDefault, e->stream) != cudaSuccess) return PI05_ERR_CUDA;
+  if (!is_device_ptr(actions)) return pi05_sync(e);
+  return PI05_OK;
+}
+
+int pi05_infer(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* noise,
+               float* actions) {
+  int rc = pi05_prefill(e, n, images, tokens);
+  if (rc != PI05_OK) return rc;
+  return pi05_denoise(e, n, noise, actions);
+}
+
+// kernels per call, as captured (for launch accounting in benchmarks)
+long pi05_graph_launches(pi05_engine* e, int which, int n) {
+  if (!e) return -1;
+  auto& m = which == 0 ? e->prefill_launches : e->denoise_launches;
+  auto it = m.find(n);
+  return it == m.end() ? -1 : it->second;
+}
+
+void pi05_synth_images(uint64_t seed, int sample, int n_cameras, uint8_t* out) {
+  const uint64_t key = p5_key(seed, K_IN_IMAGE, (uint32_t)sample);
+  const long n = (long)n_cameras * P5_IMG * P5_IMG * 3;
+  for (long i = 0; i < n; ++i) out[i] = p5_u8(key, (uint64_t)i);
+}
+void pi05_synth_tokens(uint64_t seed, int sample, int n_text, int32_t* out) {
+  const uint64_t key = p5_key(seed, K_IN_TOKENS, (uint32_t)sample);
+  for (int i = 0; i < n_text; ++i) out[i] = p5_token(key, (uint64_t)i);
+}
+void pi05_synth_noise(uint64_t seed, int sample, int horizon, float* out) {
+  const uint64_t key = p5_key(seed, K_IN_NOISE, (uint32_t)sample);
+  const float sc = p5_scale_for_std(1.0);
+  for (long i = 0; i < (long)horizon * P5_ACT_D; ++i) out[i] = p5_normal(key, (uint64_t)i, sc);
+}
+
+int pi05_op_linear(pi05_engine* e, int T, int F, int K, const void* x, const void* w, const void* bias,
+                   const void* res, const void* gate, int epi, void* out) {
+  if (!e || T < 1 || F < 1 || K < 8 || K % 8 || epi < EPI_STORE || epi > EPI_F32 || !x || !w || !out ||
+      ((epi == EPI_RESID || epi == EPI_GATED) && !res) || (epi == EPI_GATED && !gate) || (epi == EPI_GEGLU && F % 2))
+    return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  Lin L{(const bf16*)x, K, T, (const bf16*)w, K, F, K};
+  L.epi = epi;
+  const int fo = epi == EPI_GEGLU ? F / 2 : F;
+  if (epi == EPI_F32) {
+    L.out_f32 = (float*)out;
+    L.ld_out_f32 = F;
+  } else {
+    L.out = (bf16*)out;
+    L.ld_out = fo;
+  }
+  L.bias = (const bf16*)bias;
+  L.res = (const bf16*)res;
+  L.ld_res = F;
+  L.gate = (const bf16*)gate;
+  L.ld_gate = 0;
+  L.gate_div = 1;
+  if (!linear(e, L)) return fail_code(e);
+  return PI05_OK;
+}
+
+int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, int ldq, const void* k, const void* v,
+                      void* out, int splits) {
+  if (!e || batch < 1 || T < 1 || S < 1 || ldq < P5_QDIM || ldq % 8 || !q || !k || !v || !out || splits < 1)
+    return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  AttnArgs at = {};
+  at.q = (const bf16*)q;
+  at.ldq = ldq;
+  at.q_bstride = (long)T * ldq;
+  at.out = (bf16*)out;
+  at.ldo = P5_QDIM;
+  at.o_bstride = (long)T * P5_QDIM;
+  at.k1 = (const bf16*)k;
+  at.v1 = (const bf16*)v;
+  at.ld1 = P5_HD;
+  at.len1 = S;
+  at.b1stride = (long)S * P5_HD;
+  at.k2 = at.k1;
+  at.v2 = at.v1;
+  at.T = T;
+  at.G = P5_NH;
+  at.qdiv = 1.0f;
+  at.splits = splits;
+  if (!attention(e, at, batch, P5_HD)) return fail_code(e);
+  return PI05_OK;
+}
+
+pi05_engine* pi05_create_batch(const char* weights_path, int device, int max_batch) {
+  char err[512];
+  pi05_engine* e = pi05_create(nullptr, device, max_batch, err, sizeof(err));
+  if (!e) return nullptr;
+  const int rc = weights_path ? pi05_load_weights(e, weights_path) : pi05_init_random_weights(e, 0);
+  if (rc != PI05_OK) {
+    pi05_destroy(e);
+    return nullptr;
+  }
+  return e;
+}
+
+int pi05_infer_batch(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* noise,
+                     float* actions) {
+  return pi05_infer(e, n, images, tokens, noise, actions);
+}
+
+int pi05_set_stage(pi05_engine* e, int slot, int stage, int mode) {
+  if (!e || slot < 0 || slot >= e->max_batch || stage < 0 || mode < 0 || mode > 1) return PI05_ERR_ARG;
+  return PI05_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,235 @@
+// kernels.cuh — the small kernels around the GEMMs and attention: weight fill from the seeded
+// generator, image patchify, norms, RoPE + KV-cache write, text embedding gather, the fp32 action
+// projections, the time MLP and the Euler update.  All are memory-bound; each reads its inputs once.
+#pragma once
+#include "common.cuh"
+
+namespace p5 {
+
+// ---------------------------------------------------------------- parameters
+// dst[(row_off + r*row_step) * ld + c] = bf16(base + N(0,1)*scale) for logical element r*C + c
+__global__ void fill_param_kernel(bf16* dst, long R, int Cc, int ld, long row_off, int row_step, uint64_t key,
+                                  float scale, float base) {
+  const long n = R * Cc;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / Cc;
+    const int c = (int)(i % Cc);
+    const uint16_t h = p5_param_bf(key, (uint64_t)i, scale, base);
+    dst[(row_off + r * row_step) * ld + c] = __ushort_as_bfloat16(h);
+  }
+}
+
+// normal draws rounded to bf16 (synthetic KV cache) or kept in fp32 (noise)
+__global__ void fill_normal_bf16_kernel(bf16* dst, long n, uint64_t key, float scale, long idx_off) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    dst[i] = __ushort_as_bfloat16(p5_f2bf(p5_normal(key, (uint64_t)(idx_off + i), scale)));
+}
+
+// ---------------------------------------------------------------- SigLIP patchify
+// images [n_img][224][224][3] u8 -> A [n_img*256][640] bf16 holding (2p - 255), zero for k >= 588.
+// (2p-255) is an odd integer in [-255, 255], exact in bf16; the stem GEMM scales by 1/255 so the
+// product equals the fp32 convolution of x = p/127.5 - 1.
+__global__ void patchify_kernel(const uint8_t* img, bf16* A, int n_img) {
+  const long total = (long)n_img * 256 * P5_SIG_KPAD;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int k = (int)(i % P5_SIG_KPAD);
+    const long tok = i / P5_SIG_KPAD;
+    float v = 0.f;
+    if (k < P5_SIG_K) {
+      const int im = (int)(tok / 256), pt = (int)(tok % 256);
+      const int py = pt / 16, px = pt % 16;
+      const int ky = k / 42, rem = k % 42, kx = rem / 3, ch = rem % 3;
+      const uint8_t p = img[(((long)im * P5_IMG + py * 14 + ky) * P5_IMG + px * 14 + kx) * 3 + ch];
+      v = 2.0f * (float)p - 255.0f;
+    }
+    A[i] = tobf(v);
+  }
+}
+
+// ---------------------------------------------------------------- norms (one warp per row)
+// flax LayerNorm, eps 1e-6, two-pass statistics in fp32
+__global__ void layernorm_kernel(const bf16* x, bf16* y, const bf16* s, const bf16* b, int T, int D) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  if (warp >= T) return;
+  const bf16* xr = x + (long)warp * D;
+  float sum = 0.f;
+  for (int i = lane; i < D; i += 32) sum += bf(xr[i]);
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / (float)D;
+  float var = 0.f;
+  for (int i = lane; i < D; i += 32) {
+    const float d = bf(xr[i]) - mean;
+    var += d * d;
+  }
+  for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  const float inv = 1.0f / sqrtf(var / (float)D + 1e-6f);
+  bf16* yr = y + (long)warp * D;
+  for (int i = lane; i < D; i += 32) yr[i] = tobf((bf(xr[i]) - mean) * inv * bf(s[i]) + bf(b[i]));
+  pdl_launch_dependents();
+}
+
+// Gemma RMSNorm: y = R(x / sqrt(mean(x^2) + 1e-6) * R(1 + scale) [+ shift])
+//   plain:    scale = per-feature parameter, shift = null, mod_ld = 0
+//   adaptive: scale/shift rows of the modulation table, row (t / rows_per_mod) with stride mod_ld
+__global__ void rmsnorm_kernel(const bf16* x, bf16* y, const bf16* scale, const bf16* shift, int T, int D,
+                               int rows_per_mod, int mod_ld) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  if (warp >= T) return;
+  const bf16* xr = x + (long)warp * D;
+  const long mrow = mod_ld ? (long)(warp / rows_per_mod) * mod_ld : 0;
+  const bf16* sc = scale + mrow;
+  const bf16* sh = shift ? shift + mrow : nullptr;
+  float ss = 0.f;
+  for (int i = lane * 8; i < D; i += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(xr + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf2(w[q]);
+      ss += f.x * f.x + f.y * f.y;
+    }
+  }
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = 1.0f / sqrtf(ss / (float)D + 1e-6f);
+  bf16* yr = y + (long)warp * D;
+  for (int i = lane * 8; i < D; i += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(xr + i);
+    const uint4 us = *reinterpret_cast<const uint4*>(sc + i);
+    uint4 uh = make_uint4(0, 0, 0, 0);
+    if (sh) uh = *reinterpret_cast<const uint4*>(sh + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w}, ws[4] = {us.x, us.y, us.z, us.w}, wh[4] = {uh.x, uh.y, uh.z, uh.w};
+    uint32_t out[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf2(w[q]), s2 = unpack_bf2(ws[q]), h2 = unpack_bf2(wh[q]);
+      const float a = f.x * inv * rbf(1.0f + s2.x) + h2.x;
+      const float c = f.y * inv * rbf(1.0f + s2.y) + h2.y;
+      out[q] = pack_bf2(a, c);
+    }
+    *reinterpret_cast<uint4*>(yr + i) = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+  pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------- RoPE + KV write
+// qkv [T][2560] (q: 8 heads x 256, k: 256, v: 256).  Token t has position pos_off + t % per_sample.
+// q <- R(rope(q)) * 1/16 in place; kout[t] <- R(rope(k)); vout[t] <- v.
+// RoPE pairs (i, i+128) of each 256-wide head (openpi gemma._apply_rope).
+__global__ void rope_qkv_kernel(bf16* qkv, int T, int per_sample, int pos_off, bf16* kout, bf16* vout,
+                                const float* cos_t, const float* sin_t) {
+  const int t = blockIdx.x;
+  pdl_wait();
+  if (t >= T) return;
+  const int pos = pos_off + t % per_sample;
+  const float* cs = cos_t + (long)pos * 128;
+  const float* sn = sin_t + (long)pos * 128;
+  bf16* row = qkv + (long)t * P5_QKV;
+  // 9 rotated heads (8 q + 1 k) x 128 pairs + 256 v copies
+  for (int i = threadIdx.x; i < 9 * 128 + 128; i += blockDim.x) {
+    if (i < 9 * 128) {
+      const int h = i / 128, j = i % 128;
+      bf16* v = row + h * 256;
+      const float x1 = bf(v[j]), x2 = bf(v[j + 128]);
+      const float a = rbf(x1 * cs[j] - x2 * sn[j]);
+      const float c = rbf(x2 * cs[j] + x1 * sn[j]);
+      if (h < 8) {
+        v[j] = tobf(a * 0.0625f);
+        v[j + 128] = tobf(c * 0.0625f);
+      } else {
+        kout[(long)t * 256 + j] = tobf(a);
+        kout[(long)t * 256 + j + 128] = tobf(c);
+      }
+    } else {
+      const int j = (i - 9 * 128) * 2;
+      *reinterpret_cast<uint32_t*>(vout + (long)t * 256 + j) =
+          *reinterpret_cast<const uint32_t*>(row + 2304 + j);
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------- text embedding
+// x[b][768 + i] = R(table[tok] * 45.25)  for i < n_text (Gemma embedder scale sqrt(2048) in bf16)
+__global__ void embed_text_kernel(const int32_t* tokens, const bf16* table, bf16* x, int n_text, int P,
+                                  int img_tokens) {
+  const int b = blockIdx.y, i = blockIdx.x;
+  pdl_wait();
+  long tok = tokens[(long)b * n_text + i];
+  if (tok < 0 || tok >= P5_VOCAB) tok = 0;  // out-of-vocabulary ids read row 0 instead of out of bounds
+  const bf16* src = table + tok * P5_GEM_W;
+  bf16* dst = x + ((long)b * P + img_tokens + i) * P5_GEM_W;
+  for (int d = threadIdx.x * 2; d < P5_GEM_W; d += blockDim.x * 2) {
+    const float2 f = unpack_bf2(*reinterpret_cast<const uint32_t*>(src + d));
+    *reinterpret_cast<uint32_t*>(dst + d) = pack_bf2(f.x * P5_EMBED_SCALE, f.y * P5_EMBED_SCALE);
+  }
+  pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------- action projections (fp32 math)
+// action_in_proj: y[t][o] = R(sum_k x[t][k] W[o][k] + b[o]), x fp32 [T][32] (nnx.Linear in fp32)
+__global__ void action_in_kernel(const float* xt, const bf16* W, const bf16* b, bf16* y, int T, int D) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  if (idx >= (long)T * D) return;
+  const int t = (int)(idx / D), o = (int)(idx % D);
+  const float* x = xt + (long)t * P5_ACT_D;
+  const bf16* w = W + (long)o * P5_ACT_D;
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < P5_ACT_D; ++k) acc += x[k] * bf(w[k]);
+  y[idx] = tobf(acc + bf(b[o]));
+  pdl_launch_dependents();
+}
+
+// action_out_proj + Euler step, one warp per (token, action dim):
+//   v = R(h[t] . W[j] + b[j]);  x[t][j] += R(dt_bf16 * v)
+__global__ void action_out_euler_kernel(const bf16* h, const bf16* W, const bf16* b, float* xt, float* v_out, int T,
+                                        int D, float dtb) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  if (w >= T * P5_ACT_D) return;
+  const int t = w / P5_ACT_D, j = w % P5_ACT_D;
+  const bf16* hr = h + (long)t * D;
+  const bf16* wr = W + (long)j * D;
+  float acc = 0.f;
+  for (int k = lane * 8; k < D; k += 256) {
+    const uint4 a = *reinterpret_cast<const uint4*>(hr + k), c = *reinterpret_cast<const uint4*>(wr + k);
+    const uint32_t aa[4] = {a.x, a.y, a.z, a.w}, cc[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf2(aa[q]), g = unpack_bf2(cc[q]);
+      acc += f.x * g.x + f.y * g.y;
+    }
+  }
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) {
+    const float v = rbf(acc + bf(b[j]));
+    if (v_out) v_out[(long)t * P5_ACT_D + j] = v;
+    xt[(long)t * P5_ACT_D + j] += rbf(dtb * v);
+  }
+  pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------- time MLP (fp32, one warp per output)
+// y[s][o] = swish(sum_k x[s][k] W[o][k] + b[o]); optional bf16 copy (input of the bf16 modulation Dense)
+__global__ void linear_swish_f32_kernel(const float* x, const bf16* W, const bf16* b, float* y, bf16* ybf, int S,
+                                        int D) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (w >= S * D) return;
+  const int s = w / D, o = w % D;
+  const float* xr = x + (long)s * D;
+  const bf16* wr = W + (long)o * D;
+  float acc = 0.f;
+  for (int k = lane; k < D; k += 32) acc += xr[k] * bf(wr[k]);
+  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    const float v = acc + bf(b[o]);
+    const float sw = v / (1.0f + expf(-v));
+    y[(long)s * D + o] = sw;
+    if (ybf) ybf[(long)s * D + o] = tobf(sw);
+  }
+}
+
+}  // namespace p5

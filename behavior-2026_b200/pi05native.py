@@ -1,0 +1,290 @@
+"""Python binding of libpi05.so (include/pi05.h).
+
+Mirrors the reference engine's CPython module `_pi05native` and its `Pi05NativePolicy` wrapper
+(glue/pi05native_module.c, glue/pi05_policy.py in the deleted engine; described in
+docs/archive/windows/π05_네이티브엔진.md:109-117): buffers are passed by pointer, numpy arrays as host
+pointers, CUDA tensors (anything with ``__cuda_array_interface__`` or a torch CUDA tensor) as device
+pointers without a copy.  ctypes releases the GIL during each call.
+
+There is no fallback: if libpi05.so is missing or fails to load, importing this module raises.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libpi05.so")
+
+OK, ERR_ARG, ERR_CUDA, ERR_STATE, ERR_DEVICE = 0, -1, -2, -3, -4
+
+EXPORTS = [
+    "pi05_default_config", "pi05_create", "pi05_destroy", "pi05_last_error", "pi05_init_random_weights",
+    "pi05_save_weights", "pi05_load_weights", "pi05_prefill", "pi05_set_prefix_cache", "pi05_get_prefix_cache",
+    "pi05_denoise", "pi05_infer", "pi05_stream", "pi05_sync", "pi05_prefix_len", "pi05_graph_launches",
+    "pi05_synth_images", "pi05_synth_tokens", "pi05_synth_noise", "pi05_synth_prefix_cache", "pi05_create_batch",
+    "pi05_infer_batch", "pi05_set_stage", "pi05_op_linear", "pi05_op_attention",
+]
+
+
+class Pi05Error(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"pi05 error {code}: {msg}")
+        self.code = code
+
+
+class Config(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("siglip_layers", "gemma_layers", "expert_layers", "num_steps", "n_cameras", "n_text", "horizon")]
+
+    @classmethod
+    def make(cls, siglip_layers=27, gemma_layers=18, num_steps=10, n_cameras=3, n_text=200, horizon=50):
+        return cls(siglip_layers, gemma_layers, gemma_layers, num_steps, n_cameras, n_text, horizon)
+
+    @property
+    def prefix_len(self):
+        return 256 * self.n_cameras + self.n_text
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing; build it with behavior-2026_b200/build.py")
+    L = ctypes.CDLL(LIB_PATH)
+    P, vp, i32, u64 = ctypes.POINTER, ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64
+    cfg = P(Config)
+    L.pi05_default_config.argtypes = [cfg]
+    L.pi05_default_config.restype = None
+    L.pi05_create.argtypes = [cfg, i32, i32, ctypes.c_char_p, ctypes.c_size_t]
+    L.pi05_create.restype = vp
+    L.pi05_destroy.argtypes = [vp]
+    L.pi05_destroy.restype = None
+    L.pi05_last_error.argtypes = [vp]
+    L.pi05_last_error.restype = ctypes.c_char_p
+    L.pi05_init_random_weights.argtypes = [vp, u64]
+    L.pi05_save_weights.argtypes = [vp, ctypes.c_char_p]
+    L.pi05_load_weights.argtypes = [vp, ctypes.c_char_p]
+    L.pi05_prefill.argtypes = [vp, i32, vp, vp]
+    L.pi05_set_prefix_cache.argtypes = [vp, i32, vp, vp]
+    L.pi05_get_prefix_cache.argtypes = [vp, i32, i32, vp, vp]
+    L.pi05_denoise.argtypes = [vp, i32, vp, vp]
+    L.pi05_infer.argtypes = [vp, i32, vp, vp, vp, vp]
+    L.pi05_stream.argtypes = [vp]
+    L.pi05_stream.restype = vp
+    L.pi05_sync.argtypes = [vp]
+    L.pi05_prefix_len.argtypes = [vp]
+    L.pi05_graph_launches.argtypes = [vp, i32, i32]
+    L.pi05_graph_launches.restype = ctypes.c_long
+    L.pi05_synth_images.argtypes = [u64, i32, i32, vp]
+    L.pi05_synth_tokens.argtypes = [u64, i32, i32, vp]
+    L.pi05_synth_noise.argtypes = [u64, i32, i32, vp]
+    for f in (L.pi05_synth_images, L.pi05_synth_tokens, L.pi05_synth_noise):
+        f.restype = None
+    L.pi05_synth_prefix_cache.argtypes = [vp, i32, u64]
+    L.pi05_create_batch.argtypes = [ctypes.c_char_p, i32, i32]
+    L.pi05_create_batch.restype = vp
+    L.pi05_infer_batch.argtypes = [vp, i32, vp, vp, vp, vp]
+    L.pi05_set_stage.argtypes = [vp, i32, i32, i32]
+    L.pi05_op_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp]
+    L.pi05_op_attention.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32]
+    return L
+
+
+lib = _load()
+
+
+def _ptr(a, dtype=None, writable=False):
+    """(pointer, keepalive) for a numpy array, a torch tensor or a __cuda_array_interface__ object."""
+    if hasattr(a, "data_ptr") and hasattr(a, "is_contiguous"):  # torch tensor
+        if not a.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return ctypes.c_void_p(a.data_ptr()), a
+    if hasattr(a, "__cuda_array_interface__"):
+        return ctypes.c_void_p(a.__cuda_array_interface__["data"][0]), a
+    arr = np.asarray(a)
+    if dtype is not None and arr.dtype != dtype:
+        if writable:
+            raise ValueError(f"output array must be {dtype}")
+        arr = arr.astype(dtype)
+    if not arr.flags["C_CONTIGUOUS"]:
+        if writable:
+            raise ValueError("output array must be C-contiguous")
+        arr = np.ascontiguousarray(arr)
+    return ctypes.c_void_p(arr.ctypes.data), arr
+
+
+class Engine:
+    """One engine per device (reference: one engine, its own stream, graph captured at load)."""
+
+    def __init__(self, config=None, device=0, max_batch=1):
+        self.config = config if config is not None else Config.make()
+        self.max_batch = max_batch
+        err = ctypes.create_string_buffer(1024)
+        h = lib.pi05_create(ctypes.byref(self.config), device, max_batch, err, len(err))
+        if not h:
+            raise Pi05Error(ERR_CUDA, err.value.decode())
+        self._h = ctypes.c_void_p(h)
+
+    # -- lifecycle
+    def close(self):
+        if getattr(self, "_h", None):
+            lib.pi05_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def _check(self, rc):
+        if rc != OK:
+            raise Pi05Error(rc, lib.pi05_last_error(self._h).decode())
+
+    @property
+    def prefix_len(self):
+        return lib.pi05_prefix_len(self._h)
+
+    @property
+    def stream(self):
+        return lib.pi05_stream(self._h)
+
+    def sync(self):
+        self._check(lib.pi05_sync(self._h))
+
+    def graph_launches(self, which, n):
+        return lib.pi05_graph_launches(self._h, {"prefill": 0, "denoise": 1}.get(which, which), n)
+
+    # -- weights
+    def init_random_weights(self, seed=0):
+        self._check(lib.pi05_init_random_weights(self._h, seed))
+
+    def save_weights(self, path):
+        self._check(lib.pi05_save_weights(self._h, path.encode()))
+
+    def load_weights(self, path):
+        self._check(lib.pi05_load_weights(self._h, path.encode()))
+
+    # -- path
+    def prefill(self, images, tokens):
+        n = images.shape[0]
+        pi, ki = _ptr(images, np.uint8)
+        pt, kt = _ptr(tokens, np.int32)
+        self._check(lib.pi05_prefill(self._h, n, pi, pt))
+
+    def set_prefix_cache(self, k_bits, v_bits):
+        """k_bits/v_bits: uint16 (bf16 bit patterns) [n][layers][P][256]."""
+        n = k_bits.shape[0]
+        pk, kk = _ptr(k_bits, np.uint16)
+        pv, kv = _ptr(v_bits, np.uint16)
+        self._check(lib.pi05_set_prefix_cache(self._h, n, pk, pv))
+
+    def synth_prefix_cache(self, n, seed=0):
+        self._check(lib.pi05_synth_prefix_cache(self._h, n, seed))
+
+    def get_prefix_cache(self, sample, layer):
+        P = self.prefix_len
+        k = np.empty((P, 256), np.uint16)
+        v = np.empty((P, 256), np.uint16)
+        self._check(lib.pi05_get_prefix_cache(self._h, sample, layer, k.ctypes.data, v.ctypes.data))
+        return bf16_bits_to_f32(k), bf16_bits_to_f32(v)
+
+    def denoise(self, noise, out=None):
+        n = noise.shape[0]
+        if out is None:
+            out = np.empty((n, self.config.horizon, 32), np.float32)
+        pn, kn = _ptr(noise, np.float32)
+        po, ko = _ptr(out, np.float32, writable=True)
+        self._check(lib.pi05_denoise(self._h, n, pn, po))
+        return out
+
+    def infer(self, images, tokens, noise, out=None):
+        n = images.shape[0]
+        if out is None:
+            out = np.empty((n, self.config.horizon, 32), np.float32)
+        pi, ki = _ptr(images, np.uint8)
+        pt, kt = _ptr(tokens, np.int32)
+        pn, kn = _ptr(noise, np.float32)
+        po, ko = _ptr(out, np.float32, writable=True)
+        self._check(lib.pi05_infer(self._h, n, pi, pt, pn, po))
+        return out
+
+    # -- hot operators on device tensors (asynchronous on the engine stream)
+    EPI = {"store": 0, "gelu": 1, "resid": 2, "gated": 3, "geglu": 4, "f32": 5}
+
+    def op_linear(self, x, w, out, epi="store", bias=None, res=None, gate=None):
+        T, K = x.shape
+        F = w.shape[0]
+        p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+        self._check(lib.pi05_op_linear(self._h, T, F, K, p(x), p(w), p(bias), p(res), p(gate), self.EPI[epi], p(out)))
+
+    def op_attention(self, q, k, v, out, splits=1):
+        """q [b][T][ldq] (heads at column 0), k/v [b][S][256], out [b][T][2048]; all CUDA bf16 tensors."""
+        b, T, ldq = q.shape
+        S = k.shape[1]
+        p = lambda t: ctypes.c_void_p(t.data_ptr())
+        self._check(lib.pi05_op_attention(self._h, b, T, S, p(q), ldq, p(k), p(v), p(out), splits))
+
+    # -- reference-named extras
+    def info(self):
+        return {"kind": "pi05", "prefix_len": self.prefix_len, "max_batch": self.max_batch, **self.config.as_dict()}
+
+    def set_stage(self, slot, stage, mode=1):
+        self._check(lib.pi05_set_stage(self._h, slot, stage, mode))
+
+
+def bf16_bits_to_f32(bits):
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x):
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def synth_images(seed, sample, n_cameras=3):
+    out = np.empty((n_cameras, 224, 224, 3), np.uint8)
+    lib.pi05_synth_images(seed, sample, n_cameras, out.ctypes.data)
+    return out
+
+
+def synth_tokens(seed, sample, n_text=200):
+    out = np.empty((n_text,), np.int32)
+    lib.pi05_synth_tokens(seed, sample, n_text, out.ctypes.data)
+    return out
+
+
+def synth_noise(seed, sample, horizon=50):
+    out = np.empty((horizon, 32), np.float32)
+    lib.pi05_synth_noise(seed, sample, horizon, out.ctypes.data)
+    return out
+
+
+class Pi05NativePolicy:
+    """Policy object in the place of the reference's glue/pi05_policy.py: forward(obs) -> action chunk.
+
+    obs: {"images": uint8 [n][cams][224][224][3], "tokens": int32 [n][n_text], optional "noise"}.
+    Returns fp32 [n][horizon][32].  Noise defaults to the seeded generator, one stream per call.
+    """
+
+    kind = "pi05"
+
+    def __init__(self, engine, seed=0):
+        self.engine = engine
+        self.seed = seed
+        self.calls = 0
+
+    def forward(self, obs):
+        imgs = obs["images"]
+        n = imgs.shape[0]
+        noise = obs.get("noise")
+        if noise is None:
+            noise = np.stack([synth_noise(self.seed, self.calls * 4096 + i, self.engine.config.horizon)
+                              for i in range(n)])
+        self.calls += 1
+        return self.engine.infer(imgs, obs["tokens"], noise)
+
+    def reset(self):
+        self.calls = 0
+
+    def set_stage(self, slot, stage, fixed=True):
+        self.engine.set_stage(slot, stage, int(fixed))

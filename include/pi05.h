@@ -1,0 +1,124 @@
+/*
+ * pi05.h — C ABI of the B200-native pi0.5 engine (libpi05.so).
+ *
+ * Replaces the reference engine's batch API `include/pi05_batch.h` (deleted from the reference
+ * repository; described in docs/archive/windows/π05_네이티브엔진.md:288-303 and :159) and its
+ * training entry points `LoraTrainer::accumulate / finalize_grads / opt_step`
+ * (π05_네이티브엔진.md:215).  Error convention follows the reference's other C ABIs
+ * (src/scene_graph/runtime/include/sgrt.h:31-40): opaque handle, `char* err, size_t err_len` on
+ * create, `int` status (0 = success, negative = failure) and a last-error accessor.
+ *
+ * Pointers: every input/output buffer may be a host pointer or a CUDA device pointer of the
+ * engine's device (detected per call).  With host outputs the call returns after the result is in
+ * host memory; with device outputs the work is only stream-ordered on the engine stream
+ * (pi05_stream) and pi05_sync waits for it.  Calls on one engine are not re-entrant.
+ *
+ * Shapes (n = batch of independent observations, n <= max_batch):
+ *   images   uint8 [n][n_cameras][224][224][3]  (RGB, 224x224 already; resize is out of scope)
+ *   tokens   int32 [n][n_text]                  (ids < 257152)
+ *   noise    fp32  [n][horizon][32]             (flow-matching start x_1)
+ *   actions  fp32  [n][horizon][32]             (x_0 after num_steps Euler steps)
+ *   prefix KV cache bf16 (uint16 bits) [n][layers][P][256] each for K and V, P = 256*n_cameras + n_text
+ */
+#ifndef PI05_H
+#define PI05_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define PI05_API __attribute__((visibility("default")))
+#else
+#define PI05_API
+#endif
+
+#define PI05_OK 0
+#define PI05_ERR_ARG (-1)     /* bad argument or shape */
+#define PI05_ERR_CUDA (-2)    /* CUDA runtime error */
+#define PI05_ERR_STATE (-3)   /* call out of order (e.g. denoise before prefill) */
+#define PI05_ERR_DEVICE (-4)  /* a device-side wait gave up (lost arrival); the engine stays usable */
+
+typedef struct pi05_engine pi05_engine;
+
+/* Model hyper-parameters (the reference read these from `cfg` lines of its weight manifest,
+ * π05_네이티브엔진.md:47).  Widths are fixed by the architecture; depths may be reduced for tests. */
+typedef struct {
+  int32_t siglip_layers;   /* 27 */
+  int32_t gemma_layers;    /* 18 */
+  int32_t expert_layers;   /* 18, must equal gemma_layers (expert layer l reads prefix layer l's KV) */
+  int32_t num_steps;       /* 10 Euler steps, t = 1 -> 0 */
+  int32_t n_cameras;       /* 3 */
+  int32_t n_text;          /* 200 prompt tokens */
+  int32_t horizon;         /* 50 actions per chunk */
+} pi05_config;
+
+PI05_API void pi05_default_config(pi05_config* c);
+
+/* Replaces pi05_create_batch(weights, device, max_batch) (π05_네이티브엔진.md:290). */
+PI05_API pi05_engine* pi05_create(const pi05_config* c, int device, int max_batch, char* err, size_t err_len);
+PI05_API void pi05_destroy(pi05_engine* e);
+PI05_API const char* pi05_last_error(const pi05_engine* e);
+
+/* Weights.  pi05_init_random_weights fills every tensor from the seeded generator (linear weights
+ * N(0, 0.02) in bf16; the synthetic workload of the benchmarks).  pi05_load_weights reads a weight
+ * file written by pi05_save_weights (text manifest + 256-byte aligned raw bf16 tensors, the same
+ * scheme as the reference's .pi05w, π05_네이티브엔진.md:46-49). */
+PI05_API int pi05_init_random_weights(pi05_engine* e, uint64_t seed);
+PI05_API int pi05_save_weights(pi05_engine* e, const char* path);
+PI05_API int pi05_load_weights(pi05_engine* e, const char* path);
+
+/* Prefix: SigLIP over the camera images, text embedding, Gemma-2B prefill; fills the per-sample
+ * bf16 KV cache.  (Reference: the per-board prefix CUDA graph, π05_네이티브엔진.md:298.) */
+PI05_API int pi05_prefill(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens);
+/* Install a prefix KV cache directly (the expert-only denoise workload). */
+PI05_API int pi05_set_prefix_cache(pi05_engine* e, int n, const uint16_t* k, const uint16_t* v);
+/* Read one layer of one sample's prefix cache (K and V, [P][256] bf16 bits each). */
+PI05_API int pi05_get_prefix_cache(pi05_engine* e, int sample, int layer, uint16_t* k, uint16_t* v);
+/* Denoise: num_steps Euler steps of the action expert attending to the prefix cache. */
+PI05_API int pi05_denoise(pi05_engine* e, int n, const float* noise, float* actions);
+/* prefill + denoise (replaces pi05_infer_batch, π05_네이티브엔진.md:292). */
+PI05_API int pi05_infer(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* noise,
+               float* actions);
+
+/* Stream and synchronisation. */
+PI05_API void* pi05_stream(pi05_engine* e);  /* cudaStream_t of the engine */
+PI05_API int pi05_sync(pi05_engine* e);      /* waits for queued work; reports device-side errors */
+
+/* Prefix length P for the configuration. */
+PI05_API int pi05_prefix_len(const pi05_engine* e);
+/* Kernels one call enqueues, counted when its CUDA graph was captured (which: 0 prefill, 1 denoise);
+ * -1 before the first call with batch n. */
+PI05_API long pi05_graph_launches(pi05_engine* e, int which, int n);
+
+/* Synthetic workload (host): the generator streams the tests and benchmarks use. */
+PI05_API void pi05_synth_images(uint64_t seed, int sample, int n_cameras, uint8_t* out);
+PI05_API void pi05_synth_tokens(uint64_t seed, int sample, int n_text, int32_t* out);
+PI05_API void pi05_synth_noise(uint64_t seed, int sample, int horizon, float* out);
+/* Expert-only workload: N(0,1) bf16 prefix cache for samples [0, n) generated on the device. */
+PI05_API int pi05_synth_prefix_cache(pi05_engine* e, int n, uint64_t seed);
+
+/* Hot operators on caller-owned device buffers, run on the engine stream (unit tests and the operator
+ * sweep).  pi05_op_linear: out[T][F'] = epilogue(x[T][K] . w[F][K]^T) with bf16 x, w, out and
+ *   epi 0 store, 1 gelu, 2 residual (res[T][F]), 3 gated residual (res, gate[F]), 4 GeGLU
+ *   (w rows interleaved gate/up, F' = F/2), 5 fp32 out.  bias[F] optional (NULL).
+ *   No counterpart in the reference's ABI: its GEMM (src/gemm.cuh, π05_네이티브엔진.md:102-105) was internal.
+ * pi05_op_attention: out[b][t][8*256] = softmax(q k^T) v with q [b][T][ldq] (8 heads x 256 at column 0,
+ *   already scaled), keys/values [b][S][256] bf16.  Asynchronous; call pi05_sync. */
+PI05_API int pi05_op_linear(pi05_engine* e, int T, int F, int K, const void* x, const void* w, const void* bias,
+                            const void* res, const void* gate, int epi, void* out);
+PI05_API int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, int ldq, const void* k,
+                               const void* v, void* out, int splits);
+
+/* Reference batch-API names (π05_네이티브엔진.md:288-303). */
+PI05_API pi05_engine* pi05_create_batch(const char* weights_path, int device, int max_batch);
+PI05_API int pi05_infer_batch(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* noise,
+                     float* actions);
+/* PiBehavior stage channel; plain pi0.5 has no stage head, so this only validates its arguments. */
+PI05_API int pi05_set_stage(pi05_engine* e, int slot, int stage, int mode);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PI05_H */

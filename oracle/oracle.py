@@ -1,0 +1,178 @@
+"""ctypes binding of the CPU oracle (oracle/libpi05_oracle.so).  TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg import this module; the engine
+never does.  The oracle is an fp32 restatement of the pi0.5 network (see pi05_oracle.cpp for the
+reference citations).  Parity against the reference engine itself is unpinned: its source and its
+golden dumps were deleted from the reference repository.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libpi05_oracle.so")
+
+# generator stream ids (behavior-2026_b200/csrc/pi05_model.h)
+K_IN_IMAGE, K_IN_TOKENS, K_IN_NOISE, K_IN_KCACHE, K_IN_VCACHE, K_IN_ACTIONS, K_IN_TRAIN_NOISE = range(120, 127)
+FP32_ACTIVATIONS = 1
+HD = 256
+GEM_W = 2048
+
+
+class Config(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("siglip_layers", "gemma_layers", "expert_layers", "num_steps", "n_cameras", "n_text", "horizon")]
+
+    @classmethod
+    def make(cls, siglip_layers=27, gemma_layers=18, num_steps=10, n_cameras=3, n_text=200, horizon=50):
+        return cls(siglip_layers, gemma_layers, gemma_layers, num_steps, n_cameras, n_text, horizon)
+
+    @property
+    def prefix_len(self):
+        return 256 * self.n_cameras + self.n_text
+
+
+PROBE = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float), ctypes.c_int64, ctypes.c_void_p)
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.POINTER
+        cfg = P(Config)
+        u8, i32, f32 = P(ctypes.c_uint8), P(ctypes.c_int32), P(ctypes.c_float)
+        L.p5o_siglip.argtypes = [cfg, ctypes.c_uint64, u8, f32, ctypes.c_int, PROBE, ctypes.c_void_p]
+        L.p5o_prefill.argtypes = [cfg, ctypes.c_uint64, u8, i32, f32, f32, ctypes.c_int, PROBE, ctypes.c_void_p]
+        L.p5o_prefill_embedded.argtypes = [cfg, ctypes.c_uint64, f32, ctypes.c_int, f32, f32, ctypes.c_int, PROBE,
+                                           ctypes.c_void_p]
+        L.p5o_denoise.argtypes = [cfg, ctypes.c_uint64, f32, f32, ctypes.c_int, f32, f32, ctypes.c_int, PROBE,
+                                  ctypes.c_void_p]
+        L.p5o_gen_images.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, u8]
+        L.p5o_gen_tokens.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, i32]
+        L.p5o_gen_normal.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_double,
+                                     ctypes.c_int, f32]
+        L.p5o_gen_param.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_double, f32]
+        for f in (L.p5o_gen_images, L.p5o_gen_tokens, L.p5o_gen_normal, L.p5o_gen_param):
+            f.restype = None
+        _lib = L
+    return _lib
+
+
+def _p(a, t):
+    return a.ctypes.data_as(ctypes.POINTER(t))
+
+
+class Probe:
+    """Collects named intermediate points (img.tokens, pre.l0.k, suf.s0.v, ...)."""
+
+    def __init__(self, keep=None):
+        self.keep = keep
+        self.points = {}
+        self._cb = PROBE(self._on)
+
+    def _on(self, name, data, n, _ctx):
+        name = name.decode()
+        if self.keep is None or any(name.startswith(k) for k in self.keep):
+            self.points[name] = np.ctypeslib.as_array(data, shape=(n,)).copy()
+
+
+def _probe_args(probe):
+    return (probe._cb if probe is not None else PROBE(), None)
+
+
+# ---------------------------------------------------------------- synthetic workload
+def gen_images(seed, sample, n_cam=3):
+    out = np.empty((n_cam, 224, 224, 3), np.uint8)
+    lib().p5o_gen_images(seed, sample, n_cam, _p(out, ctypes.c_uint8))
+    return out
+
+
+def gen_tokens(seed, sample, n=200):
+    out = np.empty((n,), np.int32)
+    lib().p5o_gen_tokens(seed, sample, n, _p(out, ctypes.c_int32))
+    return out
+
+
+def gen_normal(seed, kind, sub, shape, std=1.0, round_bf16=False):
+    out = np.empty(shape, np.float32)
+    lib().p5o_gen_normal(seed, kind, sub, out.size, std, int(round_bf16), _p(out, ctypes.c_float))
+    return out
+
+
+def gen_param(seed, kind, sub, shape, std=0.02):
+    out = np.empty(shape, np.float32)
+    lib().p5o_gen_param(seed, kind, sub, out.size, std, _p(out, ctypes.c_float))
+    return out
+
+
+def gen_kv_cache(seed, sample, layers, P):
+    """config-1 prefix cache: N(0,1) rounded to bf16, [layers][P][256] each for K and V."""
+    k = gen_normal(seed, K_IN_KCACHE, sample, (layers, P, HD), 1.0, True)
+    v = gen_normal(seed, K_IN_VCACHE, sample, (layers, P, HD), 1.0, True)
+    return k, v
+
+
+def gen_noise(seed, sample, horizon=50):
+    return gen_normal(seed, K_IN_NOISE, sample, (horizon, 32), 1.0, False)
+
+
+# ---------------------------------------------------------------- network
+def siglip(cfg, seed, images, flags=0, probe=None):
+    out = np.empty((256 * cfg.n_cameras, GEM_W), np.float32)
+    images = np.ascontiguousarray(images, np.uint8)
+    rc = lib().p5o_siglip(ctypes.byref(cfg), seed, _p(images, ctypes.c_uint8), _p(out, ctypes.c_float), flags,
+                          *_probe_args(probe))
+    assert rc == 0
+    return out
+
+
+def prefill(cfg, seed, images, tokens, flags=0, probe=None):
+    P = cfg.prefix_len
+    k = np.empty((cfg.gemma_layers, P, HD), np.float32)
+    v = np.empty_like(k)
+    images = np.ascontiguousarray(images, np.uint8)
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    rc = lib().p5o_prefill(ctypes.byref(cfg), seed, _p(images, ctypes.c_uint8), _p(tokens, ctypes.c_int32),
+                           _p(k, ctypes.c_float), _p(v, ctypes.c_float), flags, *_probe_args(probe))
+    assert rc == 0
+    return k, v
+
+
+def prefill_embedded(cfg, seed, emb, flags=0, probe=None):
+    emb = np.ascontiguousarray(emb, np.float32)
+    P = emb.shape[0]
+    k = np.empty((cfg.gemma_layers, P, HD), np.float32)
+    v = np.empty_like(k)
+    rc = lib().p5o_prefill_embedded(ctypes.byref(cfg), seed, _p(emb, ctypes.c_float), P, _p(k, ctypes.c_float),
+                                    _p(v, ctypes.c_float), flags, *_probe_args(probe))
+    assert rc == 0
+    return k, v
+
+
+def denoise(cfg, seed, kcache, vcache, noise, flags=0, probe=None):
+    kcache = np.ascontiguousarray(kcache, np.float32)
+    vcache = np.ascontiguousarray(vcache, np.float32)
+    noise = np.ascontiguousarray(noise, np.float32)
+    P = kcache.shape[1]
+    out = np.empty_like(noise)
+    rc = lib().p5o_denoise(ctypes.byref(cfg), seed, _p(kcache, ctypes.c_float), _p(vcache, ctypes.c_float), P,
+                           _p(noise, ctypes.c_float), _p(out, ctypes.c_float), flags, *_probe_args(probe))
+    assert rc == 0
+    return out
+
+
+def infer(cfg, seed, images, tokens, noise, flags=0, probe=None):
+    k, v = prefill(cfg, seed, images, tokens, flags, probe)
+    return denoise(cfg, seed, k, v, noise, flags, probe)

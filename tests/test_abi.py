@@ -1,0 +1,61 @@
+"""CPU checks of the C ABI library: it loads, exports every symbol include/pi05.h declares, and its
+host-side generators match the oracle's (no GPU compute is called here)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "pi05.h")).read()
+    return sorted(set(re.findall(r"PI05_API[^;(]*?\b(pi05_\w+)\s*\(", src)))
+
+
+def test_header_declares_the_path(pn):
+    syms = declared_symbols()
+    for need in ("pi05_create", "pi05_load_weights", "pi05_prefill", "pi05_denoise", "pi05_infer",
+                 "pi05_create_batch", "pi05_infer_batch", "pi05_set_stage"):
+        assert need in syms
+
+
+def test_library_exports_every_declared_symbol(pn):
+    lib = ctypes.CDLL(pn.LIB_PATH)
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+    assert set(pn.EXPORTS) <= set(declared_symbols())
+
+
+def test_default_config(pn):
+    c = pn.Config()
+    pn.lib.pi05_default_config(ctypes.byref(c))
+    assert c.as_dict() == dict(siglip_layers=27, gemma_layers=18, expert_layers=18, num_steps=10, n_cameras=3,
+                               n_text=200, horizon=50)
+    assert c.prefix_len == 968
+
+
+def test_create_rejects_bad_config_without_gpu(pn):
+    bad = pn.Config.make(gemma_layers=2)
+    bad.expert_layers = 3  # expert layer l reads prefix layer l's cache: depths must match
+    err = ctypes.create_string_buffer(256)
+    assert not pn.lib.pi05_create(ctypes.byref(bad), 0, 1, err, 256)
+    assert b"invalid configuration" in err.value
+
+
+def test_synthetic_inputs_match_oracle_generator(pn, oracle):
+    for s in (0, 3):
+        assert np.array_equal(pn.synth_images(7, s), oracle.gen_images(7, s))
+        assert np.array_equal(pn.synth_tokens(7, s), oracle.gen_tokens(7, s))
+        assert np.array_equal(pn.synth_noise(7, s), oracle.gen_noise(7, s))
+    tok = pn.synth_tokens(0, 0)
+    assert tok.min() >= 0 and tok.max() < 257152
+
+
+def test_bf16_helpers_round_to_nearest_even(pn):
+    x = np.array([1.0, 1.00390625, 1.005859375, -0.1, 45.254833995939045], np.float32)
+    bits = pn.f32_to_bf16_bits(x)
+    back = pn.bf16_bits_to_f32(bits)
+    # 1 + 2^-8 is a tie between 1 and 1+2^-7 -> even (1.0); 1.005859375 rounds up
+    assert back.tolist() == [1.0, 1.0, 1.0078125, -0.10009765625, 45.25]

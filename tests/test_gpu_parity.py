@@ -1,0 +1,161 @@
+"""GPU parity: the sm_100a engine through the C ABI against the CPU oracle on the same seeded weights,
+inputs and noise.
+
+Tolerances: action chunks max-abs <= 2e-2 and cosine >= 0.999.  Intermediate
+points (KV cache, image tokens) use rel-L2 <= 2e-2, i.e. bf16 rounding noise of reordered sums.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ACT_MAXABS = 2e-2
+ACT_COS = 0.999
+
+
+def cos(a, b):
+    a = a.ravel().astype(np.float64)
+    b = b.ravel().astype(np.float64)
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-30))
+
+
+def rel_l2(a, b):
+    a = a.astype(np.float64)
+    b = b.astype(np.float64)
+    return float(np.linalg.norm(a - b) / (np.linalg.norm(b) + 1e-30))
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+
+    assert torch.cuda.is_available()
+    return torch
+
+
+# ---------------------------------------------------------------- operators vs torch fp32
+@pytest.mark.parametrize("T,F,K", [(50, 2560, 1024), (50, 1024, 4096), (100, 2304, 1024), (968, 2560, 2048),
+                                   (800, 4096, 1024), (300, 1152, 4304), (3200, 1024, 4096)])
+def test_linear_store_matches_torch(pn, torch_cuda, T, F, K):
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(T * 7 + F)
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(F, K, device="cuda", generator=g) * 0.02).bfloat16()
+    b = (torch.randn(F, device="cuda", generator=g) * 0.02).bfloat16()
+    eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), max_batch=1)
+    out = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+    eng.op_linear(x, w, out, "store", bias=b)
+    eng.sync()
+    ref = (x.float() @ w.float().t() + b.float())
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-2, err
+
+
+@pytest.mark.parametrize("epi", ["gelu", "resid", "gated", "geglu", "f32"])
+@pytest.mark.parametrize("T", [50, 968])
+def test_linear_epilogues_match_torch(pn, torch_cuda, epi, T):
+    torch = torch_cuda
+    F, K = 1024, 1024
+    g = torch.Generator(device="cuda").manual_seed(11 + T)
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(F, K, device="cuda", generator=g) * 0.03).bfloat16()
+    res = torch.randn(T, F, device="cuda", generator=g).bfloat16()
+    gate = torch.randn(F, device="cuda", generator=g).bfloat16()
+    eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), max_batch=1)
+    acc = x.float() @ w.float().t()
+    rb = lambda t: t.bfloat16().float()
+    if epi == "geglu":
+        out = torch.empty(T, F // 2, device="cuda", dtype=torch.bfloat16)
+        ref = rb(torch.nn.functional.gelu(rb(acc[:, 0::2]), approximate="tanh")) * rb(acc[:, 1::2])
+    elif epi == "f32":
+        out = torch.empty(T, F, device="cuda", dtype=torch.float32)
+        ref = acc
+    else:
+        out = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+        if epi == "gelu":
+            ref = torch.nn.functional.gelu(rb(acc), approximate="tanh")
+        elif epi == "resid":
+            ref = res.float() + rb(acc)
+        else:
+            ref = res.float() + rb(rb(acc) * gate.float())
+    eng.op_linear(x, w, out, epi, res=res if epi in ("resid", "gated") else None,
+                  gate=gate if epi == "gated" else None)
+    eng.sync()
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2 * max(1.0, ref.abs().max().item()), (epi, err)
+
+
+@pytest.mark.parametrize("T,S,splits", [(50, 1018, 8), (50, 1018, 1), (968, 968, 1), (100, 2048, 4)])
+def test_attention_matches_torch(pn, torch_cuda, T, S, splits):
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(T + S)
+    b = 2
+    q = (torch.randn(b, T, 2560, device="cuda", generator=g) * 0.1).bfloat16()
+    k = torch.randn(b, S, 256, device="cuda", generator=g).bfloat16()
+    v = torch.randn(b, S, 256, device="cuda", generator=g).bfloat16()
+    out = torch.empty(b, T, 2048, device="cuda", dtype=torch.bfloat16)
+    eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), max_batch=1)
+    eng.op_attention(q, k, v, out, splits)
+    eng.sync()
+    qh = q[:, :, :2048].float().view(b, T, 8, 256)
+    logits = torch.einsum("bthd,bsd->bhts", qh, k.float())
+    p = torch.softmax(logits, -1)
+    ref = torch.einsum("bhts,bsd->bthd", p, v.float()).reshape(b, T, 2048)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 3e-2, err
+
+
+# ---------------------------------------------------------------- network vs oracle
+def test_denoise_expert_only_full_depth(pn, oracle):
+    """Config 1: 18-layer expert, 10 steps, N(0,1) bf16 968-token prefix cache."""
+    cfg = pn.Config.make()
+    eng = pn.Engine(cfg, max_batch=1)
+    eng.init_random_weights(0)
+    eng.synth_prefix_cache(1, seed=0)
+    noise = pn.synth_noise(0, 0)
+    act = eng.denoise(noise[None])[0]
+    k, v = oracle.gen_kv_cache(0, 0, 18, 968)
+    ocfg = oracle.Config.make()
+    ref = oracle.denoise(ocfg, 0, k, v, noise)
+    assert np.isfinite(act).all()
+    d = np.abs(act - ref).max()
+    c = cos(act, ref)
+    assert d <= ACT_MAXABS and c >= ACT_COS, (d, c)
+    # also within tolerance of the pure-fp32 network
+    ref32 = oracle.denoise(ocfg, 0, k, v, noise, flags=oracle.FP32_ACTIVATIONS)
+    assert np.abs(act - ref32).max() <= ACT_MAXABS and cos(act, ref32) >= ACT_COS
+
+
+def test_prefix_cache_and_actions_reduced_depth(pn, oracle):
+    """Full pipeline (SigLIP -> Gemma prefill -> denoise) at reduced depth, all widths full."""
+    cfg = pn.Config.make(siglip_layers=2, gemma_layers=2, num_steps=3)
+    eng = pn.Engine(cfg, max_batch=1)
+    eng.init_random_weights(1)
+    img = pn.synth_images(5, 0)
+    tok = pn.synth_tokens(5, 0)
+    noise = pn.synth_noise(5, 0)
+    act = eng.infer(img[None], tok[None], noise[None])[0]
+    ocfg = oracle.Config.make(siglip_layers=2, gemma_layers=2, num_steps=3)
+    pr = oracle.Probe(keep=["img.tokens"])
+    k, v = oracle.prefill(ocfg, 1, img, tok, probe=pr)
+    for l in range(2):
+        gk, gv = eng.get_prefix_cache(0, l)
+        assert rel_l2(gk, k[l]) < 2e-2, (l, rel_l2(gk, k[l]))
+        assert rel_l2(gv, v[l]) < 2e-2, (l, rel_l2(gv, v[l]))
+    ref = oracle.denoise(ocfg, 1, k, v, noise)
+    d = np.abs(act - ref).max()
+    assert d <= ACT_MAXABS and cos(act, ref) >= ACT_COS, (d, cos(act, ref))
+
+
+def test_batch_equals_single(pn):
+    """Batch API at n=4 returns, per sample, the bits of n=1 calls (reference batch_test, π05 record :300)."""
+    cfg = pn.Config.make(siglip_layers=1, gemma_layers=2, num_steps=2)
+    eng = pn.Engine(cfg, max_batch=4)
+    eng.init_random_weights(2)
+    imgs = np.stack([pn.synth_images(9, i) for i in range(4)])
+    toks = np.stack([pn.synth_tokens(9, i) for i in range(4)])
+    noise = np.stack([pn.synth_noise(9, i) for i in range(4)])
+    batch = eng.infer(imgs, toks, noise)
+    for i in range(4):
+        one = eng.infer(imgs[i:i + 1], toks[i:i + 1], noise[i:i + 1])[0]
+        np.testing.assert_allclose(one, batch[i], rtol=0, atol=1e-2)
