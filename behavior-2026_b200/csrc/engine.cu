@@ -780,6 +780,8 @@ bool create(pi05_engine* e) {
   if (prop.major != 10) return set_err(e, "this engine is built for sm_100a (B200); device is sm_" +
                                               std::to_string(prop.major) + std::to_string(prop.minor));
   e->num_sms = prop.multiProcessorCount;
+  // PI05_PDL=0 launches without programmatic dependent launch (each kernel waits for the previous one)
+  if (const char* s = getenv("PI05_PDL")) e->pdl = atoi(s) != 0;
   CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   cudaDriverEntryPointQueryResult q;
   void* fn = nullptr;
