@@ -11,7 +11,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libpi05.so")
-SOURCES = ["engine.cu"]
+SOURCES = ["engine.cu", "static_scratch.cu"]
 DEPS = SOURCES + ["common.cuh", "gemm_tc.cuh", "attention.cuh", "kernels.cuh", "pi05_model.h"]
 
 NVCC_FLAGS = [

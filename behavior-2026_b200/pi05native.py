@@ -23,7 +23,7 @@ EXPORTS = [
     "pi05_save_weights", "pi05_load_weights", "pi05_prefill", "pi05_set_prefix_cache", "pi05_get_prefix_cache",
     "pi05_denoise", "pi05_infer", "pi05_stream", "pi05_sync", "pi05_prefix_len", "pi05_graph_launches",
     "pi05_synth_images", "pi05_synth_tokens", "pi05_synth_noise", "pi05_synth_prefix_cache", "pi05_create_batch",
-    "pi05_infer_batch", "pi05_set_stage", "pi05_op_linear", "pi05_op_attention",
+    "pi05_infer_batch", "pi05_set_stage", "pi05_op_linear", "pi05_op_attention", "pi05_linear_static",
 ]
 
 
@@ -89,6 +89,7 @@ def _load():
     L.pi05_set_stage.argtypes = [vp, i32, i32, i32]
     L.pi05_op_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp]
     L.pi05_op_attention.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32]
+    L.pi05_linear_static.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_char_p, ctypes.c_size_t]
     return L
 
 
@@ -230,6 +231,22 @@ class Engine:
 
     def set_stage(self, slot, stage, mode=1):
         self._check(lib.pi05_set_stage(self._h, slot, stage, mode))
+
+
+def linear_static(x, w, out, bias=None, stream=None):
+    """pi05_linear_static on CUDA bf16 tensors: out = x . w^T + bias with no device allocation.
+
+    For callers that cannot allocate device memory; its scratch is a fixed 16 MiB device array
+    inside the library, shared by all calls (calls that overlap on the GPU race).  `stream` is a
+    raw cudaStream_t (int) or None for the legacy default stream.  Asynchronous.
+    """
+    T, K = x.shape
+    F = w.shape[0]
+    err = ctypes.create_string_buffer(512)
+    p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+    rc = lib.pi05_linear_static(T, F, K, p(x), p(w), p(bias), p(out), ctypes.c_void_p(stream or 0), err, len(err))
+    if rc != OK:
+        raise Pi05Error(rc, err.value.decode())
 
 
 def bf16_bits_to_f32(bits):

@@ -111,6 +111,19 @@ PI05_API int pi05_op_linear(pi05_engine* e, int T, int F, int K, const void* x, 
 PI05_API int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, int ldq, const void* k,
                                const void* v, void* out, int splits);
 
+/* Few-token linear layer that allocates nothing: out[T][F] = bf16(x[T][K] . w[F][K]^T + bias[F]), the
+ * same kernel and tiling as the engine's weight-streaming path, for callers that cannot call
+ * cudaMalloc (a process whose device memory is owned by another allocator, a real-time loop that
+ * must not allocate after start-up).  Its split-K scratch is one file-scope device array of
+ * 16 MiB that every GPU loading this library holds until exit.  Limits: 1 <= T <= 64,
+ * 1 <= F <= 65536, 8 <= K <= 65536, K % 8 == 0; other sizes return PI05_ERR_ARG with a message in err.
+ * The first call on a device sets that device up (looks up the array's address) and should come
+ * before any stream capture.  All calls share the array: calls that overlap on the GPU race.
+ * Asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream); x, w, bias, out are device
+ * pointers.  No counterpart in the reference's ABI. */
+PI05_API int pi05_linear_static(int T, int F, int K, const void* x, const void* w, const void* bias, void* out,
+                                void* stream, char* err, size_t err_len);
+
 /* Reference batch-API names (π05_네이티브엔진.md:288-303). */
 PI05_API pi05_engine* pi05_create_batch(const char* weights_path, int device, int max_batch);
 PI05_API int pi05_infer_batch(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* noise,
