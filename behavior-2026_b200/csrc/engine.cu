@@ -243,8 +243,30 @@ struct Lin {
 
 template <int BN>
 bool launch_gemm_bn(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga) {
-  dim3 grid(ga.tiles_m * ga.tiles_n, ga.splits);
-  return launch(e, gemm_tc_kernel<BN>, grid, dim3(256), (size_t)GemmCfg<BN>::SMEM, ga.pdl != 0, ta, tb, ga);
+  // persistent: at most one CTA per SM, each walks units blockIdx.x, +gridDim.x, ...
+  const int units = ga.tiles_m * ga.tiles_n * ga.splits;
+  dim3 grid(std::min(units, e->num_sms));
+  const size_t sm = (size_t)GemmCfg<BN>::SMEM;
+  switch (ga.epi) {
+    case EPI_GELU: return launch(e, gemm_tc_kernel<BN, EPI_GELU>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+    case EPI_RESID: return launch(e, gemm_tc_kernel<BN, EPI_RESID>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+    case EPI_GATED: return launch(e, gemm_tc_kernel<BN, EPI_GATED>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+    case EPI_GEGLU: return launch(e, gemm_tc_kernel<BN, EPI_GEGLU>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+    case EPI_F32: return launch(e, gemm_tc_kernel<BN, EPI_F32>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+    default: return launch(e, gemm_tc_kernel<BN, EPI_STORE>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+  }
+}
+
+template <int BN>
+bool set_gemm_smem(pi05_engine* e) {
+  const int sm = GemmCfg<BN>::SMEM;
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_GEGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  return true;
 }
 
 bool linear(pi05_engine* e, const Lin& L) {
@@ -271,7 +293,9 @@ bool linear(pi05_engine* e, const Lin& L) {
   }
   ga.K = L.K;
   ga.swap = swap;
-  ga.group_m = swap ? 1 : 16;
+  // Tile order: walk all N-tiles for a group of M-tiles whose A rows (~48 MB) stay in L2, so the
+  // weights are streamed from HBM once per group.
+  ga.group_m = swap ? 1 : std::max(1, std::min(ga.tiles_m, (int)((48ull << 20) / (128ull * L.K * 2))));
   const int tiles = ga.tiles_m * ga.tiles_n;
   int splits = 1;
   if (tiles < e->num_sms && kt >= 4) {
@@ -789,9 +813,7 @@ bool create(pi05_engine* e) {
   if (!fn || q != cudaDriverEntryPointSuccess) return set_err(e, "cuTensorMapEncodeTiled unavailable");
   e->encode = reinterpret_cast<EncodeTiledFn>(fn);
 
-  CK(cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<64>::SMEM));
-  CK(cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<128>::SMEM));
-  CK(cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<256>::SMEM));
+  if (!set_gemm_smem<64>(e) || !set_gemm_smem<128>(e) || !set_gemm_smem<256>(e)) return false;
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<P5_HD>::SMEM));
   CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_SIG_HD>::SMEM));
@@ -1145,7 +1167,7 @@ void pi05_synth_noise(uint64_t seed, int sample, int horizon, float* out) {
 int pi05_op_linear(pi05_engine* e, int T, int F, int K, const void* x, const void* w, const void* bias,
                    const void* res, const void* gate, int epi, void* out) {
   if (!e || T < 1 || F < 1 || K < 8 || K % 8 || epi < EPI_STORE || epi > EPI_F32 || !x || !w || !out ||
-      ((epi == EPI_RESID || epi == EPI_GATED) && !res) || (epi == EPI_GATED && !gate) || (epi == EPI_GEGLU && F % 2))
+      ((epi == EPI_RESID || epi == EPI_GATED) && !res) || (epi == EPI_GATED && !gate) || (epi == EPI_GEGLU && F % 32))
     return PI05_ERR_ARG;
   cudaSetDevice(e->device);
   Lin L{(const bf16*)x, K, T, (const bf16*)w, K, F, K};

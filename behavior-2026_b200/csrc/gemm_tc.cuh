@@ -1,16 +1,19 @@
 // gemm_tc.cuh — tcgen05/TMEM GEMM for sm_100a:  D[M][N] = A[M][K] . B[N][K]^T, bf16 in, fp32 accumulate.
 //
-// One CTA computes one 128 x BN tile (optionally a K-slice of it, split-K).  Warp roles:
-//   warp 0  TMA producer (one thread): STAGES-deep ring of (A, B) K-tiles of 64, 128-byte swizzle
-//   warp 1  MMA issuer (one thread):   tcgen05.mma 128xBNx16, accumulator in TMEM (BN f32 columns)
-//   warp 2  TMEM allocator
-//   warps 4-7 epilogue: tcgen05.ld of their 32-lane TMEM sub-partition, fused epilogue, global stores
+// Persistent: the grid has at most one CTA per SM and each CTA walks work units (tile, K-split)
+// u = blockIdx.x, blockIdx.x + gridDim.x, ...  Warp roles:
+//   warp 0  TMA producer (lane 0): STAGES-deep ring of (A, B) K-tiles of 64, 128-byte swizzle;
+//           the ring runs on across units, so the next tile's loads start while this one computes
+//   warp 1  MMA issuer (lane 0): tcgen05.mma 128xBNx16 into one of two TMEM accumulators
+//   warp 2  TMEM allocator (2 x BN f32 columns)
+//   warps 4-7 epilogue: tcgen05.ld of their 32-lane TMEM sub-partition, fused epilogue, stores.
+//           The accumulator is handed back as soon as it is read, so the epilogue of unit j
+//           overlaps the MMAs of unit j+1.
 //
-// The weights of every linear layer are stored [out][in] (K contiguous), so both operands are
-// K-major.  Two orientations:
+// Every linear layer stores its weights [out][in] (K contiguous): both operands are K-major.
 //   normal (swap = 0): A = activations [tokens][K], B = weights [features][K]; row = token, col = feature
-//   swap   (swap = 1): A = weights, B = activations; row = feature, col = token.  Used when there are
-//                      few tokens (the 50-token action expert): the 128-row MMA side walks the weights.
+//   swap   (swap = 1): A = weights, B = activations; row = feature, col = token.  Used for few tokens
+//                      (the 50-token action expert): the 128-row MMA side walks the weights.
 // Split-K partial tiles go to an fp32 workspace; the last CTA of a tile (ticket counter) sums the
 // partials in split order, so results do not depend on CTA timing.
 #pragma once
@@ -61,97 +64,161 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 4);
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
 };
 
-// ---- epilogue value pipeline (one scalar) ----
-__device__ __forceinline__ float epi_pre(const GemmArgs& a, float acc, int t, int f) {
-  float v = acc;
-  if (a.out_scale != 1.0f) v *= a.out_scale;
-  if (a.bias) v += bf(a.bias[f]);
-  if (a.addend) v += bf(a.addend[(size_t)(t % a.add_mod) * a.add_ld + f]);
-  return v;
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y), c = unpack_bf2(u.z), d = unpack_bf2(u.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
 }
-__device__ __forceinline__ float epi_final(const GemmArgs& a, float v, int t, int f) {
-  switch (a.epi) {
-    case EPI_GELU: return rbf(gelu_tanh(rbf(v)));
-    case EPI_RESID: return rbf(bf(a.res[(size_t)t * a.ld_res + f]) + rbf(v));
-    case EPI_GATED: {
-      const float g = bf(a.gate[(size_t)(t / a.gate_div) * a.ld_gate + f]);
-      return rbf(bf(a.res[(size_t)t * a.ld_res + f]) + rbf(rbf(v) * g));
+
+// ---- normal orientation: one token row t, 32 consecutive features f0..f0+31 ----
+template <int EPI>
+__device__ __forceinline__ void epi_row32(const GemmArgs& a, float (&v)[32], int t, int f0) {
+  if (t >= a.M || f0 >= a.N) return;
+  const bool full = f0 + 32 <= a.N;
+  if (full) {
+    if (a.out_scale != 1.0f) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= a.out_scale;
     }
-    default: return rbf(v);
+    if (a.bias) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float b[8];
+        unpack8(reinterpret_cast<const uint4*>(a.bias + f0)[q], b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[8 * q + i] += b[i];
+      }
+    }
+    if (a.addend) {
+      const bf16* ad = a.addend + (size_t)(t % a.add_mod) * a.add_ld + f0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float b[8];
+        unpack8(reinterpret_cast<const uint4*>(ad)[q], b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[8 * q + i] += b[i];
+      }
+    }
+    if (EPI == EPI_F32) {
+      float4* dst = reinterpret_cast<float4*>(a.out_f32 + (size_t)t * a.ld_out_f32 + f0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      return;
+    }
+    if (EPI == EPI_GEGLU) {
+      uint32_t o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float g0 = rbf(v[4 * j]), u0 = rbf(v[4 * j + 1]);
+        const float g1 = rbf(v[4 * j + 2]), u1 = rbf(v[4 * j + 3]);
+        o[j] = pack_bf2(rbf(gelu_tanh(g0)) * u0, rbf(gelu_tanh(g1)) * u1);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(a.out + (size_t)t * a.ld_out + f0 / 2);
+      dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      return;
+    }
+    if (EPI == EPI_GELU) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(rbf(v[i]));
+    }
+    if (EPI == EPI_RESID || EPI == EPI_GATED) {
+      const bf16* rr = a.res + (size_t)t * a.ld_res + f0;
+      const bf16* gg = EPI == EPI_GATED ? a.gate + (size_t)(t / a.gate_div) * a.ld_gate + f0 : nullptr;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float r8[8];
+        unpack8(reinterpret_cast<const uint4*>(rr)[q], r8);
+        if (EPI == EPI_GATED) {
+          float g8[8];
+          unpack8(reinterpret_cast<const uint4*>(gg)[q], g8);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[8 * q + i] = r8[i] + rbf(rbf(v[8 * q + i]) * g8[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[8 * q + i] = r8[i] + rbf(v[8 * q + i]);
+        }
+      }
+    }
+    uint32_t o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = pack_bf2(v[2 * j], v[2 * j + 1]);
+    uint4* dst = reinterpret_cast<uint4*>(a.out + (size_t)t * a.ld_out + f0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+    return;
+  }
+  // ragged edge: scalar
+#pragma unroll 1
+  for (int i = 0; i < 32; ++i) {
+    const int f = f0 + i;
+    if (f >= a.N) break;
+    float x = v[0];
+#pragma unroll
+    for (int k = 1; k < 32; ++k) x = (k == i) ? v[k] : x;
+    x *= a.out_scale;
+    if (a.bias) x += bf(a.bias[f]);
+    if (a.addend) x += bf(a.addend[(size_t)(t % a.add_mod) * a.add_ld + f]);
+    if (EPI == EPI_F32) {
+      a.out_f32[(size_t)t * a.ld_out_f32 + f] = x;
+      continue;
+    }
+    if (EPI == EPI_GEGLU) break;  // GeGLU widths are multiples of 32 (checked by the host)
+    if (EPI == EPI_GELU) x = gelu_tanh(rbf(x));
+    if (EPI == EPI_RESID) x = bf(a.res[(size_t)t * a.ld_res + f]) + rbf(x);
+    if (EPI == EPI_GATED)
+      x = bf(a.res[(size_t)t * a.ld_res + f]) + rbf(rbf(x) * bf(a.gate[(size_t)(t / a.gate_div) * a.ld_gate + f]));
+    a.out[(size_t)t * a.ld_out + f] = tobf(x);
   }
 }
 
-// Apply the epilogue to 32 accumulator values of one TMEM lane.
-//   normal: row = token t, columns f0..f0+31 (features)
-//   swap:   row = feature f, columns t0..t0+31 (tokens)
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const float (&v)[32], int row, int col0, int lane) {
-  if (!a.swap) {
-    const int t = row, f0 = col0;
-    if (t >= a.M) return;
-    const int nf = min(32, a.N - f0);
-    if (nf <= 0) return;
-    if (a.epi == EPI_F32) {
-      for (int i = 0; i < nf; ++i) a.out_f32[(size_t)t * a.ld_out_f32 + f0 + i] = epi_pre(a, v[i], t, f0 + i);
-      return;
-    }
-    if (a.epi == EPI_GEGLU) {
-      // columns (2j, 2j+1) = (gate_j, up_j)
-      __align__(16) bf16 o[16];
-      for (int j = 0; j < 16; ++j) {
-        const float g = rbf(epi_pre(a, v[2 * j], t, f0 + 2 * j));
-        const float u = rbf(epi_pre(a, v[2 * j + 1], t, f0 + 2 * j + 1));
-        o[j] = tobf(rbf(gelu_tanh(g)) * u);
-      }
-      bf16* dst = a.out + (size_t)t * a.ld_out + f0 / 2;
-      if (nf == 32) {
-        reinterpret_cast<uint4*>(dst)[0] = reinterpret_cast<const uint4*>(o)[0];
-        reinterpret_cast<uint4*>(dst)[1] = reinterpret_cast<const uint4*>(o)[1];
-      } else {
-        for (int j = 0; j < nf / 2; ++j) dst[j] = o[j];
-      }
-      return;
-    }
-    __align__(16) bf16 o[32];
-    for (int i = 0; i < 32; ++i) o[i] = tobf(i < nf ? epi_final(a, epi_pre(a, v[i], t, f0 + i), t, f0 + i) : 0.f);
-    bf16* dst = a.out + (size_t)t * a.ld_out + f0;
-    if (nf == 32) {
+// ---- swap orientation: one feature row f, 32 consecutive tokens t0..t0+31 ----
+template <int EPI>
+__device__ __forceinline__ void epi_col32(const GemmArgs& a, float (&v)[32], int f, int t0) {
+  const bool fok = f < a.M;
+  const float bias = (fok && a.bias) ? bf(a.bias[f]) : 0.f;
+  if (EPI == EPI_GEGLU) {
+    // rows (2j, 2j+1) = (gate_j, up_j): the partner value lives in the neighbouring lane
 #pragma unroll
-      for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(dst)[q] = reinterpret_cast<const uint4*>(o)[q];
-    } else {
-      for (int i = 0; i < nf; ++i) dst[i] = o[i];
-    }
-  } else {
-    const int f = row, t0 = col0;
-    const bool fok = f < a.M;
-    if (a.epi == EPI_GEGLU) {
-      // rows (2j, 2j+1) = (gate_j, up_j): partner lives in the neighbouring lane
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int t = t0 + i;
-        float mine = fok ? rbf(epi_pre(a, v[i], t, f)) : 0.f;
-        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
-        if (fok && (f & 1) == 0 && t < a.N) a.out[(size_t)t * a.ld_out + f / 2] = tobf(rbf(gelu_tanh(mine)) * other);
-      }
-      return;
-    }
-    if (!fok) return;
-#pragma unroll 4
     for (int i = 0; i < 32; ++i) {
       const int t = t0 + i;
-      if (t >= a.N) break;
-      if (a.epi == EPI_F32) {
-        a.out_f32[(size_t)t * a.ld_out_f32 + f] = epi_pre(a, v[i], t, f);
+      const float mine = rbf(v[i] * a.out_scale + bias);
+      const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+      if (fok && (f & 1) == 0 && t < a.N) a.out[(size_t)t * a.ld_out + f / 2] = tobf(rbf(gelu_tanh(mine)) * other);
+    }
+    return;
+  }
+  if (!fok) return;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int t = t0 + i;
+    if (t < a.N) {
+      float x = v[i] * a.out_scale + bias;
+      if (EPI == EPI_F32) {
+        a.out_f32[(size_t)t * a.ld_out_f32 + f] = x;
       } else {
-        a.out[(size_t)t * a.ld_out + f] = tobf(epi_final(a, epi_pre(a, v[i], t, f), t, f));
+        if (EPI == EPI_GELU) x = gelu_tanh(rbf(x));
+        if (EPI == EPI_RESID) x = bf(a.res[(size_t)t * a.ld_res + f]) + rbf(x);
+        if (EPI == EPI_GATED)
+          x = bf(a.res[(size_t)t * a.ld_res + f]) +
+              rbf(rbf(x) * bf(a.gate[(size_t)(t / a.gate_div) * a.ld_gate + f]));
+        a.out[(size_t)t * a.ld_out + f] = tobf(x);
       }
     }
   }
 }
 
-template <int BN>
+template <int EPI>
+__device__ __forceinline__ void epi_chunk(const GemmArgs& a, float (&v)[32], int row, int col0) {
+  if (a.swap)
+    epi_col32<EPI>(a, v, row, col0);
+  else
+    epi_row32<EPI>(a, v, row, col0);
+}
+
+template <int BN, int EPI>
 __global__ void __launch_bounds__(256, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    const GemmArgs args) {
@@ -163,27 +230,14 @@ __global__ void __launch_bounds__(256, 1)
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
   uint64_t* empty_bar = full_bar + C::STAGES;
-  uint64_t* accum_bar = empty_bar + C::STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+  uint64_t* tfull_bar = empty_bar + C::STAGES;  // [2] accumulator ready
+  uint64_t* tempty_bar = tfull_bar + 2;          // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort, [1] last split, [2] skip
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // tile coordinates (grouped along M so consecutive CTAs share B tiles in L2)
-  const int tile = blockIdx.x;
-  const int per_group = args.group_m * args.tiles_n;
-  const int group = tile / per_group;
-  const int first_m = group * args.group_m;
-  const int gm = min(args.group_m, args.tiles_m - first_m);
-  const int in_group = tile % per_group;
-  const int tm = first_m + in_group % gm;
-  const int tn = in_group / gm;
-  const int m0 = tm * C::BM, n0 = tn * BN;
-  const int split = blockIdx.y;
   const int kt_total = (args.K + C::BK - 1) / C::BK;
-  const int kt0 = split * args.kt_per_split;
-  const int kt1 = min(kt_total, kt0 + args.kt_per_split);
-  const int nkt = max(0, kt1 - kt0);
+  const int n_units = args.tiles_m * args.tiles_n * args.splits;
 
   // a device-side wait already gave up in an earlier kernel: skip the work (uniformly for the CTA)
   if (threadIdx.x == 0) flags[2] = args.status ? *((volatile int*)args.status) : 0;
@@ -195,7 +249,10 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(accum_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 4);  // one arrival per epilogue warp
+    }
     flags[0] = 0;
     flags[1] = 0;
     fence_barrier_init();
@@ -213,124 +270,192 @@ __global__ void __launch_bounds__(256, 1)
 
   if (args.pdl) pdl_launch_dependents();
 
+  // unit -> (tm, tn, split, k range); splits of one tile are consecutive units
+  auto decode = [&](int u, int& tm, int& tn, int& split, int& kt0, int& nkt) {
+    const int tile = u / args.splits;
+    split = u % args.splits;
+    const int per_group = args.group_m * args.tiles_n;
+    const int group = tile / per_group;
+    const int first_m = group * args.group_m;
+    const int gm = min(args.group_m, args.tiles_m - first_m);
+    const int in_group = tile % per_group;
+    tm = first_m + in_group % gm;
+    tn = in_group / gm;
+    kt0 = split * args.kt_per_split;
+    nkt = max(0, min(kt_total, kt0 + args.kt_per_split) - kt0);
+  };
+
   if (warp == 0) {
     if (lane == 0) {
-    // ---------------- producer
-    // In swap orientation A holds weights, which never depend on the previous kernel, so the
-    // first stages of A are requested before waiting for the predecessor grid.
-    const int pre = args.swap && args.pdl ? min(nkt, C::STAGES) : 0;
-    for (int i = 0; i < pre; ++i) {
-      mbar_arrive_expect_tx(&full_bar[i], C::STAGE_BYTES);
-      tma_load_2d(sA + i * C::A_BYTES, &tma_a, &full_bar[i], (kt0 + i) * C::BK, m0);
-    }
-    if (args.pdl) pdl_wait();
-    for (int i = 0; i < nkt; ++i) {
-      const int s = i % C::STAGES;
-      const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
-      if (i >= pre) {
-        if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.status, P5_ERR_WAIT_EMPTY)) {
-          flags[0] = 1;
-          break;
+      // ---------------- producer
+      int it = 0;
+      bool waited = !args.pdl;
+      for (int u = blockIdx.x; u < n_units && !flags[0]; u += gridDim.x) {
+        int tm, tn, split, kt0, nkt;
+        decode(u, tm, tn, split, kt0, nkt);
+        for (int i = 0; i < nkt; ++i, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.status, P5_ERR_WAIT_EMPTY)) {
+            flags[0] = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+          if (args.swap) {
+            // weights (A) never depend on the previous kernel: fetch them before waiting for it
+            tma_load_2d(sA + s * C::A_BYTES, &tma_a, &full_bar[s], (kt0 + i) * C::BK, tm * C::BM);
+            if (!waited) {
+              pdl_wait();
+              waited = true;
+            }
+            tma_load_2d(sB + s * C::B_BYTES, &tma_b, &full_bar[s], (kt0 + i) * C::BK, tn * BN);
+          } else {
+            if (!waited) {
+              pdl_wait();
+              waited = true;
+            }
+            tma_load_2d(sA + s * C::A_BYTES, &tma_a, &full_bar[s], (kt0 + i) * C::BK, tm * C::BM);
+            tma_load_2d(sB + s * C::B_BYTES, &tma_b, &full_bar[s], (kt0 + i) * C::BK, tn * BN);
+          }
         }
-        mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
-        tma_load_2d(sA + s * C::A_BYTES, &tma_a, &full_bar[s], (kt0 + i) * C::BK, m0);
       }
-      tma_load_2d(sB + s * C::B_BYTES, &tma_b, &full_bar[s], (kt0 + i) * C::BK, n0);
-    }
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
-    // ---------------- MMA issuer
-    if (args.pdl) pdl_wait();
-    constexpr uint32_t idesc = mma_idesc_bf16(C::BM, BN);
-    for (int i = 0; i < nkt; ++i) {
-      const int s = i % C::STAGES;
-      const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
-      if (flags[0] || !mbar_wait(&full_bar[s], ph, args.status, P5_ERR_WAIT_FULL)) {
-        flags[0] = 1;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES), b_addr = smem_u32(sB + s * C::B_BYTES);
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = mma_idesc_bf16(C::BM, BN);
+      int it = 0, j = 0;
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++j) {
+        int tm, tn, split, kt0, nkt;
+        decode(u, tm, tn, split, kt0, nkt);
+        const int acc = j & 1;
+        const uint32_t aph = (uint32_t)(j >> 1) & 1u;
+        if (!flags[0] && !mbar_wait(&tempty_bar[acc], aph ^ 1u, args.status, P5_ERR_WAIT_ACCUM)) flags[0] = 1;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int i = 0; i < nkt && !flags[0]; ++i, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+          if (!mbar_wait(&full_bar[s], ph, args.status, P5_ERR_WAIT_FULL)) {
+            flags[0] = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES), b_addr = smem_u32(sB + s * C::B_BYTES);
 #pragma unroll
-      for (int kk = 0; kk < C::BK / 16; ++kk) {
-        tc_mma_f16(tmem_base, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
-                   (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < C::BK / 16; ++kk)
+            tc_mma_f16(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
+                       (i > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&empty_bar[s]);  // frees the stage once these MMAs have read it
+        }
+        tc_commit(&tfull_bar[acc]);  // accumulator complete (or abandoned on abort)
       }
-      tc_commit(&empty_bar[s]);  // frees the stage once these MMAs have read it
-    }
-    tc_commit(accum_bar);  // accumulator complete
     }
     __syncwarp();
   } else if (warp >= 4) {
     // ---------------- epilogue
     if (args.pdl) pdl_wait();
     const int sub = warp & 3;  // TMEM lanes [32*sub, 32*sub+32)
-    const int row = m0 + sub * 32 + lane;
-    const bool ok = mbar_wait(accum_bar, 0, args.status, P5_ERR_WAIT_ACCUM) && nkt > 0;
-    tc_fence_after();
-    const int ntid = 128;
-    if (args.splits == 1) {
-      if (ok) {
+    const uint32_t lane_addr = (uint32_t)(sub * 32) << 16;
+    int j = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++j) {
+      int tm, tn, split, kt0, nkt;
+      decode(u, tm, tn, split, kt0, nkt);
+      const int acc = j & 1;
+      const uint32_t aph = (uint32_t)(j >> 1) & 1u;
+      const bool ok = mbar_wait(&tfull_bar[acc], aph, args.status, P5_ERR_WAIT_ACCUM) && !flags[0] && nkt > 0;
+      tc_fence_after();
+      const uint32_t t_acc = tmem_base + lane_addr + (uint32_t)(acc * BN);
+      const int row = tm * C::BM + sub * 32 + lane;
+      const int col_base = tn * BN;
+      if (args.splits == 1) {
+#pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
-          tmem_ld32(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)c, r);
+          tmem_ld32(t_acc + (uint32_t)c, r);
           tmem_wait_ld();
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          epilogue_chunk(args, v, row, n0 + c, lane);
+          for (int i = 0; i < 32; ++i) v[i] = ok ? __uint_as_float(r[i]) : 0.f;
+          if (ok) epi_chunk<EPI>(args, v, row, col_base + c);
         }
-      }
-    } else {
-      // split-K: write the partial tile, take a ticket, the last split reduces in split order
-      const int tile_id = tm * args.tiles_n + tn;
-      const size_t tile_elems = (size_t)C::BM * BN;
-      float* mine = args.ws + ((size_t)split * args.tiles_m * args.tiles_n + tile_id) * tile_elems;
-      const int lrow = sub * 32 + lane;
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        if (ok) {
-          tmem_ld32(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)c, r);
-          tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = 0u;
-        }
-        float4* dst = reinterpret_cast<float4*>(mine + (size_t)lrow * BN + c);
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
-                               __uint_as_float(r[4 * q + 3]));
-      }
-      __threadfence();
-      asm volatile("bar.sync 1, %0;" ::"r"(ntid));
-      if (threadIdx.x == 128) {
-        const int prev = atomicAdd(&args.counters[tile_id], 1);
-        flags[1] = (prev == args.splits - 1) ? 1 : 0;
-        if (prev == args.splits - 1) args.counters[tile_id] = 0;  // re-arm for the next launch
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(ntid));
-      if (flags[1]) {
-        __threadfence();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      } else {
+        // split-K: partial tile to the workspace, ticket, the last split reduces in split order
+        const int tile_id = tm * args.tiles_n + tn;
+        const size_t tile_elems = (size_t)C::BM * BN;
+        const int lrow = sub * 32 + lane;
+        float* mine = args.ws + ((size_t)split * args.tiles_m * args.tiles_n + tile_id) * tile_elems + (size_t)lrow * BN;
+#pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
-          float v[32];
+          uint32_t r[32];
+          tmem_ld32(t_acc + (uint32_t)c, r);
+          tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(mine + c);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
-          for (int s = 0; s < args.splits; ++s) {
-            const float4* src = reinterpret_cast<const float4*>(
-                args.ws + ((size_t)s * args.tiles_m * args.tiles_n + tile_id) * tile_elems + (size_t)lrow * BN + c);
+          for (int q = 0; q < 8; ++q)
+            dst[q] = ok ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                      __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);  // accumulator free for the next unit
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 128) {
+          const int prev = atomicAdd(&args.counters[tile_id], 1);
+          flags[1] = (prev == args.splits - 1) ? 1 : 0;
+          if (prev == args.splits - 1) args.counters[tile_id] = 0;  // re-arm for the next launch
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (flags[1]) {
+          __threadfence();
+          const float* base = args.ws + (size_t)tile_id * tile_elems + (size_t)lrow * BN;
+          const size_t sstride = (size_t)args.tiles_m * args.tiles_n * tile_elems;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            float v[32];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 p = __ldcg(src + q);
-              v[4 * q] += p.x;
-              v[4 * q + 1] += p.y;
-              v[4 * q + 2] += p.z;
-              v[4 * q + 3] += p.w;
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            // four splits' loads in flight per round; the sums still run in split order
+            int s = 0;
+#pragma unroll 1
+            for (; s + 4 <= args.splits; s += 4) {
+              float4 p[4][8];
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const float4* src = reinterpret_cast<const float4*>(base + (s + h) * sstride + c);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) p[h][q] = __ldcg(src + q);
+              }
+#pragma unroll
+              for (int h = 0; h < 4; ++h)
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  v[4 * q] += p[h][q].x;
+                  v[4 * q + 1] += p[h][q].y;
+                  v[4 * q + 2] += p[h][q].z;
+                  v[4 * q + 3] += p[h][q].w;
+                }
             }
+#pragma unroll 1
+            for (; s < args.splits; ++s) {
+              const float4* src = reinterpret_cast<const float4*>(base + s * sstride + c);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 p = __ldcg(src + q);
+                v[4 * q] += p.x;
+                v[4 * q + 1] += p.y;
+                v[4 * q + 2] += p.z;
+                v[4 * q + 3] += p.w;
+              }
+            }
+            epi_chunk<EPI>(args, v, row, col_base + c);
           }
-          epilogue_chunk(args, v, row, n0 + c, lane);
         }
       }
     }

@@ -65,7 +65,8 @@ int setup(int dev, char* err, size_t err_len) {
   void* p = nullptr;
   cudaError_t ce = cudaGetSymbolAddress(&p, g_static_scratch);
   if (ce != cudaSuccess || !p) return fail(err, err_len, PI05_ERR_CUDA, "cudaGetSymbolAddress(g_static_scratch) failed");
-  ce = cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<64>::SMEM);
+  ce = cudaFuncSetAttribute(gemm_tc_kernel<64, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            GemmCfg<64>::SMEM);
   if (ce != cudaSuccess) return fail(err, err_len, PI05_ERR_CUDA, "cudaFuncSetAttribute failed");
   if (cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return fail(err, err_len, PI05_ERR_CUDA, "cudaDeviceGetAttribute failed");
@@ -145,7 +146,8 @@ extern "C" PI05_API int pi05_linear_static(int T, int F, int K, const void* x, c
     return fail(err, err_len, PI05_ERR_ARG, "pi05_linear_static: tensor map rejected the operands");
   if (cudaMemsetAsync(s.scratch, 0, P5_STATIC_TICKET_BYTES, st) != cudaSuccess)
     return fail(err, err_len, PI05_ERR_CUDA, "pi05_linear_static: clearing the tickets failed");
-  gemm_tc_kernel<64><<<dim3(ga.tiles_m, ga.splits), 256, GemmCfg<64>::SMEM, st>>>(ta, tb, ga);
+  const int units = ga.tiles_m * ga.splits;
+  gemm_tc_kernel<64, EPI_STORE><<<dim3(std::min(units, s.num_sms)), 256, GemmCfg<64>::SMEM, st>>>(ta, tb, ga);
   const cudaError_t ce = cudaGetLastError();
   if (ce != cudaSuccess) return fail(err, err_len, PI05_ERR_CUDA, cudaGetErrorString(ce));
   return PI05_OK;

@@ -419,13 +419,31 @@ def run_sweep(args, local):
     return 0
 
 
+def run_gemm(args, local):
+    """One linear layer M x N x K (`--gemm M,N,K`, epilogue `--epi`), timed with CUDA events: the small,
+    self-contained case the kernel profiles are captured on."""
+    import pi05native as pn
+    M, N, K = (int(v) for v in args.gemm.split(","))
+    hbm, tf_burst, _, src = peaks()
+    eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), device=local, max_batch=1)
+    ms = gemm_roofline(pn, eng, M, N, K, args.epi, reps=max(1, args.steps))
+    fl = 2.0 * M * N * K
+    print(json.dumps({"op": "linear", "epi": args.epi, "M": M, "N": N, "K": K, "ms": ms,
+                      "tflops": fl / (ms / 1e3) / 1e12, "frac": fl / (ms / 1e3) / 1e12 / tf_burst,
+                      "peak": tf_burst, "peak_source": src}), flush=True)
+    eng.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="bs64", choices=["bs64", "bs1", "denoise", "sweep"])
+    ap.add_argument("--workload", default="bs64", choices=["bs64", "bs1", "denoise", "sweep", "gemm"])
+    ap.add_argument("--gemm", default="7744,32768,2048", help="M,N,K for --workload gemm")
+    ap.add_argument("--epi", default="geglu", help="epilogue for --workload gemm")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -440,6 +458,8 @@ def main():
     try:
         if args.workload == "sweep":
             return run_sweep(args, local) if rank == 0 else 0
+        if args.workload == "gemm":
+            return run_gemm(args, local) if rank == 0 else 0
         return run_ours(args, world, rank, local)
     finally:
         if world > 1:
