@@ -39,6 +39,8 @@ struct AttnArgs {
   float* ws_o;      // [batch*splits][rows][HD] unnormalised partial outputs
   float* ws_ml;     // [batch*splits][rows][2]   running max, running sum
   int pdl;
+  float* lse;       // optional (splits == 1): log-sum-exp per row, [b * lse_b + row]
+  long lse_b;
 };
 
 template <int HD>
@@ -245,6 +247,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
     const int hq = a.G > 1 ? row % a.G : mha_head;
     if (a.splits == 1) {
       const float inv = l_run[h] > 0.f ? 1.0f / l_run[h] : 0.f;
+      if (a.lse && cq == 0) a.lse[b * a.lse_b + row] = m_run[h] + logf(l_run[h]);
       bf16* dst = a.out + b * a.o_bstride + (long)tok * a.ldo + hq * HD;
 #pragma unroll
       for (int dt = 0; dt < C::ND; ++dt)

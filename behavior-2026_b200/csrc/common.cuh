@@ -149,6 +149,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 32 lanes x 16 consecutive 32-bit columns -> 16 registers per thread
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with 128-byte swizzle:
@@ -162,9 +171,23 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
   d |= (uint64_t)2 << 61;                  // layout: 128-byte swizzle
   return d;
 }
-// Instruction descriptor: kind::f16, A=B=bf16, D=f32, both K-major, M x N tile.
-__host__ __device__ constexpr uint32_t mma_idesc_bf16(int M, int N) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// Descriptor for an MN-major tile written by TMA with 128-byte swizzle as boxes of 64 (MN) x rows (K):
+// each 128-byte row holds 64 consecutive MN elements, consecutive rows are consecutive K, 8-row atoms
+// are 1024 bytes apart (stride byte offset) and the second 64-wide MN block starts `mn_block_bytes`
+// after the first (leading byte offset).
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t saddr, uint32_t mn_block_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((mn_block_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+// Instruction descriptor: kind::f16, A=B=bf16, D=f32, M x N tile; A K-major unless a_mn (MN-major).
+__host__ __device__ constexpr uint32_t mma_idesc_bf16(int M, int N, bool a_mn = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
 }
 
 // ------------------------------------------------------------------ legacy tensor-core helpers (attention)

@@ -94,6 +94,7 @@ struct pi05_engine {
   std::map<int, cudaGraphExec_t> denoise_graphs, prefill_graphs;
   std::map<int, long> denoise_launches, prefill_launches;
   long launches = 0;  // kernels enqueued (counted at capture time)
+  struct Trainer* tr = nullptr;  // LoRA train state (train.cuh), created by pi05_lora_init
 };
 
 namespace {
@@ -220,6 +221,21 @@ bool make_tmap(pi05_engine* e, CUtensorMap* m, const bf16* base, long rows, int 
   return true;
 }
 
+// general 2-D map: `inner` contiguous elements per row, `rows` rows of stride `ld`, box inner x box_rows
+bool make_tmap_box(pi05_engine* e, CUtensorMap* m, const bf16* base, long rows, long inner, int ld, int box_inner,
+                   int box_rows) {
+  if (((uintptr_t)base & 15) || (ld * 2) % 16) return set_err(e, "tensor map: misaligned operand");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = e->encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16*>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_err(e, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return true;
+}
+
 // One linear layer y = x W^T with a fused epilogue.  x: [T][K] (ld ldx), W: [F][K] (ld ldw).
 struct Lin {
   const bf16* x;
@@ -239,6 +255,13 @@ struct Lin {
   float out_scale = 1.0f;
   const bf16* addend = nullptr;
   int add_ld = 0, add_mod = 1;
+  // LoRA path
+  bool no_swap = false;  // keep tokens on the 128-row side even for few tokens
+  bool amn = false;      // x is [K rows][T columns] read MN-major: D[T][F] = x^T . w^T (weight gradients)
+  bf16* out_t = nullptr;
+  int ld_out_t = 0;
+  int lg_mode = 0, lg_trans = 0, lg_K = 0;
+  long lg_off[3] = {0, 0, 0};
 };
 
 template <int BN>
@@ -258,6 +281,33 @@ bool launch_gemm_bn(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb
 }
 
 template <int BN>
+bool launch_gemm_small(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga, bool amn) {
+  const int units = ga.tiles_m * ga.tiles_n * ga.splits;
+  dim3 grid(std::min(units, e->num_sms));
+  const size_t sm = (size_t)GemmCfg<BN>::SMEM;
+  if (amn) return launch(e, gemm_tc_kernel<BN, EPI_LORA_GRAD, true>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+  switch (ga.epi) {
+    case EPI_STORE_T:
+      return launch(e, gemm_tc_kernel<BN, EPI_STORE_T>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+    case EPI_LORA_GRAD:
+      return launch(e, gemm_tc_kernel<BN, EPI_LORA_GRAD>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+    case EPI_F32: return launch(e, gemm_tc_kernel<BN, EPI_F32>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+    default: return launch(e, gemm_tc_kernel<BN, EPI_STORE>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+  }
+}
+
+template <int BN>
+bool set_gemm_smem_small(pi05_engine* e) {
+  const int sm = GemmCfg<BN>::SMEM;
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_LORA_GRAD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_STORE_T>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_LORA_GRAD>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  return true;
+}
+
+template <int BN>
 bool set_gemm_smem(pi05_engine* e) {
   const int sm = GemmCfg<BN>::SMEM;
   CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
@@ -271,11 +321,26 @@ bool set_gemm_smem(pi05_engine* e) {
 
 bool linear(pi05_engine* e, const Lin& L) {
   GemmArgs ga = {};
-  const bool swap = L.T <= 128;
+  const bool swap = L.T <= 128 && !L.no_swap && !L.amn;
   int BN;
   CUtensorMap ta, tb;
   const int kt = (L.K + 63) / 64;
-  if (swap) {
+  if (L.F <= 48 && !swap) {
+    // small-N GEMMs of the LoRA path: U = x A^T, V = dy B, and the weight gradients (N = 16 per adapter)
+    BN = (L.F + 15) / 16 * 16;
+    ga.M = L.T;
+    ga.N = L.F;
+    ga.tiles_m = (L.T + 127) / 128;
+    ga.tiles_n = 1;
+    if (L.amn) {
+      if (!make_tmap_box(e, &ta, L.x, L.K, L.T, L.ldx, 64, 64)) return false;
+    } else if (!make_tmap(e, &ta, L.x, L.T, L.K, L.ldx, 128)) {
+      return false;
+    }
+    if (!make_tmap(e, &tb, L.w, L.F, L.K, L.ldw, BN)) return false;
+  } else if (L.amn) {
+    return set_err(e, "MN-major A operand is only wired for N <= 48");
+  } else if (swap) {
     BN = L.T <= 64 ? 64 : 128;
     ga.M = L.F;
     ga.N = L.T;
@@ -327,6 +392,15 @@ bool linear(pi05_engine* e, const Lin& L) {
   ga.counters = e->counters;
   ga.status = e->d_status;
   ga.pdl = e->pdl ? 1 : 0;
+  ga.out_t = L.out_t;
+  ga.ld_out_t = L.ld_out_t;
+  ga.lg_mode = L.lg_mode;
+  ga.lg_trans = L.lg_trans;
+  ga.lg_K = L.lg_K;
+  for (int i = 0; i < 3; ++i) ga.lg_off[i] = L.lg_off[i];
+  if (BN == 16) return launch_gemm_small<16>(e, ta, tb, ga, L.amn);
+  if (BN == 32) return launch_gemm_small<32>(e, ta, tb, ga, L.amn);
+  if (BN == 48) return launch_gemm_small<48>(e, ta, tb, ga, L.amn);
   if (BN == 64) return launch_gemm_bn<64>(e, ta, tb, ga);
   if (BN == 128) return launch_gemm_bn<128>(e, ta, tb, ga);
   return launch_gemm_bn<256>(e, ta, tb, ga);
@@ -460,7 +534,7 @@ bool run_gemma(pi05_engine* e, int n) {
   for (int l = 0; l < e->cfg.gemma_layers; ++l) {
     const GemLayer& g = e->gem[l];
     if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.px, A.ph, g.rms1, (const bf16*)nullptr,
-                T, D, 1, 0))
+                T, D, 1, 0, D))
       return false;
     Lin q{A.ph, D, T, g.wqkv, D, P5_QKV, D};
     q.out = A.pqkv;
@@ -469,7 +543,7 @@ bool run_gemma(pi05_engine* e, int n) {
     bf16* kc = A.kcache + l * cache_layer;
     bf16* vc = A.vcache + l * cache_layer;
     if (!launch(e, rope_qkv_kernel, dim3(T), dim3(256), 0, true, A.pqkv, T, P, 0, kc, vc, (const float*)e->d_cos,
-                (const float*)e->d_sin))
+                (const float*)e->d_sin, 256))
       return false;
     if (l == e->cfg.gemma_layers - 1) break;  // later outputs of the last layer feed nothing
     AttnArgs at = {};
@@ -499,7 +573,7 @@ bool run_gemma(pi05_engine* e, int n) {
     o.ld_res = D;
     if (!linear(e, o)) return false;
     if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.px, A.ph, g.rms2, (const bf16*)nullptr,
-                T, D, 1, 0))
+                T, D, 1, 0, D))
       return false;
     Lin gu{A.ph, D, T, g.wgu, D, 2 * P5_GEM_MLP, D};
     gu.epi = EPI_GEGLU;
@@ -542,14 +616,14 @@ bool run_denoise_body(pi05_engine* e, int n) {
       const ExpLayer& x = e->ex[l];
       const bf16* m1 = mrow + (size_t)(2 * l) * 3 * D;
       const bf16* m2 = mrow + (size_t)(2 * l + 1) * 3 * D;
-      if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m1, m1 + D, T, D, 1, 0))
+      if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m1, m1 + D, T, D, 1, 0, D))
         return false;
       Lin q{A.eh, D, T, x.wqkv, D, P5_QKV, D};
       q.out = A.eqkv;
       q.ld_out = P5_QKV;
       if (!linear(e, q)) return false;
       if (!launch(e, rope_qkv_kernel, dim3(T), dim3(256), 0, true, A.eqkv, T, H, P, A.ek, A.ev, (const float*)e->d_cos,
-                  (const float*)e->d_sin))
+                  (const float*)e->d_sin, 256))
         return false;
       AttnArgs at = {};
       at.q = A.eqkv;
@@ -583,7 +657,7 @@ bool run_denoise_body(pi05_engine* e, int n) {
       o.ld_gate = 0;
       o.gate_div = 1;
       if (!linear(e, o)) return false;
-      if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m2, m2 + D, T, D, 1, 0))
+      if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m2, m2 + D, T, D, 1, 0, D))
         return false;
       Lin gu{A.eh, D, T, x.wgu, D, 2 * P5_EXP_MLP, D};
       gu.epi = EPI_GEGLU;
@@ -602,7 +676,7 @@ bool run_denoise_body(pi05_engine* e, int n) {
       if (!linear(e, dn)) return false;
     }
     const bf16* mf = mrow + (size_t)(e->NM - 1) * 3 * D;
-    if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, mf, mf + D, T, D, 1, 0))
+    if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, mf, mf + D, T, D, 1, 0, D))
       return false;
     if (!launch(e, action_out_euler_kernel, dim3(rows_grid((long)T * P5_ACT_D)), dim3(256), 0, true,
                 (const bf16*)A.eh, (const bf16*)e->aout_w, (const bf16*)e->aout_b, A.xt, (float*)nullptr, T, D, dtb))
@@ -814,6 +888,7 @@ bool create(pi05_engine* e) {
   e->encode = reinterpret_cast<EncodeTiledFn>(fn);
 
   if (!set_gemm_smem<64>(e) || !set_gemm_smem<128>(e) || !set_gemm_smem<256>(e)) return false;
+  if (!set_gemm_smem_small<16>(e) || !set_gemm_smem_small<32>(e) || !set_gemm_smem_small<48>(e)) return false;
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<P5_HD>::SMEM));
   CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_SIG_HD>::SMEM));
@@ -869,6 +944,8 @@ bool create(pi05_engine* e) {
 
 }  // namespace
 
+#include "train.cuh"
+
 // ===================================================================== C ABI
 extern "C" {
 
@@ -914,6 +991,7 @@ void pi05_destroy(pi05_engine* e) {
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (auto& kv : e->denoise_graphs) cudaGraphExecDestroy(kv.second);
   for (auto& kv : e->prefill_graphs) cudaGraphExecDestroy(kv.second);
+  delete e->tr;
   for (void* p : e->allocs) cudaFree(p);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;

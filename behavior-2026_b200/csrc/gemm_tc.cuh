@@ -28,6 +28,9 @@ enum EpiKind : int {
   EPI_GATED = 3,  // out = R(res + R(R(v) * gate))          (adaRMS gated residual)
   EPI_GEGLU = 4,  // features interleaved (gate, up): out[f/2] = R(R(gelu(R(g))) * R(u))
   EPI_F32 = 5,    // out_f32 = v (no rounding)
+  // small-N epilogues of the LoRA path (normal orientation, BN <= 48)
+  EPI_STORE_T = 6,    // x = R(v*out_scale): out[t][f] = x and out_t[f][t] = x (transposed copy)
+  EPI_LORA_GRAD = 7,  // fp32 gradient accumulate: D[m][c] with adapter c/16 (see GemmArgs lg_*)
 };
 // v = acc * out_scale + bias[f] + addend[(t % add_mod)][f]
 
@@ -54,6 +57,16 @@ struct GemmArgs {
   int* counters;
   int* status;
   int pdl;  // kernel launched with programmatic stream serialization
+  // EPI_STORE_T
+  bf16* out_t;
+  int ld_out_t;
+  // EPI_LORA_GRAD: D[m][c] (m = feature row, c = adapter column, adapter a = c / 16) is added to
+  //   lg_trans == 0 (dB, [rows][16]):  out_f32[lg_off[a] + r_a(m) * 16 + c % 16], kept when m belongs to a
+  //   lg_trans == 1 (dA, [16][lg_K]):  out_f32[lg_off[a] + (c % 16) * lg_K + m]
+  // lg_mode selects which rows belong to which adapter: 0 all rows to adapter 0; 1 the q|k|v row ranges
+  // (2048 | 256 | 256); 2 interleaved gate/up rows (a = m % 2, r_a = m / 2).
+  int lg_mode, lg_trans, lg_K;
+  long lg_off[3];
 };
 
 template <int BN>
@@ -62,9 +75,10 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 4);
+  static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : (BN >= 64 ? 4 : 6));
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+  static constexpr int CH = (BN % 32 == 0) ? 32 : 16;  // epilogue chunk (TMEM columns per tcgen05.ld)
 };
 
 __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
@@ -108,6 +122,14 @@ __device__ __forceinline__ void epi_row32(const GemmArgs& a, float (&v)[32], int
       return;
     }
     if (EPI == EPI_GEGLU) {
+      if (a.out_t) {
+        // keep the pre-activations R(gate), R(up) (interleaved) for the backward pass
+        uint4* pre = reinterpret_cast<uint4*>(a.out_t + (size_t)t * a.ld_out_t + f0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          pre[q] = make_uint4(pack_bf2(v[8 * q], v[8 * q + 1]), pack_bf2(v[8 * q + 2], v[8 * q + 3]),
+                              pack_bf2(v[8 * q + 4], v[8 * q + 5]), pack_bf2(v[8 * q + 6], v[8 * q + 7]));
+      }
       uint32_t o[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -210,6 +232,39 @@ __device__ __forceinline__ void epi_col32(const GemmArgs& a, float (&v)[32], int
   }
 }
 
+// small-N epilogues (BN <= 48, normal orientation): one row, CH consecutive columns, scalar
+template <int EPI, int CH>
+__device__ __forceinline__ void epi_small(const GemmArgs& a, const float (&v)[32], int row, int col0) {
+  if (row >= a.M) return;
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const int c = col0 + i;
+    if (c >= a.N) break;
+    if (EPI == EPI_LORA_GRAD) {
+      const int ad = c >> 4;
+      if (a.lg_trans) {
+        a.out_f32[a.lg_off[ad] + (long)(c & 15) * a.lg_K + row] += v[i];
+      } else {
+        int owner = 0, r = row;
+        if (a.lg_mode == 1) {
+          owner = row < 2048 ? 0 : (row < 2304 ? 1 : 2);
+          r = row - (owner == 0 ? 0 : (owner == 1 ? 2048 : 2304));
+        } else if (a.lg_mode == 2) {
+          owner = row & 1;
+          r = row >> 1;
+        }
+        if (owner == ad) a.out_f32[a.lg_off[ad] + (long)r * 16 + (c & 15)] += v[i];
+      }
+    } else if (EPI == EPI_F32) {
+      a.out_f32[(size_t)row * a.ld_out_f32 + c] = v[i] * a.out_scale;
+    } else {
+      const bf16 x = tobf(v[i] * a.out_scale);
+      a.out[(size_t)row * a.ld_out + c] = x;
+      if (EPI == EPI_STORE_T) a.out_t[(size_t)c * a.ld_out_t + row] = x;
+    }
+  }
+}
+
 template <int EPI>
 __device__ __forceinline__ void epi_chunk(const GemmArgs& a, float (&v)[32], int row, int col0) {
   if (a.swap)
@@ -218,7 +273,7 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs& a, float (&v)[32], int
     epi_row32<EPI>(a, v, row, col0);
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool AMN = false>
 __global__ void __launch_bounds__(256, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    const GemmArgs args) {
@@ -314,7 +369,14 @@ __global__ void __launch_bounds__(256, 1)
               pdl_wait();
               waited = true;
             }
-            tma_load_2d(sA + s * C::A_BYTES, &tma_a, &full_bar[s], (kt0 + i) * C::BK, tm * C::BM);
+            if (AMN) {
+              // A is [K rows][M columns]: two boxes of 64 M-columns x 64 K-rows
+              tma_load_2d(sA + s * C::A_BYTES, &tma_a, &full_bar[s], tm * C::BM, (kt0 + i) * C::BK);
+              tma_load_2d(sA + s * C::A_BYTES + C::A_BYTES / 2, &tma_a, &full_bar[s], tm * C::BM + 64,
+                          (kt0 + i) * C::BK);
+            } else {
+              tma_load_2d(sA + s * C::A_BYTES, &tma_a, &full_bar[s], (kt0 + i) * C::BK, tm * C::BM);
+            }
             tma_load_2d(sB + s * C::B_BYTES, &tma_b, &full_bar[s], (kt0 + i) * C::BK, tn * BN);
           }
         }
@@ -324,7 +386,7 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      constexpr uint32_t idesc = mma_idesc_bf16(C::BM, BN);
+      constexpr uint32_t idesc = mma_idesc_bf16(C::BM, BN, AMN);
       int it = 0, j = 0;
       for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++j) {
         int tm, tn, split, kt0, nkt;
@@ -344,9 +406,11 @@ __global__ void __launch_bounds__(256, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES), b_addr = smem_u32(sB + s * C::B_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < C::BK / 16; ++kk)
-            tc_mma_f16(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
-                       (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < C::BK / 16; ++kk) {
+            const uint64_t ad = AMN ? sw128_mnmajor_desc(a_addr + kk * 2048, C::A_BYTES / 2)
+                                    : sw128_kmajor_desc(a_addr + kk * 32);
+            tc_mma_f16(d_tmem, ad, sw128_kmajor_desc(b_addr + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          }
           tc_commit(&empty_bar[s]);  // frees the stage once these MMAs have read it
         }
         tc_commit(&tfull_bar[acc]);  // accumulator complete (or abandoned on abort)
@@ -371,14 +435,23 @@ __global__ void __launch_bounds__(256, 1)
       const int col_base = tn * BN;
       if (args.splits == 1) {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = 0; c < BN; c += C::CH) {
           uint32_t r[32];
-          tmem_ld32(t_acc + (uint32_t)c, r);
+          if (C::CH == 32) {
+            tmem_ld32(t_acc + (uint32_t)c, r);
+          } else {
+            tmem_ld16(t_acc + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
           tmem_wait_ld();
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = ok ? __uint_as_float(r[i]) : 0.f;
-          if (ok) epi_chunk<EPI>(args, v, row, col_base + c);
+          for (int i = 0; i < 32; ++i) v[i] = (ok && i < C::CH) ? __uint_as_float(r[i]) : 0.f;
+          if (ok) {
+            if (BN < 64)
+              epi_small<EPI, C::CH>(args, v, row, col_base + c);
+            else
+              epi_chunk<EPI>(args, v, row, col_base + c);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -390,13 +463,17 @@ __global__ void __launch_bounds__(256, 1)
         const int lrow = sub * 32 + lane;
         float* mine = args.ws + ((size_t)split * args.tiles_m * args.tiles_n + tile_id) * tile_elems + (size_t)lrow * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = 0; c < BN; c += C::CH) {
           uint32_t r[32];
-          tmem_ld32(t_acc + (uint32_t)c, r);
+          if (C::CH == 32) {
+            tmem_ld32(t_acc + (uint32_t)c, r);
+          } else {
+            tmem_ld16(t_acc + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
           tmem_wait_ld();
           float4* dst = reinterpret_cast<float4*>(mine + c);
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
+          for (int q = 0; q < C::CH / 4; ++q)
             dst[q] = ok ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
                                       __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
                         : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -417,7 +494,7 @@ __global__ void __launch_bounds__(256, 1)
           const float* base = args.ws + (size_t)tile_id * tile_elems + (size_t)lrow * BN;
           const size_t sstride = (size_t)args.tiles_m * args.tiles_n * tile_elems;
 #pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
+          for (int c = 0; c < BN; c += C::CH) {
             float v[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.f;
@@ -430,12 +507,12 @@ __global__ void __launch_bounds__(256, 1)
               for (int h = 0; h < 4; ++h) {
                 const float4* src = reinterpret_cast<const float4*>(base + (s + h) * sstride + c);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) p[h][q] = __ldcg(src + q);
+                for (int q = 0; q < C::CH / 4; ++q) p[h][q] = __ldcg(src + q);
               }
 #pragma unroll
               for (int h = 0; h < 4; ++h)
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
+                for (int q = 0; q < C::CH / 4; ++q) {
                   v[4 * q] += p[h][q].x;
                   v[4 * q + 1] += p[h][q].y;
                   v[4 * q + 2] += p[h][q].z;
@@ -446,7 +523,7 @@ __global__ void __launch_bounds__(256, 1)
             for (; s < args.splits; ++s) {
               const float4* src = reinterpret_cast<const float4*>(base + s * sstride + c);
 #pragma unroll
-              for (int q = 0; q < 8; ++q) {
+              for (int q = 0; q < C::CH / 4; ++q) {
                 const float4 p = __ldcg(src + q);
                 v[4 * q] += p.x;
                 v[4 * q + 1] += p.y;
@@ -454,7 +531,10 @@ __global__ void __launch_bounds__(256, 1)
                 v[4 * q + 3] += p.w;
               }
             }
-            epi_chunk<EPI>(args, v, row, col_base + c);
+            if (BN < 64)
+              epi_small<EPI, C::CH>(args, v, row, col_base + c);
+            else
+              epi_chunk<EPI>(args, v, row, col_base + c);
           }
         }
       }

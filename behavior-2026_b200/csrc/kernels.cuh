@@ -73,7 +73,7 @@ __global__ void layernorm_kernel(const bf16* x, bf16* y, const bf16* s, const bf
 //   plain:    scale = per-feature parameter, shift = null, mod_ld = 0
 //   adaptive: scale/shift rows of the modulation table, row (t / rows_per_mod) with stride mod_ld
 __global__ void rmsnorm_kernel(const bf16* x, bf16* y, const bf16* scale, const bf16* shift, int T, int D,
-                               int rows_per_mod, int mod_ld) {
+                               int rows_per_mod, int mod_ld, int ld_y) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   pdl_wait();
   if (warp >= T) return;
@@ -93,7 +93,7 @@ __global__ void rmsnorm_kernel(const bf16* x, bf16* y, const bf16* scale, const 
   }
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float inv = 1.0f / sqrtf(ss / (float)D + 1e-6f);
-  bf16* yr = y + (long)warp * D;
+  bf16* yr = y + (long)warp * ld_y;
   for (int i = lane * 8; i < D; i += 256) {
     const uint4 u = *reinterpret_cast<const uint4*>(xr + i);
     const uint4 us = *reinterpret_cast<const uint4*>(sc + i);
@@ -118,7 +118,7 @@ __global__ void rmsnorm_kernel(const bf16* x, bf16* y, const bf16* scale, const 
 // q <- R(rope(q)) * 1/16 in place; kout[t] <- R(rope(k)); vout[t] <- v.
 // RoPE pairs (i, i+128) of each 256-wide head (openpi gemma._apply_rope).
 __global__ void rope_qkv_kernel(bf16* qkv, int T, int per_sample, int pos_off, bf16* kout, bf16* vout,
-                                const float* cos_t, const float* sin_t) {
+                                const float* cos_t, const float* sin_t, int ld_kv) {
   const int t = blockIdx.x;
   pdl_wait();
   if (t >= T) return;
@@ -138,12 +138,12 @@ __global__ void rope_qkv_kernel(bf16* qkv, int T, int per_sample, int pos_off, b
         v[j] = tobf(a * 0.0625f);
         v[j + 128] = tobf(c * 0.0625f);
       } else {
-        kout[(long)t * 256 + j] = tobf(a);
-        kout[(long)t * 256 + j + 128] = tobf(c);
+        kout[(long)t * ld_kv + j] = tobf(a);
+        kout[(long)t * ld_kv + j + 128] = tobf(c);
       }
     } else {
       const int j = (i - 9 * 128) * 2;
-      *reinterpret_cast<uint32_t*>(vout + (long)t * 256 + j) =
+      *reinterpret_cast<uint32_t*>(vout + (long)t * ld_kv + j) =
           *reinterpret_cast<const uint32_t*>(row + 2304 + j);
     }
   }

@@ -1,0 +1,809 @@
+// train.cuh — LoRA train step of the pi0.5 engine (included by engine.cu; shares its helpers).
+//
+// Replaces the reference's LoraTrainer::accumulate / finalize_grads / opt_step (π05_네이티브엔진.md:215,
+// :226-229).  Per sample: t ~ Beta(1.5,1)*0.999+0.001 (drawn by the caller), x_t = t*eps + (1-t)*a,
+// u = eps - a, v = net(x_t, t, prefix), loss = mean((v-u)^2) (openpi pi0.py:189-214).  Trainable: rank-16
+// LoRA (scale alpha/r = 2) on q/k/v/o/gate/up/down of the Gemma-2B prefix and of the action expert;
+// SigLIP, embeddings, norms and projections are frozen.
+//
+// Every LoRA projection is one tcgen05 GEMM in each direction.  Forward: the input buffer carries
+// 16 extra columns per adapter holding 2*R(x A^T) and the weight carries B^T in the matching columns:
+//   y = [x | 2U] . [W | B]^T = x W^T + 2 (x A^T) B^T.
+// Backward: dx = [dy | 2V] . [W^T | A^T]^T with V = R(dy B) and a transposed copy of the frozen
+// weight; dB = dy^T (2U) and dA = (2V)^T x reduce over tokens and read dy / x MN-major.
+// Activations of every layer are kept (B200 has the memory), so nothing is recomputed.
+#pragma once
+#include "attention_bwd.cuh"
+#include "train_kernels.cuh"
+
+namespace {
+
+struct LoraGroup {
+  int n_ad = 1, K = 0, F = 0, mode = 0;  // adapters sharing the input; input width; base output rows
+  int Fa[3] = {0, 0, 0};                 // output rows per adapter
+  long offA[3] = {0, 0, 0}, offB[3] = {0, 0, 0};
+  bf16 *Wf = nullptr, *Wb = nullptr, *Acat = nullptr, *Btcat = nullptr;
+  int ldf() const { return K + 16 * n_ad; }
+  int ldb() const { return F + 16 * n_ad; }
+};
+struct TrainLayer {
+  LoraGroup qkv, o, gu, dn;
+};
+struct Saved {  // one stack (prefix or suffix), one layer
+  bf16 *xin, *h1, *qkv, *o, *xmid, *h2, *gu, *act;
+  bf16 *uT_qkv, *uT_o, *uT_gu, *uT_dn;
+  float* lse;
+};
+
+}  // namespace
+
+struct Trainer {
+  pi05_lora_config cfg;
+  int mb = 8;
+  int n_total = 0;  // samples in the current optimizer step (loss normalisation)
+  long n_params = 0;
+  float *p = nullptr, *g = nullptr, *m = nullptr, *v = nullptr;
+  float* sumsq = nullptr;
+  int step = 0;
+  std::vector<TrainLayer> gl, el;
+  std::vector<Saved> sp, ss;
+  bf16* xin_p_final = nullptr;  // prefix output of the last layer (unused) is not kept
+  bf16* xin_s_final = nullptr;
+  // per micro-batch
+  float *d_t, *d_eps, *d_act, *d_xt, *d_u, *d_dv, *d_rowloss, *d_loss;
+  float *d_temb, *d_c1, *d_c2;
+  bf16 *d_cond, *mods;
+  bf16 *hf;
+  // backward workspaces
+  float *gx_p, *gx_s, *Dp, *Ds;
+  bf16 *dy_p, *dy_s, *dact_p, *dact_s, *dgu_p, *dgu_s, *dh_p, *dh_s, *do_p, *do_s, *dqkv_p, *dqkv_s, *vT;
+};
+
+namespace {
+
+// ------------------------------------------------------------------ parameter layout
+void lora_group_layout(LoraGroup& G, int n_ad, int K, int F, int mode, const int* Fa, long& off) {
+  G.n_ad = n_ad;
+  G.K = K;
+  G.F = F;
+  G.mode = mode;
+  for (int a = 0; a < n_ad; ++a) {
+    G.Fa[a] = Fa[a];
+    G.offA[a] = off;
+    off += 16L * K;
+    G.offB[a] = off;
+    off += (long)Fa[a] * 16;
+  }
+}
+
+void lora_layout(pi05_engine* e, Trainer* T) {
+  long off = 0;
+  const int L = e->cfg.gemma_layers;
+  T->gl.resize(L);
+  T->el.resize(L);
+  for (int s = 0; s < 2; ++s)
+    for (int l = 0; l < L; ++l) {
+      TrainLayer& t = s == 0 ? T->gl[l] : T->el[l];
+      const int D = s == 0 ? P5_GEM_W : P5_EXP_W, F = s == 0 ? P5_GEM_MLP : P5_EXP_MLP;
+      const int fq[3] = {P5_QDIM, P5_HD, P5_HD}, fo[1] = {D}, fgu[2] = {F, F}, fd[1] = {D};
+      lora_group_layout(t.qkv, 3, D, P5_QKV, 1, fq, off);
+      lora_group_layout(t.o, 1, P5_QDIM, D, 0, fo, off);
+      lora_group_layout(t.gu, 2, D, 2 * F, 2, fgu, off);
+      lora_group_layout(t.dn, 1, F, D, 0, fd, off);
+    }
+  T->n_params = off;
+}
+
+bool talloc(pi05_engine* e, void** p, size_t bytes) { return dalloc(e, p, bytes); }
+// token-major transposes ([16n][R]) are TMA operands: rows padded to 16 bytes
+inline long pad8(long r) { return (r + 7) & ~7L; }
+
+bool alloc_group(pi05_engine* e, LoraGroup& G, const bf16* W) {
+  if (!talloc(e, (void**)&G.Wf, (size_t)G.F * G.ldf() * 2) || !talloc(e, (void**)&G.Wb, (size_t)G.K * G.ldb() * 2) ||
+      !talloc(e, (void**)&G.Acat, (size_t)16 * G.n_ad * G.K * 2) ||
+      !talloc(e, (void**)&G.Btcat, (size_t)16 * G.n_ad * G.F * 2))
+    return false;
+  lora_frozen_copy_kernel<<<148 * 8, 256, 0, e->stream>>>(W, G.F, G.K, G.Wf, G.ldf(), G.Wb, G.ldb());
+  CK(cudaGetLastError());
+  return true;
+}
+
+bool scatter_group(pi05_engine* e, Trainer* T, const LoraGroup& G) {
+  for (int a = 0; a < G.n_ad; ++a) {
+    LoraScatter s;
+    s.A = T->p + G.offA[a];
+    s.B = T->p + G.offB[a];
+    s.K = G.K;
+    s.Fa = G.Fa[a];
+    s.Wf = G.Wf;
+    s.ld_wf = G.ldf();
+    s.colB = G.K + 16 * a;
+    s.row_off = G.mode == 1 ? (a == 0 ? 0 : (a == 1 ? P5_QDIM : P5_QDIM + P5_HD)) : (G.mode == 2 ? a : 0);
+    s.row_step = G.mode == 2 ? 2 : 1;
+    s.Wb = G.Wb;
+    s.ld_wb = G.ldb();
+    s.colA = G.F + 16 * a;
+    s.Acat = G.Acat;
+    s.Btcat = G.Btcat;
+    s.ld_bt = G.F;
+    s.arow = 16 * a;
+    lora_scatter_kernel<<<148 * 4, 256, 0, e->stream>>>(s);
+    CK(cudaGetLastError());
+  }
+  return true;
+}
+
+bool scatter_all(pi05_engine* e, Trainer* T) {
+  for (int s = 0; s < 2; ++s)
+    for (TrainLayer& t : (s == 0 ? T->gl : T->el))
+      if (!scatter_group(e, T, t.qkv) || !scatter_group(e, T, t.o) || !scatter_group(e, T, t.gu) ||
+          !scatter_group(e, T, t.dn))
+        return false;
+  return true;
+}
+
+bool lora_create(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
+  Trainer* T = new Trainer();
+  e->tr = T;
+  T->cfg = *c;
+  T->mb = c->micro_batch;
+  if (T->mb > e->max_batch) return set_err(e, "lora: micro_batch exceeds the engine's max_batch");
+  lora_layout(e, T);
+  const int L = e->cfg.gemma_layers, P = e->P, H = e->cfg.horizon, mb = T->mb;
+  const long np = T->n_params;
+  if (!talloc(e, (void**)&T->p, np * 4) || !talloc(e, (void**)&T->g, np * 4) || !talloc(e, (void**)&T->m, np * 4) ||
+      !talloc(e, (void**)&T->v, np * 4) || !talloc(e, (void**)&T->sumsq, 1024 * 4))
+    return false;
+  lora_init_kernel<<<148 * 8, 256, 0, e->stream>>>(T->p, np, p5_key(seed, K_LORA_GEM_A, 0),
+                                                    p5_scale_for_std(P5_LORA_STD));
+  CK(cudaGetLastError());
+  for (int l = 0; l < L; ++l) {
+    const GemLayer& g = e->gem[l];
+    const ExpLayer& x = e->ex[l];
+    if (!alloc_group(e, T->gl[l].qkv, g.wqkv) || !alloc_group(e, T->gl[l].o, g.wo) ||
+        !alloc_group(e, T->gl[l].gu, g.wgu) || !alloc_group(e, T->gl[l].dn, g.wd) ||
+        !alloc_group(e, T->el[l].qkv, x.wqkv) || !alloc_group(e, T->el[l].o, x.wo) ||
+        !alloc_group(e, T->el[l].gu, x.wgu) || !alloc_group(e, T->el[l].dn, x.wd))
+      return false;
+  }
+  if (!scatter_all(e, T)) return false;
+  // saved activations
+  const long Rp = (long)mb * P, Rs = (long)mb * H;
+  T->sp.resize(L);
+  T->ss.resize(L);
+  for (int s = 0; s < 2; ++s)
+    for (int l = 0; l < L; ++l) {
+      Saved& S = s == 0 ? T->sp[l] : T->ss[l];
+      const long R = s == 0 ? Rp : Rs;
+      const int D = s == 0 ? P5_GEM_W : P5_EXP_W, F = s == 0 ? P5_GEM_MLP : P5_EXP_MLP;
+      if (!talloc(e, (void**)&S.xin, R * D * 2) || !talloc(e, (void**)&S.h1, R * (D + 48) * 2) ||
+          !talloc(e, (void**)&S.qkv, R * P5_QKV * 2) || !talloc(e, (void**)&S.o, R * (P5_QDIM + 16) * 2) ||
+          !talloc(e, (void**)&S.xmid, R * D * 2) || !talloc(e, (void**)&S.h2, R * (D + 32) * 2) ||
+          !talloc(e, (void**)&S.gu, R * 2 * F * 2) || !talloc(e, (void**)&S.act, R * (F + 16) * 2) ||
+          !talloc(e, (void**)&S.uT_qkv, 48 * pad8(R) * 2) || !talloc(e, (void**)&S.uT_o, 16 * pad8(R) * 2) ||
+          !talloc(e, (void**)&S.uT_gu, 32 * pad8(R) * 2) || !talloc(e, (void**)&S.uT_dn, 16 * pad8(R) * 2) ||
+          !talloc(e, (void**)&S.lse, R * P5_NH * 4))
+        return false;
+    }
+  if (!talloc(e, (void**)&T->xin_p_final, Rp * P5_GEM_W * 2) || !talloc(e, (void**)&T->xin_s_final, Rs * P5_EXP_W * 2))
+    return false;
+  const size_t actb = (size_t)Rs * P5_ACT_D * 4;
+  if (!talloc(e, (void**)&T->d_t, 1024 * 4) || !talloc(e, (void**)&T->d_eps, actb) ||
+      !talloc(e, (void**)&T->d_act, actb) || !talloc(e, (void**)&T->d_xt, actb) || !talloc(e, (void**)&T->d_u, actb) ||
+      !talloc(e, (void**)&T->d_dv, actb) || !talloc(e, (void**)&T->d_rowloss, Rs * 4) ||
+      !talloc(e, (void**)&T->d_loss, 64) || !talloc(e, (void**)&T->d_temb, (size_t)mb * P5_EXP_W * 4) ||
+      !talloc(e, (void**)&T->d_c1, (size_t)mb * P5_EXP_W * 4) || !talloc(e, (void**)&T->d_c2, (size_t)mb * P5_EXP_W * 4) ||
+      !talloc(e, (void**)&T->d_cond, (size_t)mb * P5_EXP_W * 2) ||
+      !talloc(e, (void**)&T->mods, (size_t)mb * e->NM * 3 * P5_EXP_W * 2) ||
+      !talloc(e, (void**)&T->hf, Rs * P5_EXP_W * 2))
+    return false;
+  // backward workspaces
+  if (!talloc(e, (void**)&T->gx_p, Rp * P5_GEM_W * 4) || !talloc(e, (void**)&T->gx_s, Rs * P5_EXP_W * 4) ||
+      !talloc(e, (void**)&T->Dp, Rp * P5_NH * 4) || !talloc(e, (void**)&T->Ds, Rs * P5_NH * 4) ||
+      !talloc(e, (void**)&T->dy_p, Rp * (P5_GEM_W + 16) * 2) || !talloc(e, (void**)&T->dy_s, Rs * (P5_EXP_W + 16) * 2) ||
+      !talloc(e, (void**)&T->dact_p, Rp * P5_GEM_MLP * 2) || !talloc(e, (void**)&T->dact_s, Rs * P5_EXP_MLP * 2) ||
+      !talloc(e, (void**)&T->dgu_p, Rp * (2 * P5_GEM_MLP + 32) * 2) ||
+      !talloc(e, (void**)&T->dgu_s, Rs * (2 * P5_EXP_MLP + 32) * 2) || !talloc(e, (void**)&T->dh_p, Rp * P5_GEM_W * 2) ||
+      !talloc(e, (void**)&T->dh_s, Rs * P5_EXP_W * 2) || !talloc(e, (void**)&T->do_p, Rp * P5_QDIM * 2) ||
+      !talloc(e, (void**)&T->do_s, Rs * P5_QDIM * 2) || !talloc(e, (void**)&T->dqkv_p, Rp * (P5_QKV + 48) * 2) ||
+      !talloc(e, (void**)&T->dqkv_s, Rs * (P5_QKV + 48) * 2) || !talloc(e, (void**)&T->vT, 48 * pad8(std::max(Rp, Rs)) * 2))
+    return false;
+  CK(cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DQ));
+  CK(cudaFuncSetAttribute(attn_bwd_dkv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DKV));
+  CK(cudaFuncSetAttribute(attn_bwd_dkv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DKV));
+  CK(cudaStreamSynchronize(e->stream));
+  return true;
+}
+
+// ------------------------------------------------------------------ GEMM helpers of the LoRA path
+// U = R(x A^T) * 2 into the extra columns of the input buffer, and its transpose [16n][R]
+bool lora_u(pi05_engine* e, const LoraGroup& G, bf16* xcat, int R, bf16* uT) {
+  Lin L{xcat, G.ldf(), R, G.Acat, G.K, 16 * G.n_ad, G.K};
+  L.epi = EPI_STORE_T;
+  L.no_swap = true;
+  L.out = xcat + G.K;
+  L.ld_out = G.ldf();
+  L.out_scale = 2.0f;
+  L.out_t = uT;
+  L.ld_out_t = (int)pad8(R);
+  return linear(e, L);
+}
+// V = R(dy B) * 2 into the extra columns of the gradient buffer, and its transpose
+bool lora_v(pi05_engine* e, const LoraGroup& G, bf16* dycat, int R, bf16* vT) {
+  Lin L{dycat, G.ldb(), R, G.Btcat, G.F, 16 * G.n_ad, G.F};
+  L.epi = EPI_STORE_T;
+  L.no_swap = true;
+  L.out = dycat + G.F;
+  L.ld_out = G.ldb();
+  L.out_scale = 2.0f;
+  L.out_t = vT;
+  L.ld_out_t = (int)pad8(R);
+  return linear(e, L);
+}
+// dB_a += dy^T (2U) over the adapter's rows; dA_a += (2V)^T x
+bool lora_wgrad(pi05_engine* e, Trainer* T, const LoraGroup& G, const bf16* dycat, const bf16* xcat, const bf16* uT,
+                const bf16* vT, int R) {
+  Lin b{dycat, G.ldb(), G.F, uT, (int)pad8(R), 16 * G.n_ad, R};
+  b.amn = true;
+  b.epi = EPI_LORA_GRAD;
+  b.out_f32 = T->g;
+  b.lg_mode = G.mode;
+  b.lg_trans = 0;
+  for (int a = 0; a < 3; ++a) b.lg_off[a] = G.offB[a];
+  if (!linear(e, b)) return false;
+  Lin a{xcat, G.ldf(), G.K, vT, (int)pad8(R), 16 * G.n_ad, R};
+  a.amn = true;
+  a.epi = EPI_LORA_GRAD;
+  a.out_f32 = T->g;
+  a.lg_trans = 1;
+  a.lg_K = G.K;
+  for (int i = 0; i < 3; ++i) a.lg_off[i] = G.offA[i];
+  return linear(e, a);
+}
+// dx = [dy | 2V] . [W^T | A^T]^T
+bool lora_dx(pi05_engine* e, const LoraGroup& G, const bf16* dycat, int R, bf16* dx) {
+  Lin L{dycat, G.ldb(), R, G.Wb, G.ldb(), G.K, G.ldb()};
+  L.no_swap = true;
+  L.out = dx;
+  L.ld_out = G.K;
+  return linear(e, L);
+}
+
+bool rms(pi05_engine* e, const bf16* x, bf16* y, int ld_y, const bf16* scale, const bf16* shift, int R, int D,
+         int rows_per_mod, int mod_ld) {
+  return launch(e, rmsnorm_kernel, dim3(rows_grid(R)), dim3(256), 0, false, x, y, scale, shift, R, D, rows_per_mod,
+                mod_ld, ld_y);
+}
+bool rms_bwd(pi05_engine* e, const bf16* x, const bf16* dy, int ld_dy, const bf16* scale, int rows_per_mod,
+             int mod_ld, float* gx, int R, int D) {
+  return launch(e, rmsnorm_bwd_kernel, dim3(rows_grid(R)), dim3(256), 0, false, x, dy, ld_dy, scale, rows_per_mod,
+                mod_ld, gx, R, D);
+}
+
+// ------------------------------------------------------------------ forward of one stack-layer
+struct StackCtx {
+  bool prefix;
+  int R, per_sample, pos_off, D, F;
+  const bf16* mrow1;  // adaptive norm rows (suffix) or plain scale (prefix)
+  const bf16* mrow2;
+  int mod_ld;
+};
+
+bool fwd_qkv(pi05_engine* e, const LoraGroup& G, const StackCtx& c, Saved& S) {
+  if (!rms(e, S.xin, S.h1, c.D + 48, c.mrow1, c.prefix ? nullptr : c.mrow1 + c.D, c.R, c.D, c.per_sample, c.mod_ld))
+    return false;
+  if (!lora_u(e, G, S.h1, c.R, S.uT_qkv)) return false;
+  Lin q{S.h1, G.ldf(), c.R, G.Wf, G.ldf(), P5_QKV, G.ldf()};
+  q.no_swap = true;
+  q.out = S.qkv;
+  q.ld_out = P5_QKV;
+  if (!linear(e, q)) return false;
+  return launch(e, rope_qkv_kernel, dim3(c.R), dim3(256), 0, false, S.qkv, c.R, c.per_sample, c.pos_off,
+                S.qkv + P5_QDIM, S.qkv + P5_QDIM + P5_HD, (const float*)e->d_cos, (const float*)e->d_sin, P5_QKV);
+}
+
+bool fwd_after_attn(pi05_engine* e, const TrainLayer& t, const StackCtx& c, Saved& S, bf16* xout, const bf16* gate1,
+                    const bf16* gate2, int nb) {
+  if (!lora_u(e, t.o, S.o, c.R, S.uT_o)) return false;
+  Lin o{S.o, t.o.ldf(), c.R, t.o.Wf, t.o.ldf(), c.D, t.o.ldf()};
+  o.no_swap = true;
+  o.out = S.xmid;
+  o.ld_out = c.D;
+  o.res = S.xin;
+  o.ld_res = c.D;
+  if (c.prefix) {
+    o.epi = EPI_RESID;
+  } else {
+    o.epi = EPI_GATED;
+    o.gate = gate1;
+    o.ld_gate = c.mod_ld;
+    o.gate_div = c.per_sample;
+  }
+  if (!linear(e, o)) return false;
+  if (!rms(e, S.xmid, S.h2, c.D + 32, c.mrow2, c.prefix ? nullptr : c.mrow2 + c.D, c.R, c.D, c.per_sample, c.mod_ld))
+    return false;
+  if (!lora_u(e, t.gu, S.h2, c.R, S.uT_gu)) return false;
+  Lin gu{S.h2, t.gu.ldf(), c.R, t.gu.Wf, t.gu.ldf(), 2 * c.F, t.gu.ldf()};
+  gu.no_swap = true;
+  gu.epi = EPI_GEGLU;
+  gu.out = S.act;
+  gu.ld_out = c.F + 16;
+  gu.out_t = S.gu;
+  gu.ld_out_t = 2 * c.F;
+  if (!linear(e, gu)) return false;
+  if (!lora_u(e, t.dn, S.act, c.R, S.uT_dn)) return false;
+  Lin dn{S.act, t.dn.ldf(), c.R, t.dn.Wf, t.dn.ldf(), c.D, t.dn.ldf()};
+  dn.no_swap = true;
+  dn.out = xout;
+  dn.ld_out = c.D;
+  dn.res = S.xmid;
+  dn.ld_res = c.D;
+  if (c.prefix) {
+    dn.epi = EPI_RESID;
+  } else {
+    dn.epi = EPI_GATED;
+    dn.gate = gate2;
+    dn.ld_gate = c.mod_ld;
+    dn.gate_div = c.per_sample;
+  }
+  (void)nb;
+  return linear(e, dn);
+}
+
+// ------------------------------------------------------------------ one micro-batch: forward + backward
+bool micro_step(pi05_engine* e, int nb, const float* h_t) {
+  Trainer* T = e->tr;
+  const int L = e->cfg.gemma_layers, P = e->P, H = e->cfg.horizon, NM = e->NM;
+  const int Rp = nb * P, Rs = nb * H, MW = NM * 3 * P5_EXP_W;
+  Acts& A = e->A;
+  // prefix embeddings (frozen SigLIP + text) into layer 0's input
+  if (!run_siglip(e, nb)) return false;
+  if (e->cfg.n_text > 0 &&
+      !launch(e, embed_text_kernel, dim3(e->cfg.n_text, nb), dim3(256), 0, false, (const int32_t*)A.tokens,
+              (const bf16*)e->embed, A.px, e->cfg.n_text, P, e->cfg.n_cameras * P5_SIG_TOK))
+    return false;
+  CK(cudaMemcpyAsync(T->sp[0].xin, A.px, (size_t)Rp * P5_GEM_W * 2, cudaMemcpyDeviceToDevice, e->stream));
+  // time conditioning per sample
+  {
+    std::vector<float> emb((size_t)nb * P5_EXP_W);
+    for (int b = 0; b < nb; ++b) p5_time_embedding(h_t[b], P5_EXP_W, emb.data() + (size_t)b * P5_EXP_W);
+    CK(cudaMemcpyAsync(T->d_temb, emb.data(), emb.size() * 4, cudaMemcpyHostToDevice, e->stream));
+    CK(cudaStreamSynchronize(e->stream));  // emb lives on the host stack
+    const int warps = nb * P5_EXP_W;
+    linear_swish_f32_kernel<<<(warps * 32 + 255) / 256, 256, 0, e->stream>>>(T->d_temb, e->tin_w, e->tin_b, T->d_c1,
+                                                                            (bf16*)nullptr, nb, P5_EXP_W);
+    linear_swish_f32_kernel<<<(warps * 32 + 255) / 256, 256, 0, e->stream>>>(T->d_c1, e->tout_w, e->tout_b, T->d_c2,
+                                                                            T->d_cond, nb, P5_EXP_W);
+    CK(cudaGetLastError());
+    Lin m{T->d_cond, P5_EXP_W, nb, e->ada_w, P5_EXP_W, MW, P5_EXP_W};
+    m.out = T->mods;
+    m.ld_out = MW;
+    m.bias = e->ada_b;
+    if (!linear(e, m)) return false;
+  }
+  // suffix input
+  {
+    const long n = (long)Rs * P5_ACT_D;
+    flow_inputs_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(T->d_eps, T->d_act, T->d_t, T->d_xt, T->d_u, H, nb);
+    if (!launch(e, action_in_kernel, dim3((Rs * P5_EXP_W + 255) / 256), dim3(256), 0, false, (const float*)T->d_xt,
+                (const bf16*)e->ain_w, (const bf16*)e->ain_b, T->ss[0].xin, Rs, P5_EXP_W))
+      return false;
+  }
+  // ---------------- forward
+  for (int l = 0; l < L; ++l) {
+    Saved& Sp = T->sp[l];
+    Saved& Ss = T->ss[l];
+    const bool last = l == L - 1;
+    StackCtx cp{true, Rp, P, 0, P5_GEM_W, P5_GEM_MLP, e->gem[l].rms1, e->gem[l].rms2, 0};
+    StackCtx cs{false, Rs, H, P, P5_EXP_W, P5_EXP_MLP, T->mods + (size_t)(2 * l) * 3 * P5_EXP_W,
+                T->mods + (size_t)(2 * l + 1) * 3 * P5_EXP_W, MW};
+    if (!fwd_qkv(e, T->gl[l].qkv, cp, Sp) || !fwd_qkv(e, T->el[l].qkv, cs, Ss)) return false;
+    AttnArgs at = {};
+    at.G = P5_NH;
+    at.qdiv = 1.0f;
+    at.splits = 1;
+    if (!last) {  // prefix rows attend the prefix
+      at.q = Sp.qkv;
+      at.ldq = P5_QKV;
+      at.q_bstride = (long)P * P5_QKV;
+      at.out = Sp.o;
+      at.ldo = P5_QDIM + 16;
+      at.o_bstride = (long)P * (P5_QDIM + 16);
+      at.k1 = Sp.qkv + P5_QDIM;
+      at.v1 = Sp.qkv + P5_QDIM + P5_HD;
+      at.ld1 = P5_QKV;
+      at.len1 = P;
+      at.b1stride = (long)P * P5_QKV;
+      at.k2 = at.k1;
+      at.v2 = at.v1;
+      at.T = P;
+      at.lse = Sp.lse;
+      at.lse_b = (long)P * P5_NH;
+      if (!attention(e, at, nb, P5_HD)) return false;
+    }
+    // suffix rows attend [prefix || suffix]
+    at.q = Ss.qkv;
+    at.ldq = P5_QKV;
+    at.q_bstride = (long)H * P5_QKV;
+    at.out = Ss.o;
+    at.ldo = P5_QDIM + 16;
+    at.o_bstride = (long)H * (P5_QDIM + 16);
+    at.k1 = Sp.qkv + P5_QDIM;
+    at.v1 = Sp.qkv + P5_QDIM + P5_HD;
+    at.ld1 = P5_QKV;
+    at.len1 = P;
+    at.b1stride = (long)P * P5_QKV;
+    at.k2 = Ss.qkv + P5_QDIM;
+    at.v2 = Ss.qkv + P5_QDIM + P5_HD;
+    at.ld2 = P5_QKV;
+    at.len2 = H;
+    at.b2stride = (long)H * P5_QKV;
+    at.T = H;
+    at.lse = Ss.lse;
+    at.lse_b = (long)H * P5_NH;
+    if (!attention(e, at, nb, P5_HD)) return false;
+    bf16* xo_p = last ? T->xin_p_final : T->sp[l + 1].xin;
+    bf16* xo_s = last ? T->xin_s_final : T->ss[l + 1].xin;
+    if (!last && !fwd_after_attn(e, T->gl[l], cp, Sp, xo_p, nullptr, nullptr, nb)) return false;
+    if (!fwd_after_attn(e, T->el[l], cs, Ss, xo_s, cs.mrow1 + 2 * P5_EXP_W, cs.mrow2 + 2 * P5_EXP_W, nb)) return false;
+  }
+  // final adaRMS, v, loss
+  const bf16* mf = T->mods + (size_t)(NM - 1) * 3 * P5_EXP_W;
+  if (!rms(e, T->xin_s_final, T->hf, P5_EXP_W, mf, mf + P5_EXP_W, Rs, P5_EXP_W, H, MW)) return false;
+  const float inv_count = 1.0f / ((float)T->n_total * H * P5_ACT_D);
+  out_proj_loss_kernel<<<Rs, 1024, 0, e->stream>>>(T->hf, e->aout_w, e->aout_b, T->d_u, T->d_dv, T->d_rowloss, Rs,
+                                                   P5_EXP_W, inv_count);
+  sum_rows_kernel<<<1, 256, 0, e->stream>>>(T->d_rowloss, Rs, inv_count, T->d_loss);
+  // ---------------- backward
+  out_proj_bwd_kernel<<<(Rs * P5_EXP_W + 255) / 256, 256, 0, e->stream>>>(T->d_dv, e->aout_w, T->dh_s, Rs, P5_EXP_W);
+  CK(cudaMemsetAsync(T->gx_s, 0, (size_t)Rs * P5_EXP_W * 4, e->stream));
+  CK(cudaMemsetAsync(T->gx_p, 0, (size_t)Rp * P5_GEM_W * 4, e->stream));
+  if (!rms_bwd(e, T->xin_s_final, T->dh_s, P5_EXP_W, mf, H, MW, T->gx_s, Rs, P5_EXP_W)) return false;
+  for (int l = L - 1; l >= 0; --l) {
+    Saved& Sp = T->sp[l];
+    Saved& Ss = T->ss[l];
+    const TrainLayer& tp = T->gl[l];
+    const TrainLayer& ts = T->el[l];
+    const bool last = l == L - 1;
+    const bf16* m1 = T->mods + (size_t)(2 * l) * 3 * P5_EXP_W;
+    const bf16* m2 = T->mods + (size_t)(2 * l + 1) * 3 * P5_EXP_W;
+    // stack-generic MLP + O backward
+    auto mlp_o_bwd = [&](bool prefix) -> bool {
+      const int R = prefix ? Rp : Rs, D = prefix ? P5_GEM_W : P5_EXP_W, F = prefix ? P5_GEM_MLP : P5_EXP_MLP;
+      const TrainLayer& t = prefix ? tp : ts;
+      Saved& S = prefix ? Sp : Ss;
+      float* gx = prefix ? T->gx_p : T->gx_s;
+      bf16* dy = prefix ? T->dy_p : T->dy_s;
+      bf16* dact = prefix ? T->dact_p : T->dact_s;
+      bf16* dgu = prefix ? T->dgu_p : T->dgu_s;
+      bf16* dh = prefix ? T->dh_p : T->dh_s;
+      bf16* dO = prefix ? T->do_p : T->do_s;
+      const int rpg = prefix ? 1 : H, gld = prefix ? 0 : MW;
+      // down projection (gated for the suffix)
+      const long n = (long)R * D;
+      if (!launch(e, grad_to_bf16_kernel, dim3((n + 255) / 256), dim3(256), 0, false, (const float*)gx, dy, D + 16,
+                  prefix ? (const bf16*)nullptr : m2 + 2 * D, rpg, gld, R, D))
+        return false;
+      if (!lora_v(e, t.dn, dy, R, T->vT) || !lora_wgrad(e, T, t.dn, dy, S.act, S.uT_dn, T->vT, R)) return false;
+      Lin da{dy, t.dn.ldb(), R, t.dn.Wb, t.dn.ldb(), F, t.dn.ldb()};
+      da.no_swap = true;
+      da.out = dact;
+      da.ld_out = F;
+      if (!linear(e, da)) return false;
+      const long ng = (long)R * F;
+      if (!launch(e, geglu_bwd_kernel, dim3((ng + 255) / 256), dim3(256), 0, false, (const bf16*)S.gu,
+                  (const bf16*)dact, F, dgu, 2 * F + 32, R, F))
+        return false;
+      if (!lora_v(e, t.gu, dgu, R, T->vT) || !lora_wgrad(e, T, t.gu, dgu, S.h2, S.uT_gu, T->vT, R)) return false;
+      if (!lora_dx(e, t.gu, dgu, R, dh)) return false;
+      if (!rms_bwd(e, S.xmid, dh, D, prefix ? e->gem[l].rms2 : m2, rpg, gld, gx, R, D)) return false;
+      // output projection
+      if (!launch(e, grad_to_bf16_kernel, dim3((n + 255) / 256), dim3(256), 0, false, (const float*)gx, dy, D + 16,
+                  prefix ? (const bf16*)nullptr : m1 + 2 * D, rpg, gld, R, D))
+        return false;
+      if (!lora_v(e, t.o, dy, R, T->vT) || !lora_wgrad(e, T, t.o, dy, S.o, S.uT_o, T->vT, R)) return false;
+      Lin dov{dy, t.o.ldb(), R, t.o.Wb, t.o.ldb(), P5_QDIM, t.o.ldb()};
+      dov.no_swap = true;
+      dov.out = dO;
+      dov.ld_out = P5_QDIM;
+      return linear(e, dov);
+    };
+    if (!mlp_o_bwd(false)) return false;
+    if (!last && !mlp_o_bwd(true)) return false;
+    // attention backward
+    if (!launch(e, attn_dot_kernel, dim3(rows_grid((long)Rs * P5_NH)), dim3(256), 0, false, (const bf16*)T->do_s,
+                P5_QDIM, (const bf16*)Ss.o, P5_QDIM + 16, T->Ds, Rs))
+      return false;
+    if (!last && !launch(e, attn_dot_kernel, dim3(rows_grid((long)Rp * P5_NH)), dim3(256), 0, false,
+                         (const bf16*)T->do_p, P5_QDIM, (const bf16*)Sp.o, P5_QDIM + 16, T->Dp, Rp))
+      return false;
+    QSeg qs_s{Ss.qkv, P5_QKV, (long)H * P5_QKV, T->do_s, P5_QDIM, (long)H * P5_QDIM, Ss.lse, T->Ds, (long)H * P5_NH, H};
+    QSeg qs_p{Sp.qkv, P5_QKV, (long)P * P5_QKV, T->do_p, P5_QDIM, (long)P * P5_QDIM, Sp.lse, T->Dp, (long)P * P5_NH, P};
+    AttnBwdArgs ab = {};
+    ab.k1 = Sp.qkv + P5_QDIM;
+    ab.v1 = Sp.qkv + P5_QDIM + P5_HD;
+    ab.ld1 = P5_QKV;
+    ab.len1 = P;
+    ab.b1stride = (long)P * P5_QKV;
+    ab.k2 = Ss.qkv + P5_QDIM;
+    ab.v2 = Ss.qkv + P5_QDIM + P5_HD;
+    ab.ld2 = P5_QKV;
+    ab.len2 = H;
+    ab.b2stride = (long)H * P5_QKV;
+    // dq of the action queries (keys: prefix || suffix)
+    ab.qs = qs_s;
+    ab.dq = T->dqkv_s;
+    ab.ld_dq = P5_QKV + 48;
+    ab.dq_b = (long)H * (P5_QKV + 48);
+    if (!launch(e, attn_bwd_dq_kernel, dim3((Rs / nb * P5_NH + 63) / 64, 1, nb), dim3(128), (size_t)ABW_SMEM_DQ, false,
+                ab))
+      return false;
+    if (!last) {  // dq of the prefix queries (keys: prefix only)
+      AttnBwdArgs ap = ab;
+      ap.len2 = 0;
+      ap.qs = qs_p;
+      ap.dq = T->dqkv_p;
+      ap.dq_b = (long)P * (P5_QKV + 48);
+      if (!launch(e, attn_bwd_dq_kernel, dim3((P * P5_NH + 63) / 64, 1, nb), dim3(128), (size_t)ABW_SMEM_DQ, false,
+                  ap))
+        return false;
+    } else {
+      CK(cudaMemset2DAsync(T->dqkv_p, (size_t)(P5_QKV + 48) * 2, 0, (size_t)P5_QDIM * 2, Rp, e->stream));
+    }
+    // dK, dV of the prefix keys: prefix queries (unless last) then action queries
+    AttnBwdArgs ak = ab;
+    ak.kseg = 1;
+    ak.nq = last ? 1 : 2;
+    ak.qa = last ? qs_s : qs_p;
+    ak.qbseg = qs_s;
+    ak.ld_dkv = P5_QKV + 48;
+    ak.dkv_b = (long)P * (P5_QKV + 48);
+    ak.dk = T->dqkv_p + P5_QDIM;
+    ak.dv = T->dqkv_p + P5_QDIM + P5_HD;
+    const dim3 gk((P + 63) / 64, 1, nb);
+    if (!launch(e, attn_bwd_dkv_kernel<true>, gk, dim3(128), (size_t)ABW_SMEM_DKV, false, ak) ||
+        !launch(e, attn_bwd_dkv_kernel<false>, gk, dim3(128), (size_t)ABW_SMEM_DKV, false, ak))
+      return false;
+    // dK, dV of the suffix keys: action queries only
+    AttnBwdArgs as = ab;
+    as.kseg = 2;
+    as.nq = 1;
+    as.qa = qs_s;
+    as.ld_dkv = P5_QKV + 48;
+    as.dkv_b = (long)H * (P5_QKV + 48);
+    as.dk = T->dqkv_s + P5_QDIM;
+    as.dv = T->dqkv_s + P5_QDIM + P5_HD;
+    const dim3 gs((H + 63) / 64, 1, nb);
+    if (!launch(e, attn_bwd_dkv_kernel<true>, gs, dim3(128), (size_t)ABW_SMEM_DKV, false, as) ||
+        !launch(e, attn_bwd_dkv_kernel<false>, gs, dim3(128), (size_t)ABW_SMEM_DKV, false, as))
+      return false;
+    // RoPE backward, then the q/k/v projections of both stacks
+    if (!launch(e, rope_bwd_kernel, dim3(Rs), dim3(256), 0, false, T->dqkv_s, P5_QKV + 48, Rs, H, P,
+                (const float*)e->d_cos, (const float*)e->d_sin, 1) ||
+        !launch(e, rope_bwd_kernel, dim3(Rp), dim3(256), 0, false, T->dqkv_p, P5_QKV + 48, Rp, P, 0,
+                (const float*)e->d_cos, (const float*)e->d_sin, last ? 0 : 1))
+      return false;
+    auto qkv_bwd = [&](bool prefix) -> bool {
+      const int R = prefix ? Rp : Rs, D = prefix ? P5_GEM_W : P5_EXP_W;
+      const LoraGroup& G = prefix ? tp.qkv : ts.qkv;
+      Saved& S = prefix ? Sp : Ss;
+      bf16* dq = prefix ? T->dqkv_p : T->dqkv_s;
+      bf16* dh = prefix ? T->dh_p : T->dh_s;
+      if (!lora_v(e, G, dq, R, T->vT) || !lora_wgrad(e, T, G, dq, S.h1, S.uT_qkv, T->vT, R)) return false;
+      if (!lora_dx(e, G, dq, R, dh)) return false;
+      return rms_bwd(e, S.xin, dh, D, prefix ? e->gem[l].rms1 : m1, prefix ? 1 : H, prefix ? 0 : MW,
+                     prefix ? T->gx_p : T->gx_s, R, D);
+    };
+    if (!qkv_bwd(false) || !qkv_bwd(true)) return false;
+  }
+  return true;
+}
+
+bool lora_accumulate(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* actions,
+                     const float* noise, const float* t) {
+  Trainer* T = e->tr;
+  const int H = e->cfg.horizon;
+  const size_t ib = (size_t)e->cfg.n_cameras * P5_IMG * P5_IMG * 3;
+  T->n_total = n;
+  for (int b0 = 0; b0 < n; b0 += T->mb) {
+    const int nb = std::min(T->mb, n - b0);
+    CK(cudaMemcpyAsync(e->A.images, images + b0 * ib, nb * ib, cudaMemcpyDefault, e->stream));
+    if (e->cfg.n_text > 0)
+      CK(cudaMemcpyAsync(e->A.tokens, tokens + (size_t)b0 * e->cfg.n_text, (size_t)nb * e->cfg.n_text * 4,
+                         cudaMemcpyDefault, e->stream));
+    const size_t ab = (size_t)H * P5_ACT_D * 4;
+    CK(cudaMemcpyAsync(T->d_act, actions + (size_t)b0 * H * P5_ACT_D, nb * ab, cudaMemcpyDefault, e->stream));
+    CK(cudaMemcpyAsync(T->d_eps, noise + (size_t)b0 * H * P5_ACT_D, nb * ab, cudaMemcpyDefault, e->stream));
+    std::vector<float> th(nb);
+    CK(cudaMemcpy(th.data(), t + b0, nb * 4, cudaMemcpyDefault));
+    CK(cudaMemcpyAsync(T->d_t, th.data(), nb * 4, cudaMemcpyHostToDevice, e->stream));
+    if (!micro_step(e, nb, th.data())) return false;
+  }
+  return true;
+}
+
+bool lora_opt(pi05_engine* e) {
+  Trainer* T = e->tr;
+  const int nb = 256;
+  sumsq_partial_kernel<<<nb, 256, 0, e->stream>>>(T->g, T->n_params, T->sumsq);
+  T->step += 1;
+  adamw_kernel<<<148 * 8, 256, 0, e->stream>>>(T->p, T->g, T->m, T->v, T->n_params, T->sumsq, nb, T->cfg.clip_norm,
+                                               T->cfg.lr, T->cfg.beta1, T->cfg.beta2, T->cfg.eps, T->cfg.weight_decay,
+                                               T->step);
+  CK(cudaGetLastError());
+  return scatter_all(e, T);
+}
+
+}  // namespace
+
+// ===================================================================== C ABI (LoRA)
+extern "C" {
+
+void pi05_lora_default_config(pi05_lora_config* c) {
+  if (!c) return;
+  c->rank = 16;
+  c->alpha = 32.0f;
+  c->lr = 1e-4f;
+  c->beta1 = 0.9f;
+  c->beta2 = 0.95f;
+  c->eps = 1e-8f;
+  c->weight_decay = 1e-10f;
+  c->clip_norm = 1.0f;
+  c->micro_batch = 8;
+}
+
+int pi05_lora_init(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
+  if (!e || !e->weights_ready) return PI05_ERR_STATE;
+  pi05_lora_config cfg;
+  pi05_lora_default_config(&cfg);
+  if (c) cfg = *c;
+  if (cfg.rank != 16 || cfg.alpha != 32.0f || cfg.micro_batch < 1) {
+    e->err = "pi05_lora_init: this build implements rank 16, alpha 32";
+    return PI05_ERR_ARG;
+  }
+  if (e->tr) {
+    e->err = "pi05_lora_init: already initialised";
+    return PI05_ERR_STATE;
+  }
+  cudaSetDevice(e->device);
+  if (!lora_create(e, &cfg, seed)) return fail_code(e);
+  return PI05_OK;
+}
+
+long pi05_lora_num_params(pi05_engine* e) { return (e && e->tr) ? e->tr->n_params : -1; }
+
+int pi05_lora_zero_grads(pi05_engine* e) {
+  if (!e || !e->tr) return PI05_ERR_STATE;
+  cudaSetDevice(e->device);
+  if (cudaMemsetAsync(e->tr->g, 0, e->tr->n_params * 4, e->stream) != cudaSuccess ||
+      cudaMemsetAsync(e->tr->d_loss, 0, 4, e->stream) != cudaSuccess)
+    return PI05_ERR_CUDA;
+  return PI05_OK;
+}
+
+int pi05_lora_accumulate(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* actions,
+                         const float* noise, const float* t, float* loss) {
+  if (!e || !e->tr) return PI05_ERR_STATE;
+  if (n < 1 || !images || !actions || !noise || !t || (e->cfg.n_text > 0 && !tokens)) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  if (!lora_accumulate(e, n, images, tokens, actions, noise, t)) return fail_code(e);
+  if (loss) {
+    if (cudaMemcpyAsync(loss, e->tr->d_loss, 4, cudaMemcpyDefault, e->stream) != cudaSuccess) return PI05_ERR_CUDA;
+    return pi05_sync(e);
+  }
+  return PI05_OK;
+}
+
+int pi05_lora_opt_step(pi05_engine* e) {
+  if (!e || !e->tr) return PI05_ERR_STATE;
+  cudaSetDevice(e->device);
+  if (!lora_opt(e)) return fail_code(e);
+  return PI05_OK;
+}
+
+int pi05_lora_step(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* actions,
+                   const float* noise, const float* t, float* loss) {
+  int rc = pi05_lora_zero_grads(e);
+  if (rc != PI05_OK) return rc;
+  rc = pi05_lora_accumulate(e, n, images, tokens, actions, noise, t, nullptr);
+  if (rc != PI05_OK) return rc;
+  rc = pi05_lora_opt_step(e);
+  if (rc != PI05_OK) return rc;
+  if (loss) {
+    if (cudaMemcpyAsync(loss, e->tr->d_loss, 4, cudaMemcpyDefault, e->stream) != cudaSuccess) return PI05_ERR_CUDA;
+    return pi05_sync(e);
+  }
+  return PI05_OK;
+}
+
+static int lora_copy(pi05_engine* e, float* dst, const float* src) {
+  if (!e || !e->tr || !dst) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  if (cudaMemcpyAsync(dst, src, e->tr->n_params * 4, cudaMemcpyDefault, e->stream) != cudaSuccess) return PI05_ERR_CUDA;
+  return pi05_sync(e);
+}
+int pi05_lora_get_params(pi05_engine* e, float* out) { return e && e->tr ? lora_copy(e, out, e->tr->p) : PI05_ERR_STATE; }
+int pi05_lora_get_grads(pi05_engine* e, float* out) { return e && e->tr ? lora_copy(e, out, e->tr->g) : PI05_ERR_STATE; }
+int pi05_lora_set_params(pi05_engine* e, const float* in) {
+  if (!e || !e->tr || !in) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  if (cudaMemcpyAsync(e->tr->p, in, e->tr->n_params * 4, cudaMemcpyDefault, e->stream) != cudaSuccess)
+    return PI05_ERR_CUDA;
+  if (!scatter_all(e, e->tr)) return fail_code(e);
+  return pi05_sync(e);
+}
+void* pi05_lora_grad_buffer(pi05_engine* e) { return e && e->tr ? (void*)e->tr->g : nullptr; }
+
+int pi05_lora_reset_optimizer(pi05_engine* e) {
+  if (!e || !e->tr) return PI05_ERR_STATE;
+  cudaSetDevice(e->device);
+  Trainer* T = e->tr;
+  if (cudaMemsetAsync(T->m, 0, T->n_params * 4, e->stream) != cudaSuccess ||
+      cudaMemsetAsync(T->v, 0, T->n_params * 4, e->stream) != cudaSuccess)
+    return PI05_ERR_CUDA;
+  T->step = 0;
+  return pi05_sync(e);
+}
+
+// Train state file: "pi05lora 1\nparams N\nstep S\n" padded to 256 bytes, then p, m, v (fp32, N each).
+int pi05_lora_save_state(pi05_engine* e, const char* path) {
+  if (!e || !e->tr || !path) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  Trainer* T = e->tr;
+  std::vector<float> buf((size_t)T->n_params);
+  FILE* f = fopen(path, "wb");
+  if (!f) {
+    e->err = std::string("cannot open ") + path;
+    return PI05_ERR_ARG;
+  }
+  char hdr[256] = {0};
+  snprintf(hdr, sizeof(hdr), "pi05lora 1\nparams %ld\nstep %d\n", T->n_params, T->step);
+  fwrite(hdr, 1, sizeof(hdr), f);
+  for (float* src : {T->p, T->m, T->v}) {
+    if (cudaMemcpy(buf.data(), src, T->n_params * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+      fclose(f);
+      return PI05_ERR_CUDA;
+    }
+    fwrite(buf.data(), 4, buf.size(), f);
+  }
+  fclose(f);
+  return PI05_OK;
+}
+
+int pi05_lora_load_state(pi05_engine* e, const char* path) {
+  if (!e || !e->tr || !path) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  Trainer* T = e->tr;
+  FILE* f = fopen(path, "rb");
+  if (!f) {
+    e->err = std::string("cannot open ") + path;
+    return PI05_ERR_ARG;
+  }
+  char hdr[256];
+  long np = -1;
+  int step = -1;
+  if (fread(hdr, 1, sizeof(hdr), f) != sizeof(hdr) || sscanf(hdr, "pi05lora 1\nparams %ld\nstep %d", &np, &step) != 2 ||
+      np != T->n_params) {
+    fclose(f);
+    e->err = "pi05_lora_load_state: not a train state of this configuration";
+    return PI05_ERR_ARG;
+  }
+  std::vector<float> buf((size_t)np);
+  for (float* dst : {T->p, T->m, T->v}) {
+    if (fread(buf.data(), 4, buf.size(), f) != buf.size()) {
+      fclose(f);
+      e->err = "pi05_lora_load_state: short file";
+      return PI05_ERR_ARG;
+    }
+    if (cudaMemcpy(dst, buf.data(), np * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+      fclose(f);
+      return PI05_ERR_CUDA;
+    }
+  }
+  fclose(f);
+  T->step = step;
+  if (!scatter_all(e, T)) return fail_code(e);
+  return pi05_sync(e);
+}
+
+}  // extern "C"

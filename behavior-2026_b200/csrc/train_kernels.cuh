@@ -1,0 +1,272 @@
+// train_kernels.cuh — kernels of the LoRA train step (backward pass, loss, optimizer).
+//
+// The step follows the openpi training loss the reference engine ported (π05_네이티브엔진.md:206-229,
+// openpi models/pi0.py:189-214): x_t = t*noise + (1-t)*actions, u = noise - actions, v = net(x_t, t, prefix),
+// loss = mean((v-u)^2); trainable parameters are rank-16 LoRA adapters on q/k/v/o/gate/up/down of the
+// Gemma-2B prefix and the action expert; everything else is frozen.  Gradients flow in fp32 where they
+// are reduced and in bf16 where they feed a tensor-core GEMM.
+#pragma once
+#include "attention.cuh"
+#include "common.cuh"
+
+namespace p5 {
+
+__device__ __forceinline__ float gelu_tanh_grad(float x) {
+  const float c = 0.7978845608028654f, a = 0.044715f;
+  const float inner = c * (x + a * x * x * x);
+  const float th = tanhf(inner);
+  return 0.5f * (1.0f + th) + 0.5f * x * (1.0f - th * th) * c * (1.0f + 3.0f * a * x * x);
+}
+
+// ---------------------------------------------------------------- loss
+// x_t = t*eps + (1-t)*a ; u = eps - a   (per sample t), fp32
+__global__ void flow_inputs_kernel(const float* eps, const float* act, const float* t, float* xt, float* u, int H,
+                                   int n) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)n * H * P5_ACT_D) return;
+  const int b = (int)(i / ((long)H * P5_ACT_D));
+  const float tb = t[b];
+  xt[i] = tb * eps[i] + (1.0f - tb) * act[i];
+  u[i] = eps[i] - act[i];
+}
+
+// v = R(h . Wout^T + b) (bf16 Linear), per-row squared error sum, dv = 2 (v - u) / count
+__global__ void out_proj_loss_kernel(const bf16* h, const bf16* W, const bf16* b, const float* u, float* dv,
+                                     float* row_loss, int T, int D, float inv_count) {
+  const int t = blockIdx.x;
+  const int j = threadIdx.x >> 5, lane = threadIdx.x & 31;  // 32 warps = 32 action dims
+  if (t >= T) return;
+  const bf16* hr = h + (long)t * D;
+  const bf16* wr = W + (long)j * D;
+  float acc = 0.f;
+  for (int k = lane * 8; k < D; k += 256) {
+    float a8[8], w8[8];
+    const uint4 ua = *reinterpret_cast<const uint4*>(hr + k), uw = *reinterpret_cast<const uint4*>(wr + k);
+    const uint32_t aa[4] = {ua.x, ua.y, ua.z, ua.w}, ww[4] = {uw.x, uw.y, uw.z, uw.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf2(aa[q]), g = unpack_bf2(ww[q]);
+      a8[2 * q] = f.x; a8[2 * q + 1] = f.y; w8[2 * q] = g.x; w8[2 * q + 1] = g.y;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc += a8[q] * w8[q];
+  }
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ float sq[32];
+  if (lane == 0) {
+    const float v = rbf(acc + bf(b[j]));
+    const float e = v - u[(long)t * P5_ACT_D + j];
+    dv[(long)t * P5_ACT_D + j] = 2.0f * e * inv_count;
+    sq[j] = e * e;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int i = 0; i < 32; ++i) s += sq[i];
+    row_loss[t] = s;
+  }
+}
+
+// deterministic sum of per-row losses (one block)
+__global__ void sum_rows_kernel(const float* rows, int n, float scale, float* out) {
+  __shared__ float part[256];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += 256) s += rows[i];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w; w >>= 1) {
+    if (threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *out += part[0] * scale;
+}
+
+// dh[t][k] = sum_j dv[t][j] Wout[j][k]  (action_out_proj backward, frozen weight)
+__global__ void out_proj_bwd_kernel(const float* dv, const bf16* W, bf16* dh, int T, int D) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)T * D) return;
+  const int t = (int)(i / D), k = (int)(i % D);
+  float acc = 0.f;
+#pragma unroll 8
+  for (int j = 0; j < P5_ACT_D; ++j) acc += dv[(long)t * P5_ACT_D + j] * bf(W[(long)j * D + k]);
+  dh[i] = tobf(acc);
+}
+
+// ---------------------------------------------------------------- norm backward (one warp per row)
+// y = n*w + shift with n = x*rstd, w = R(1+scale) (plain: scale per feature; adaptive: per-sample row
+// of the modulation table).  dx (+)= rstd * (dn - n * mean(dn*n)), dn = dy*w.
+__global__ void rmsnorm_bwd_kernel(const bf16* x, const bf16* dy, int ld_dy, const bf16* scale, int rows_per_mod,
+                                   int mod_ld, float* dx_acc, int T, int D) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const bf16* xr = x + (long)warp * D;
+  const bf16* dr = dy + (long)warp * ld_dy;
+  const bf16* sc = scale + (mod_ld ? (long)(warp / rows_per_mod) * mod_ld : 0);
+  float ss = 0.f;
+  for (int i = lane; i < D; i += 32) {
+    const float v = bf(xr[i]);
+    ss += v * v;
+  }
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rstd = 1.0f / sqrtf(ss / (float)D + 1e-6f);
+  float dot = 0.f;
+  for (int i = lane; i < D; i += 32) dot += bf(dr[i]) * rbf(1.0f + bf(sc[i])) * bf(xr[i]) * rstd;
+  for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  const float m = dot / (float)D;
+  float* out = dx_acc + (long)warp * D;
+  for (int i = lane; i < D; i += 32) {
+    const float n = bf(xr[i]) * rstd;
+    const float dn = bf(dr[i]) * rbf(1.0f + bf(sc[i]));
+    out[i] += rstd * (dn - n * m);
+  }
+}
+
+// fp32 residual-stream gradient -> bf16 (optionally times the per-sample gate: gated residual backward)
+__global__ void grad_to_bf16_kernel(const float* g, bf16* out, int ld_out, const bf16* gate, int rows_per_gate,
+                                    int gate_ld, int T, int D) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)T * D) return;
+  const int t = (int)(i / D), k = (int)(i % D);
+  float v = g[i];
+  if (gate) v *= bf(gate[(long)(t / rows_per_gate) * gate_ld + k]);
+  out[(long)t * ld_out + k] = tobf(v);
+}
+
+// GeGLU backward: gu interleaved [T][2F] (gate 2j, up 2j+1), dact [T][F] (ld) -> dgu [T][2F] (ld)
+__global__ void geglu_bwd_kernel(const bf16* gu, const bf16* dact, int ld_dact, bf16* dgu, int ld_dgu, int T,
+                                 int F) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)T * F) return;
+  const int t = (int)(i / F), j = (int)(i % F);
+  const float2 p = unpack_bf2(*reinterpret_cast<const uint32_t*>(gu + (long)t * 2 * F + 2 * j));
+  const float g = p.x, u = p.y;
+  const float da = bf(dact[(long)t * ld_dact + j]);
+  const float dg = da * u * gelu_tanh_grad(g);
+  const float du = da * rbf(gelu_tanh(g));
+  *reinterpret_cast<uint32_t*>(dgu + (long)t * ld_dgu + 2 * j) = pack_bf2(dg, du);
+}
+
+// RoPE backward on the attention gradients in dqkv (ld): q part was R(rope(q))*1/16, k part R(rope(k)).
+// The inverse rotation of the pair (i, i+128) by angle a is rotation by -a.
+__global__ void rope_bwd_kernel(bf16* dqkv, int ld, int T, int per_sample, int pos_off, const float* cos_t,
+                                const float* sin_t, int do_q) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const int pos = pos_off + t % per_sample;
+  const float* cs = cos_t + (long)pos * 128;
+  const float* sn = sin_t + (long)pos * 128;
+  bf16* row = dqkv + (long)t * ld;
+  for (int i = threadIdx.x; i < 9 * 128; i += blockDim.x) {
+    const int h = i / 128, j = i % 128;
+    if (h < 8 && !do_q) continue;
+    bf16* v = row + h * 256;
+    const float sc = h < 8 ? 0.0625f : 1.0f;
+    const float a = bf(v[j]) * sc, c = bf(v[j + 128]) * sc;
+    v[j] = tobf(a * cs[j] + c * sn[j]);
+    v[j + 128] = tobf(c * cs[j] - a * sn[j]);
+  }
+}
+
+// D[row] = sum_d dO[row][d] * O[row][d] for the folded MQA rows (token t, head h)
+__global__ void attn_dot_kernel(const bf16* dO, int ld_do, const bf16* O, int ld_o, float* D, int T) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T * P5_NH) return;
+  const int t = warp / P5_NH, h = warp % P5_NH;
+  const bf16* a = dO + (long)t * ld_do + h * P5_HD;
+  const bf16* b = O + (long)t * ld_o + h * P5_HD;
+  float s = 0.f;
+  for (int d = lane; d < P5_HD; d += 32) s += bf(a[d]) * bf(b[d]);
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) D[warp] = s;
+}
+
+// ---------------------------------------------------------------- LoRA parameter plumbing
+// Scatter fp32 adapters into the bf16 operands of the GEMMs (after init and every optimizer step).
+struct LoraScatter {
+  const float* A;  // [16][K]
+  const float* B;  // [Fa][16]
+  int K, Fa;
+  // forward weight: Wf[row(f)][colB + j] = B[f][j]; backward weight Wb[k][colA + j] = A[j][k]
+  bf16* Wf;
+  int ld_wf, colB, row_off, row_step;
+  bf16* Wb;
+  int ld_wb, colA;
+  bf16* Acat;  // rows [16a, 16a+16) = A : [16n][K]
+  bf16* Btcat;  // Btcat[16a + j][row(f)] = B[f][j] : [16n][F]
+  int ld_bt, arow;
+};
+__global__ void lora_scatter_kernel(LoraScatter s) {
+  const long nA = 16L * s.K, nB = (long)s.Fa * 16;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nA + nB; i += (long)gridDim.x * blockDim.x) {
+    if (i < nA) {
+      const int j = (int)(i / s.K), k = (int)(i % s.K);
+      const bf16 v = tobf(s.A[i]);
+      s.Wb[(long)k * s.ld_wb + s.colA + j] = v;
+      s.Acat[(long)(s.arow + j) * s.K + k] = v;
+    } else {
+      const long q = i - nA;
+      const int f = (int)(q / 16), j = (int)(q % 16);
+      const bf16 v = tobf(s.B[q]);
+      const long row = (long)s.row_off + (long)f * s.row_step;
+      s.Wf[row * s.ld_wf + s.colB + j] = v;
+      s.Btcat[(long)(s.arow + j) * s.ld_bt + row] = v;
+    }
+  }
+}
+
+// copy a frozen [F][K] weight into the forward [F][K+extra] and the transposed backward [K][F+extra] buffers
+__global__ void lora_frozen_copy_kernel(const bf16* W, int F, int K, bf16* Wf, int ld_wf, bf16* Wb, int ld_wb) {
+  const long n = (long)F * K;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const int f = (int)(i / K), k = (int)(i % K);
+    const bf16 v = W[i];
+    Wf[(long)f * ld_wf + k] = v;
+    Wb[(long)k * ld_wb + f] = v;
+  }
+}
+
+// ---------------------------------------------------------------- optimizer
+// sum of squares of the gradient, deterministic two-level reduction
+__global__ void sumsq_partial_kernel(const float* g, long n, float* partial) {
+  __shared__ float part[256];
+  float s = 0.f;
+  for (long i = (long)blockIdx.x * 256 + threadIdx.x; i < n; i += (long)gridDim.x * 256) s += g[i] * g[i];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w; w >>= 1) {
+    if (threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) partial[blockIdx.x] = part[0];
+}
+
+// AdamW (optax order: clip_by_global_norm -> adam moments -> bias correction -> + wd * p -> * -lr)
+__global__ void adamw_kernel(float* p, const float* g, float* m, float* v, long n, const float* sumsq_partial,
+                             int n_partial, float clip, float lr, float b1, float b2, float eps, float wd, int step) {
+  __shared__ float scale_s;
+  if (threadIdx.x == 0) {
+    float ss = 0.f;
+    for (int i = 0; i < n_partial; ++i) ss += sumsq_partial[i];
+    const float norm = sqrtf(ss);
+    scale_s = (clip > 0.f && norm > clip) ? clip / norm : 1.0f;
+  }
+  __syncthreads();
+  const float sc = scale_s;
+  const float c1 = 1.0f - powf(b1, (float)step), c2 = 1.0f - powf(b2, (float)step);
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float gi = g[i] * sc;
+    const float mi = b1 * m[i] + (1.0f - b1) * gi;
+    const float vi = b2 * v[i] + (1.0f - b2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    const float upd = (mi / c1) / (sqrtf(vi / c2) + eps) + wd * p[i];
+    p[i] -= lr * upd;
+  }
+}
+
+__global__ void lora_init_kernel(float* p, long n, uint64_t seed, float scale) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    p[i] = p5_bf2f(p5_f2bf(p5_normal(seed, (uint64_t)i, scale)));
+}
+
+}  // namespace p5

@@ -49,6 +49,12 @@ class Config(ctypes.Structure):
         return {n: getattr(self, n) for n, _ in self._fields_}
 
 
+class LoraConfig(ctypes.Structure):
+    _fields_ = [("rank", ctypes.c_int32), ("alpha", ctypes.c_float), ("lr", ctypes.c_float), ("beta1", ctypes.c_float),
+                ("beta2", ctypes.c_float), ("eps", ctypes.c_float), ("weight_decay", ctypes.c_float),
+                ("clip_norm", ctypes.c_float), ("micro_batch", ctypes.c_int32)]
+
+
 def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(f"{LIB_PATH} is missing; build it with behavior-2026_b200/build.py")
@@ -90,6 +96,23 @@ def _load():
     L.pi05_op_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp]
     L.pi05_op_attention.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32]
     L.pi05_linear_static.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_char_p, ctypes.c_size_t]
+    L.pi05_lora_default_config.argtypes = [P(LoraConfig)]
+    L.pi05_lora_default_config.restype = None
+    L.pi05_lora_init.argtypes = [vp, P(LoraConfig), u64]
+    L.pi05_lora_num_params.argtypes = [vp]
+    L.pi05_lora_num_params.restype = ctypes.c_long
+    L.pi05_lora_zero_grads.argtypes = [vp]
+    L.pi05_lora_accumulate.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp]
+    L.pi05_lora_opt_step.argtypes = [vp]
+    L.pi05_lora_step.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp]
+    L.pi05_lora_get_params.argtypes = [vp, vp]
+    L.pi05_lora_set_params.argtypes = [vp, vp]
+    L.pi05_lora_get_grads.argtypes = [vp, vp]
+    L.pi05_lora_grad_buffer.argtypes = [vp]
+    L.pi05_lora_grad_buffer.restype = vp
+    L.pi05_lora_reset_optimizer.argtypes = [vp]
+    L.pi05_lora_save_state.argtypes = [vp, ctypes.c_char_p]
+    L.pi05_lora_load_state.argtypes = [vp, ctypes.c_char_p]
     return L
 
 
@@ -224,6 +247,70 @@ class Engine:
         S = k.shape[1]
         p = lambda t: ctypes.c_void_p(t.data_ptr())
         self._check(lib.pi05_op_attention(self._h, b, T, S, p(q), ldq, p(k), p(v), p(out), splits))
+
+    # -- LoRA fine-tuning (reference: LoraTrainer::accumulate / finalize_grads / opt_step)
+    def lora_init(self, seed=0, micro_batch=8, **kw):
+        c = LoraConfig()
+        lib.pi05_lora_default_config(ctypes.byref(c))
+        c.micro_batch = micro_batch
+        for k, v in kw.items():
+            setattr(c, k, v)
+        self._check(lib.pi05_lora_init(self._h, ctypes.byref(c), seed))
+        self.lora_config = c
+
+    @property
+    def lora_num_params(self):
+        return lib.pi05_lora_num_params(self._h)
+
+    def lora_zero_grads(self):
+        self._check(lib.pi05_lora_zero_grads(self._h))
+
+    def _lora_args(self, images, tokens, actions, noise, t):
+        keep = [_ptr(images, np.uint8), _ptr(tokens, np.int32), _ptr(actions, np.float32), _ptr(noise, np.float32),
+                _ptr(t, np.float32)]
+        return [k[0] for k in keep], keep
+
+    def lora_accumulate(self, images, tokens, actions, noise, t):
+        """forward + backward; adds to the gradient buffer; returns the running mean loss"""
+        ptrs, keep = self._lora_args(images, tokens, actions, noise, t)
+        loss = ctypes.c_float(0)
+        self._check(lib.pi05_lora_accumulate(self._h, images.shape[0], *ptrs, ctypes.byref(loss)))
+        return loss.value
+
+    def lora_opt_step(self):
+        self._check(lib.pi05_lora_opt_step(self._h))
+
+    def lora_step(self, images, tokens, actions, noise, t, want_loss=True):
+        ptrs, keep = self._lora_args(images, tokens, actions, noise, t)
+        loss = ctypes.c_float(0)
+        self._check(lib.pi05_lora_step(self._h, images.shape[0], *ptrs, ctypes.byref(loss) if want_loss else None))
+        return loss.value
+
+    def lora_get_params(self):
+        out = np.empty(self.lora_num_params, np.float32)
+        self._check(lib.pi05_lora_get_params(self._h, out.ctypes.data))
+        return out
+
+    def lora_set_params(self, p):
+        p = np.ascontiguousarray(p, np.float32)
+        self._check(lib.pi05_lora_set_params(self._h, p.ctypes.data))
+
+    def lora_get_grads(self):
+        out = np.empty(self.lora_num_params, np.float32)
+        self._check(lib.pi05_lora_get_grads(self._h, out.ctypes.data))
+        return out
+
+    def lora_grad_ptr(self):
+        return lib.pi05_lora_grad_buffer(self._h)
+
+    def lora_reset_optimizer(self):
+        self._check(lib.pi05_lora_reset_optimizer(self._h))
+
+    def lora_save_state(self, path):
+        self._check(lib.pi05_lora_save_state(self._h, path.encode()))
+
+    def lora_load_state(self, path):
+        self._check(lib.pi05_lora_load_state(self._h, path.encode()))
 
     # -- reference-named extras
     def info(self):

@@ -99,6 +99,49 @@ PI05_API void pi05_synth_noise(uint64_t seed, int sample, int horizon, float* ou
 /* Expert-only workload: N(0,1) bf16 prefix cache for samples [0, n) generated on the device. */
 PI05_API int pi05_synth_prefix_cache(pi05_engine* e, int n, uint64_t seed);
 
+/* ---- LoRA fine-tuning (replaces LoraTrainer::accumulate / finalize_grads / opt_step, π05_네이티브엔진.md:215) ----
+ * Rank-16, alpha-32 adapters on q/k/v/o/gate/up/down of the Gemma-2B prefix and of the action expert;
+ * base weights frozen.  Loss: flow-matching MSE on the velocity (openpi pi0.py:189-214) with
+ * x_t = t*noise + (1-t)*actions, u = noise - actions; the caller draws t (Beta(1.5,1)*0.999+0.001)
+ * and the noise.  Optimizer: global-norm clip, AdamW.  Adapter parameters and gradients are one flat
+ * fp32 buffer (per stack, per layer, per projection: A [16][in] then B [out][16]). */
+typedef struct {
+  int32_t rank;        /* 16 */
+  float alpha;         /* 32 */
+  float lr;            /* 1e-4 */
+  float beta1, beta2;  /* 0.9, 0.95 */
+  float eps;           /* 1e-8 */
+  float weight_decay;  /* 1e-10 */
+  float clip_norm;     /* 1.0 (global norm) */
+  int32_t micro_batch; /* samples per forward/backward pass; activations of all layers are kept */
+} pi05_lora_config;
+PI05_API void pi05_lora_default_config(pi05_lora_config* c);
+/* Adapters initialised N(0, 0.01) from `seed`; needs weights loaded and max_batch >= micro_batch. */
+PI05_API int pi05_lora_init(pi05_engine* e, const pi05_lora_config* c, uint64_t seed);
+PI05_API long pi05_lora_num_params(pi05_engine* e);
+PI05_API int pi05_lora_zero_grads(pi05_engine* e);
+/* forward + backward over n samples, gradients added to the flat buffer (LoraTrainer::accumulate);
+ * images u8 [n][cams][224][224][3], tokens i32 [n][n_text], actions/noise f32 [n][horizon][32], t f32 [n];
+ * *loss (optional) = mean squared velocity error over the samples accumulated since the last zero. */
+PI05_API int pi05_lora_accumulate(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens,
+                                  const float* actions, const float* noise, const float* t, float* loss);
+/* global-norm clip + AdamW on the accumulated gradients (finalize_grads + opt_step).  For data
+ * parallelism allreduce-average pi05_lora_grad_buffer across ranks between accumulate and this call. */
+PI05_API int pi05_lora_opt_step(pi05_engine* e);
+/* zero_grads + accumulate + opt_step */
+PI05_API int pi05_lora_step(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* actions,
+                            const float* noise, const float* t, float* loss);
+PI05_API int pi05_lora_get_params(pi05_engine* e, float* out);
+PI05_API int pi05_lora_set_params(pi05_engine* e, const float* in);
+PI05_API int pi05_lora_get_grads(pi05_engine* e, float* out);
+PI05_API void* pi05_lora_grad_buffer(pi05_engine* e); /* device pointer to the fp32 gradients */
+/* zero the AdamW moments and the step count */
+PI05_API int pi05_lora_reset_optimizer(pi05_engine* e);
+/* checkpoint / resume of the train state: adapters, AdamW moments and step (fp32 flat buffers;
+ * the reference saved params, EMA, Adam m/v and step, π05_네이티브엔진.md:281-282) */
+PI05_API int pi05_lora_save_state(pi05_engine* e, const char* path);
+PI05_API int pi05_lora_load_state(pi05_engine* e, const char* path);
+
 /* Hot operators on caller-owned device buffers, run on the engine stream (unit tests and the operator
  * sweep).  pi05_op_linear: out[T][F'] = epilogue(x[T][K] . w[F][K]^T) with bf16 x, w, out and
  *   epi 0 store, 1 gelu, 2 residual (res[T][F]), 3 gated residual (res, gate[F]), 4 GeGLU

@@ -59,6 +59,7 @@ def lib():
                                            ctypes.c_void_p]
         L.p5o_denoise.argtypes = [cfg, ctypes.c_uint64, f32, f32, ctypes.c_int, f32, f32, ctypes.c_int, PROBE,
                                   ctypes.c_void_p]
+        L.p5o_prefix_embed.argtypes = [cfg, ctypes.c_uint64, u8, i32, f32, ctypes.c_int]
         L.p5o_gen_images.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, u8]
         L.p5o_gen_tokens.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, i32]
         L.p5o_gen_normal.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_double,
@@ -148,6 +149,17 @@ def prefill(cfg, seed, images, tokens, flags=0, probe=None):
                            _p(k, ctypes.c_float), _p(v, ctypes.c_float), flags, *_probe_args(probe))
     assert rc == 0
     return k, v
+
+
+def prefix_embed(cfg, seed, images, tokens, flags=0):
+    """SigLIP image tokens + scaled text embeddings, [P][2048] (bf16-valued floats)."""
+    out = np.empty((cfg.prefix_len, GEM_W), np.float32)
+    images = np.ascontiguousarray(images, np.uint8)
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    rc = lib().p5o_prefix_embed(ctypes.byref(cfg), seed, _p(images, ctypes.c_uint8), _p(tokens, ctypes.c_int32),
+                                _p(out, ctypes.c_float), flags)
+    assert rc == 0
+    return out
 
 
 def prefill_embedded(cfg, seed, emb, flags=0, probe=None):

@@ -485,6 +485,15 @@ int p5o_prefill_embedded(const p5o_config* c, uint64_t seed, const float* prefix
   return 0;
 }
 
+int p5o_prefix_embed(const p5o_config* c, uint64_t seed, const uint8_t* images, const int32_t* tokens, float* out,
+                     int flags) {
+  if (!check(c)) return -1;
+  Run r{flags, nullptr, nullptr};
+  siglip(c, seed, images, out, r);
+  embed_text(c, seed, tokens, out + (size_t)P5_SIG_TOK * c->n_cameras * P5_GEM_W, r);
+  return 0;
+}
+
 int p5o_prefill(const p5o_config* c, uint64_t seed, const uint8_t* images, const int32_t* tokens, float* kcache,
                 float* vcache, int flags, p5o_probe_fn probe, void* ctx) {
   if (!check(c)) return -1;

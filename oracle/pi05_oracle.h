@@ -46,6 +46,9 @@ int p5o_siglip(const p5o_config* c, uint64_t seed, const uint8_t* images, float*
 /* full prefix: kcache/vcache [gemma_layers][P][256], P = 256*n_cameras + n_text */
 int p5o_prefill(const p5o_config* c, uint64_t seed, const uint8_t* images, const int32_t* tokens,
                 float* kcache, float* vcache, int flags, p5o_probe_fn probe, void* ctx);
+/* prefix embeddings [P][2048]: SigLIP image tokens followed by the scaled text embeddings */
+int p5o_prefix_embed(const p5o_config* c, uint64_t seed, const uint8_t* images, const int32_t* tokens, float* out,
+                     int flags);
 /* prefix given as embeddings [P][2048] (skips SigLIP and the text gather) */
 int p5o_prefill_embedded(const p5o_config* c, uint64_t seed, const float* prefix_emb, int P,
                          float* kcache, float* vcache, int flags, p5o_probe_fn probe, void* ctx);
