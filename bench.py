@@ -186,6 +186,21 @@ def run_reference(args, world, rank):
         return 0
     steps = min(args.steps, 5)  # one full-depth chunk per step (tens of seconds each)
     warm = 1 if args.warmup > 0 else 0
+    if args.workload == "lora":
+        steps = min(args.steps, 2)
+        ts, cores = [], 1
+        for _ in range(steps):
+            t, cores = cpu_lora_sample_seconds()
+            ts.append(t)
+        v = 1.0 / statistics.median(ts)
+        line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "samples/s", "n_gpus": args.gpus,
+                "steps": steps, "steps_requested": args.steps, "warmup": 0, "ms_per_step": statistics.median(ts) * 1e3,
+                "higher_is_better": True, "dtype": "f32", "data": "synthetic", "config": config_for(args, world),
+                "cpu_baseline": {"value": v, "unit": "samples/s", "cores": cores, "kind": "port",
+                                 "sample": "one full-depth sample per step: fp32 torch-CPU loss + autograd"},
+                "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
     if args.workload == "denoise":
         fn, unit = cpu_denoise_seconds, "ms"
     else:
@@ -215,6 +230,9 @@ def run_reference(args, world, rank):
 
 
 def config_for(args, world):
+    if args.workload == "lora":
+        return {"workload": f"LoRA step: {args.lora_batch} samples per GPU", "model": MODEL,
+                "global_batch": args.lora_batch * world, "parallelism": f"dp{world}"}
     if args.workload == "bs64":
         return {"workload": f"batched pi0.5 inference: {args.batch} independent environments "
                             f"({args.batch // world} per GPU), 3x224^2 images + 200 tokens -> 50x32 chunk, 10 steps",
@@ -419,6 +437,125 @@ def run_sweep(args, local):
     return 0
 
 
+# ---------------------------------------------------------------- LoRA train step (config 4)
+LORA_TFLOP_PER_SAMPLE = None  # filled by lora_flops_per_sample()
+
+
+def lora_flops_per_sample(P=968, H=50, L=18):
+    """Algorithmic FLOPs of one sample of the LoRA step: SigLIP forward, Gemma/expert forward, the
+    dX backward through the frozen linears (no frozen dW), attention forward + backward (the backward
+    recomputes S in each of its three kernels: 8 matmuls), LoRA projections and gradients."""
+    gem = 2048 * 2560 + 2048 * 2048 + 2048 * 32768 + 16384 * 2048
+    exp = 1024 * 2560 + 2048 * 1024 + 1024 * 8192 + 4096 * 1024
+    sig_lin = 27 * (1152 * 3456 + 1152 * 1152 + 2 * 1152 * 4304) * 768 * 2 + 768 * (588 * 1152 + 1152 * 2048) * 2
+    sig_att = 27 * 3 * 4 * 256 * 256 * 1152
+    gem_fwd = 2 * P * (gem * (L - 1) + 2048 * 2560)
+    exp_fwd = 2 * H * exp * L
+    att = (L - 1) * 4 * P * P * 256 * 8 + L * 4 * H * (P + H) * 256 * 8
+    lora_cols = 16 * 2 * (L * (3 * 2048 + 2048 + 2 * 2048 + 16384) * P + L * (3 * 1024 + 2048 + 2 * 1024 + 4096) * H)
+    return sig_lin + sig_att + 2 * (gem_fwd + exp_fwd) + att * (1 + 4) + 3 * lora_cols
+
+
+def lora_inputs(pn, nb, first, seed):
+    import numpy as np
+    imgs = np.stack([pn.synth_images(seed, first + i) for i in range(nb)])
+    toks = np.stack([pn.synth_tokens(seed, first + i) for i in range(nb)])
+    acts = np.stack([pn.synth_noise(seed + 101, first + i) for i in range(nb)])
+    noise = np.stack([pn.synth_noise(seed + 202, first + i) for i in range(nb)])
+    rng = np.random.default_rng(seed * 7919 + first)
+    t = (rng.beta(1.5, 1.0, nb) * 0.999 + 0.001).astype(np.float32)
+    return imgs, toks, acts, noise, t
+
+
+def cpu_lora_sample_seconds():
+    """fp32 torch-CPU autograd of the full-depth loss for one sample (the oracle of the LoRA step)"""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    import lora_ref
+    import pi05native as pn
+    O.build()
+    cfg = O.Config.make()
+    imgs, toks, acts, noise, t = lora_inputs(pn, 1, 0, 0)
+    n = sum(a * b for _, (a, b) in lora_ref.lora_layout(cfg.gemma_layers))
+    p0 = O.gen_normal(5, 80, 0, (n,), 0.01, True)
+    import torch
+    t0 = time.perf_counter()
+    emb = O.prefix_embed(cfg, 0, imgs[0], toks[0])[None]  # frozen SigLIP forward: part of the work
+    t1 = time.perf_counter()
+    ref = lora_ref.LoraRef(cfg, 0, p0)  # generating the frozen weights is set-up, not work
+    t2 = time.perf_counter()
+    ref.loss(emb, acts, noise, t).backward()
+    t3 = time.perf_counter()
+    return (t1 - t0) + (t3 - t2), torch.get_num_threads()
+
+
+def run_lora(args, world, rank, local):
+    import numpy as np
+    import torch
+    import dp
+    import pi05native as pn
+
+    hbm, tf_burst, tf_sus, peak_src = peaks()
+    nb = args.lora_batch
+    eng = pn.Engine(pn.Config.make(), device=local, max_batch=args.micro_batch)
+    eng.init_random_weights(args.seed)
+    eng.lora_init(seed=args.seed + 1, micro_batch=args.micro_batch)
+    first, _ = dp.shard(nb * world, world, rank)
+    imgs, toks, acts, noise, t = lora_inputs(pn, nb, first, args.seed)
+    dev = [torch.from_numpy(a).cuda() for a in (imgs, toks, acts, noise, t)]
+    host = [torch.from_numpy(a).pin_memory() for a in (imgs, toks, acts, noise, t)]
+
+    def step(bufs):
+        eng.lora_zero_grads()
+        loss = eng.lora_accumulate(*bufs)
+        dp.lora_allreduce(eng, world)
+        eng.lora_opt_step()
+        return loss
+
+    for _ in range(args.warmup):
+        step(dev)
+    eng.sync()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        total_ms, per = timed(eng, lambda: step(dev), args.steps)
+    barrier(world)
+    total_ms = max_over_ranks(total_ms, world)
+    total_e2e, _ = timed(eng, lambda: step(host), args.steps)
+    barrier(world)
+    total_e2e = max_over_ranks(total_e2e, world)
+    loss = step(dev)
+    assert np.isfinite(loss)
+    samples = nb * world
+    fl = lora_flops_per_sample() * nb
+    ach = fl / (total_ms / args.steps / 1e3) / 1e12
+    line = {"metric": METRIC, "value": samples * args.steps / (total_ms / 1e3), "unit": "samples/s",
+            "higher_is_better": True, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "lora_steps_per_s": args.steps / (total_ms / 1e3),
+            "scaling": "weak", "dtype": "bf16", "data": "synthetic", "vs_baseline": None, "loss": loss,
+            "config": {"workload": f"LoRA step (rank 16, alpha 32, q/k/v/o/gate/up/down of Gemma-2B and the expert): "
+                                   f"{nb} samples per GPU, micro-batch {args.micro_batch}, flow-matching loss, "
+                                   f"AdamW lr 1e-4" + (", NCCL gradient allreduce" if world > 1 else ""),
+                       "model": MODEL, "global_batch": samples, "per_gpu_batch": nb, "parallelism": f"dp{world}",
+                       "l2": "no flush: every step streams GBs of weights and saved activations (> 126 MB L2)"},
+            "e2e": {"value": samples * args.steps / (total_e2e / 1e3), "unit": "samples/s",
+                    "h2d_bytes_per_step": sum(a.nbytes for a in (imgs, toks, acts, noise, t)), "d2h_bytes_per_step": 4},
+            "roofline": {"kernel": "whole LoRA step (tcgen05 GEMMs + attention fwd/bwd)", "bound": "tensor",
+                         "achieved": ach, "peak": tf_sus, "unit": "TFLOP/s", "frac": ach / tf_sus,
+                         "peak_source": f"{peak_src} bf16 sustained", "algorithmic_flops_per_step": fl,
+                         "traffic": None},
+            "clocks": clk.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ts, th = cpu_lora_sample_seconds()
+        line["cpu_baseline"] = {"value": 1.0 / ts, "unit": "samples/s", "cores": th, "kind": "port",
+                                "sample": "one full-depth sample: fp32 torch-CPU forward + autograd backward of the loss"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+    return 0
+
+
 def run_gemm(args, local):
     """One linear layer M x N x K (`--gemm M,N,K`, epilogue `--epi`), timed with CUDA events: the small,
     self-contained case the kernel profiles are captured on."""
@@ -441,7 +578,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="bs64", choices=["bs64", "bs1", "denoise", "sweep", "gemm"])
+    ap.add_argument("--workload", default="bs64", choices=["bs64", "bs1", "denoise", "sweep", "gemm", "lora"])
+    ap.add_argument("--lora-batch", type=int, default=32, help="samples per GPU per LoRA step")
+    ap.add_argument("--micro-batch", type=int, default=8, help="samples per LoRA forward/backward pass")
     ap.add_argument("--gemm", default="7744,32768,2048", help="M,N,K for --workload gemm")
     ap.add_argument("--epi", default="geglu", help="epilogue for --workload gemm")
     ap.add_argument("--batch", type=int, default=64)
@@ -460,6 +599,8 @@ def main():
             return run_sweep(args, local) if rank == 0 else 0
         if args.workload == "gemm":
             return run_gemm(args, local) if rank == 0 else 0
+        if args.workload == "lora":
+            return run_lora(args, world, rank, local)
         return run_ours(args, world, rank, local)
     finally:
         if world > 1:

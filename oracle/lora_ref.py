@@ -142,14 +142,19 @@ class LoraRef:
 
     # ---- the loss
     def loss(self, prefix_emb, actions, noise, t):
-        nb, P, _ = prefix_emb.shape
-        H = actions.shape[1]
-        xp = torch.from_numpy(np.ascontiguousarray(prefix_emb, np.float32))
         a = torch.from_numpy(np.asarray(actions, np.float32))
         eps = torch.from_numpy(np.asarray(noise, np.float32))
         tt = torch.from_numpy(np.asarray(t, np.float32))[:, None, None]
         xt = tt * eps + (1 - tt) * a
         u = eps - a
+        v = self.velocity(prefix_emb, xt, t)
+        return ((v - u) ** 2).mean()
+
+    def velocity(self, prefix_emb, xt, t):
+        """v = net(x_t, t, prefix) for a batch: prefix_emb [nb][P][2048], xt [nb][H][32] (tensor), t [nb]"""
+        nb, P, _ = prefix_emb.shape
+        H = xt.shape[1]
+        xp = torch.from_numpy(np.ascontiguousarray(prefix_emb, np.float32))
         xs = R(xt @ self.ain_w.t() + self.ain_b)
         md = self.mods(t)
         cos, sin = rope_table(P + H)
@@ -181,8 +186,7 @@ class LoraRef:
             xs = R(xmid_s + R(self.lin(act, e["d"], "exp", l, "d") * gate2))
         mf = md[:, -1]
         hf = self.rms(xs, mf[:, None, :1024], mf[:, None, 1024:2048])
-        v = R(hf @ self.aout_w.t() + self.aout_b)
-        return ((v - u) ** 2).mean()
+        return R(hf @ self.aout_w.t() + self.aout_b)
 
     def grads(self):
         out = []
