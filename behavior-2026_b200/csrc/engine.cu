@@ -95,6 +95,7 @@ struct pi05_engine {
   std::map<int, long> denoise_launches, prefill_launches;
   long launches = 0;  // kernels enqueued (counted at capture time)
   struct Trainer* tr = nullptr;  // LoRA train state (train.cuh), created by pi05_lora_init
+  bool cluster_splitk = true;    // few-token split-K GEMMs reduce inside a cluster (PI05_CLUSTER_SPLITK=0: tickets)
 };
 
 namespace {
@@ -280,6 +281,55 @@ bool launch_gemm_bn(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb
   }
 }
 
+template <typename... KArgs, typename... Args>
+bool launch_cluster(pi05_engine* e, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster, bool pdl,
+                    Args&&... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = e->stream;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cluster;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = (pdl && e->pdl) ? 1 : 0;
+  lc.attrs = at;
+  lc.numAttrs = 2;
+  CK(cudaLaunchKernelEx(&lc, kern, std::forward<Args>(args)...));
+  e->launches++;
+  return true;
+}
+
+template <int BN>
+bool launch_swap_cluster(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga, int S) {
+  const dim3 grid(ga.tiles_m * S);
+  const size_t sm = (size_t)GemmCfg<BN>::SMEM;
+  const bool p = ga.pdl != 0;
+  switch (ga.epi) {
+    case EPI_GELU: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_GELU>, grid, dim3(256), sm, S, p, ta, tb, ga);
+    case EPI_RESID: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_RESID>, grid, dim3(256), sm, S, p, ta, tb, ga);
+    case EPI_GATED: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_GATED>, grid, dim3(256), sm, S, p, ta, tb, ga);
+    case EPI_GEGLU: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_GEGLU>, grid, dim3(256), sm, S, p, ta, tb, ga);
+    case EPI_F32: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_F32>, grid, dim3(256), sm, S, p, ta, tb, ga);
+    default: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_STORE>, grid, dim3(256), sm, S, p, ta, tb, ga);
+  }
+}
+
+template <int BN>
+bool set_swap_cluster_smem(pi05_engine* e) {
+  const int sm = GemmCfg<BN>::SMEM;
+  CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_GEGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  return true;
+}
+
 template <int BN>
 bool launch_gemm_small(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga, bool amn) {
   const int units = ga.tiles_m * ga.tiles_n * ga.splits;
@@ -398,6 +448,17 @@ bool linear(pi05_engine* e, const Lin& L) {
   ga.lg_trans = L.lg_trans;
   ga.lg_K = L.lg_K;
   for (int i = 0; i < 3; ++i) ga.lg_off[i] = L.lg_off[i];
+  if (swap && splits > 1 && e->cluster_splitk) {
+    // few tokens, K split: reduce the split partials on chip inside a cluster of S CTAs
+    int S = 1;
+    const int want = std::min(8, std::max(1, std::min(e->num_sms / ga.tiles_m, kt / 2)));
+    while (S * 2 <= want) S *= 2;
+    if (S > 1) {
+      ga.kt_per_split = (kt + S - 1) / S;
+      ga.splits = S;
+      return BN == 64 ? launch_swap_cluster<64>(e, ta, tb, ga, S) : launch_swap_cluster<128>(e, ta, tb, ga, S);
+    }
+  }
   if (BN == 16) return launch_gemm_small<16>(e, ta, tb, ga, L.amn);
   if (BN == 32) return launch_gemm_small<32>(e, ta, tb, ga, L.amn);
   if (BN == 48) return launch_gemm_small<48>(e, ta, tb, ga, L.amn);
@@ -880,6 +941,7 @@ bool create(pi05_engine* e) {
   e->num_sms = prop.multiProcessorCount;
   // PI05_PDL=0 launches without programmatic dependent launch (each kernel waits for the previous one)
   if (const char* s = getenv("PI05_PDL")) e->pdl = atoi(s) != 0;
+  if (const char* s = getenv("PI05_CLUSTER_SPLITK")) e->cluster_splitk = atoi(s) != 0;
   CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   cudaDriverEntryPointQueryResult q;
   void* fn = nullptr;
@@ -889,6 +951,7 @@ bool create(pi05_engine* e) {
 
   if (!set_gemm_smem<64>(e) || !set_gemm_smem<128>(e) || !set_gemm_smem<256>(e)) return false;
   if (!set_gemm_smem_small<16>(e) || !set_gemm_smem_small<32>(e) || !set_gemm_smem_small<48>(e)) return false;
+  if (!set_swap_cluster_smem<64>(e) || !set_swap_cluster_smem<128>(e)) return false;
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<P5_HD>::SMEM));
   CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_SIG_HD>::SMEM));
@@ -1266,6 +1329,101 @@ int pi05_op_linear(pi05_engine* e, int T, int F, int K, const void* x, const voi
   L.gate_div = 1;
   if (!linear(e, L)) return fail_code(e);
   return PI05_OK;
+}
+
+// Device time of one linear layer: `reps` launches captured in a CUDA graph, each on its own copy of the
+// weights (enough copies to exceed 256 MB, so every launch streams its weights from HBM, not L2).
+int pi05_op_bench_linear(pi05_engine* e, int T, int F, int K, int epi, int reps, float* us_per_launch) {
+  if (!e || T < 1 || F < 1 || K < 64 || K % 8 || reps < 1 || !us_per_launch || epi < EPI_STORE || epi > EPI_F32 ||
+      (epi == EPI_GEGLU && F % 32))
+    return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  const size_t wbytes = (size_t)F * K * 2;
+  const int copies = (int)std::max<size_t>(1, std::min<size_t>(64, ((256ull << 20) + wbytes - 1) / wbytes));
+  std::vector<void*> bufs;
+  auto release = [&]() {
+    cudaStreamSynchronize(e->stream);
+    for (void* p : bufs) cudaFree(p);
+  };
+  void *x = nullptr, *out = nullptr, *res = nullptr, *gate = nullptr;
+  if (cudaMalloc(&x, (size_t)T * K * 2) != cudaSuccess) return PI05_ERR_CUDA;
+  bufs.push_back(x);
+  if (cudaMalloc(&out, (size_t)T * F * 4) != cudaSuccess || cudaMalloc(&res, (size_t)T * F * 2) != cudaSuccess ||
+      cudaMalloc(&gate, (size_t)F * 2) != cudaSuccess) {
+    release();
+    return PI05_ERR_CUDA;
+  }
+  bufs.push_back(out);
+  bufs.push_back(res);
+  bufs.push_back(gate);
+  std::vector<bf16*> ws;
+  for (int c = 0; c < copies; ++c) {
+    void* w = nullptr;
+    if (cudaMalloc(&w, wbytes) != cudaSuccess) {
+      release();
+      return PI05_ERR_CUDA;
+    }
+    bufs.push_back(w);
+    ws.push_back((bf16*)w);
+    fill_param_kernel<<<148 * 4, 256, 0, e->stream>>>((bf16*)w, F, K, K, 0, 1, p5_key(c, 999, 0),
+                                                     p5_scale_for_std(0.02), 0.f);
+  }
+  fill_param_kernel<<<148 * 4, 256, 0, e->stream>>>((bf16*)x, T, K, K, 0, 1, p5_key(1, 998, 0), p5_scale_for_std(1.0),
+                                                   0.f);
+  cudaMemsetAsync(res, 0, (size_t)T * F * 2, e->stream);
+  cudaMemsetAsync(gate, 0, (size_t)F * 2, e->stream);
+  auto one = [&](int i) {
+    Lin L{(const bf16*)x, K, T, ws[i % copies], K, F, K};
+    L.epi = epi;
+    if (epi == EPI_F32) {
+      L.out_f32 = (float*)out;
+      L.ld_out_f32 = F;
+    } else {
+      L.out = (bf16*)out;
+      L.ld_out = epi == EPI_GEGLU ? F / 2 : F;
+    }
+    L.res = (const bf16*)res;
+    L.ld_res = F;
+    L.gate = (const bf16*)gate;
+    return linear(e, L);
+  };
+  // warm-up (also sets up every launch's tensor maps), then capture and replay
+  for (int i = 0; i < std::min(reps, copies); ++i)
+    if (!one(i)) {
+      release();
+      return fail_code(e);
+    }
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t gx = nullptr;
+  if (cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    release();
+    return PI05_ERR_CUDA;
+  }
+  bool ok = true;
+  for (int i = 0; i < reps && ok; ++i) ok = one(i);
+  cudaStreamEndCapture(e->stream, &g);
+  if (!ok || !g || cudaGraphInstantiate(&gx, g, 0) != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    release();
+    return ok ? PI05_ERR_CUDA : fail_code(e);
+  }
+  cudaGraphDestroy(g);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaGraphLaunch(gx, e->stream);  // warm replay
+  cudaEventRecord(e0, e->stream);
+  cudaGraphLaunch(gx, e->stream);
+  cudaEventRecord(e1, e->stream);
+  cudaEventSynchronize(e1);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  *us_per_launch = ms * 1000.0f / reps;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaGraphExecDestroy(gx);
+  release();
+  return check_status(e) ? PI05_OK : fail_code(e);
 }
 
 int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, int ldq, const void* k, const void* v,

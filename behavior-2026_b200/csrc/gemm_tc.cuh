@@ -549,4 +549,186 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------------
+// Few-token weight streaming with split-K inside a thread-block cluster (swap orientation only).
+//
+// A tile of 128 weight rows is split along K over the S CTAs of one cluster (S <= 8).  Each CTA
+// stages its fp32 partial tile in its own shared memory; after a cluster barrier CTA r reduces rows
+// [r*128/S, (r+1)*128/S) by reading the S partials over distributed shared memory in rank order
+// (deterministic), applies the epilogue and stores.  The partials never leave the chip and the
+// reduction is spread over all S CTAs instead of the last one.
+template <int EPI>
+__device__ __forceinline__ float epi_swap_value(const GemmArgs& a, float v, int f, int t) {
+  float x = v * a.out_scale + (a.bias ? bf(a.bias[f]) : 0.f);
+  if (EPI == EPI_F32) return x;
+  if (EPI == EPI_GELU) return gelu_tanh(rbf(x));
+  if (EPI == EPI_RESID) return bf(a.res[(size_t)t * a.ld_res + f]) + rbf(x);
+  if (EPI == EPI_GATED)
+    return bf(a.res[(size_t)t * a.ld_res + f]) + rbf(rbf(x) * bf(a.gate[(size_t)(t / a.gate_div) * a.ld_gate + f]));
+  return x;
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(256, 1)
+    gemm_swap_cluster_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                             const GemmArgs args) {
+  using C = GemmCfg<BN>;
+  constexpr int RED_LD = BN + 4;  // fp32 partial row stride: 16-byte rows, 8 rows hit 8 distinct 16-byte slots
+  static_assert(128 * RED_LD * 4 <= C::STAGES * C::STAGE_BYTES, "partial tile must fit in the stage buffers");
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  float* red = reinterpret_cast<float*>(smem);  // reuses the stage buffers once the MMAs are done
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+  uint64_t* empty_bar = full_bar + C::STAGES;
+  uint64_t* accum_bar = empty_bar + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = (int)cluster_size(), rank = (int)cluster_rank();
+  const int tm = blockIdx.x / S;
+  const int m0 = tm * C::BM;
+  const int kt_total = (args.K + C::BK - 1) / C::BK;
+  const int kt0 = rank * args.kt_per_split;
+  const int nkt = max(0, min(kt_total, kt0 + args.kt_per_split) - kt0);
+  constexpr uint32_t TCOLS = BN < 32 ? 32 : BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(accum_bar, 1);
+    flags[0] = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, TCOLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (args.pdl) pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool waited = !args.pdl;
+      for (int i = 0; i < nkt; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
+        if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.status, P5_ERR_WAIT_EMPTY)) {
+          flags[0] = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+        tma_load_2d(sA + s * C::A_BYTES, &tma_a, &full_bar[s], (kt0 + i) * C::BK, m0);  // weights: no dependency
+        if (!waited) {
+          pdl_wait();
+          waited = true;
+        }
+        tma_load_2d(sB + s * C::B_BYTES, &tma_b, &full_bar[s], (kt0 + i) * C::BK, 0);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = mma_idesc_bf16(C::BM, BN);
+      for (int i = 0; i < nkt && !flags[0]; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
+        if (!mbar_wait(&full_bar[s], ph, args.status, P5_ERR_WAIT_FULL)) {
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES), b_addr = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < C::BK / 16; ++kk)
+          tc_mma_f16(tmem_base, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
+                     (i > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&empty_bar[s]);
+      }
+      tc_commit(accum_bar);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // partial tile -> own shared memory (zeros when this split had no K-tiles or gave up)
+    const int sub = warp & 3;
+    const bool ok = mbar_wait(accum_bar, 0, args.status, P5_ERR_WAIT_ACCUM) && !flags[0] && nkt > 0;
+    tc_fence_after();
+    const int row = sub * 32 + lane;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)c, r);
+      tmem_wait_ld();
+      float4* dst = reinterpret_cast<float4*>(red + row * RED_LD + c);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        dst[q] = ok ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                  __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  tc_fence_before();
+  cluster_sync();  // every partial tile of the cluster is in shared memory
+
+  if (warp >= 4) {
+    if (args.pdl) pdl_wait();
+    const int R = C::BM / S;  // rows this CTA reduces
+    const int tid = threadIdx.x - 128;
+    const uint32_t red_base = smem_u32(red);
+    // items = (row, group of 4 tokens); consecutive threads take consecutive weight rows of one group,
+    // so the stores of each token are contiguous across the warp.  R*BN/4 is a multiple of 128.
+    for (int it = tid; it < R * (BN / 4); it += 128) {
+      const int lr = it % R, cg = it / R;
+      const int row = rank * R + lr;
+      const uint32_t addr = red_base + (uint32_t)(row * RED_LD + cg * 4) * 4u;
+      float4 pv[8];
+#pragma unroll
+      for (int p = 0; p < 8; ++p)  // all peers' loads in flight before the first add
+        pv[p] = p < S ? ld_peer_v4(map_peer(addr, (uint32_t)p)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {  // rank order: deterministic
+        v[0] += pv[p].x;
+        v[1] += pv[p].y;
+        v[2] += pv[p].z;
+        v[3] += pv[p].w;
+      }
+      const int f = m0 + row;
+      const float bias = (f < args.M && args.bias) ? bf(args.bias[f]) : 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int t = cg * 4 + q;
+        const bool valid = f < args.M && t < args.N;
+        if (EPI == EPI_GEGLU) {
+          // rows (2j, 2j+1) = (gate_j, up_j) sit in neighbouring lanes (R is even)
+          const float mine = rbf(v[q] * args.out_scale + bias);
+          const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+          if (valid && (f & 1) == 0) args.out[(size_t)t * args.ld_out + f / 2] = tobf(rbf(gelu_tanh(mine)) * other);
+        } else if (valid) {
+          const float x = epi_swap_value<EPI>(args, v[q], f, t);
+          if (EPI == EPI_F32)
+            args.out_f32[(size_t)t * args.ld_out_f32 + f] = x;
+          else
+            args.out[(size_t)t * args.ld_out + f] = tobf(x);
+        }
+      }
+    }
+  }
+  cluster_sync();  // peers are done reading this CTA's partial tile
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TCOLS);
+  }
+}
+
 }  // namespace p5

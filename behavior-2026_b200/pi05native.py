@@ -110,6 +110,7 @@ def _load():
     L.pi05_lora_get_grads.argtypes = [vp, vp]
     L.pi05_lora_grad_buffer.argtypes = [vp]
     L.pi05_lora_grad_buffer.restype = vp
+    L.pi05_op_bench_linear.argtypes = [vp, i32, i32, i32, i32, i32, P(ctypes.c_float)]
     L.pi05_lora_reset_optimizer.argtypes = [vp]
     L.pi05_lora_save_state.argtypes = [vp, ctypes.c_char_p]
     L.pi05_lora_load_state.argtypes = [vp, ctypes.c_char_p]
@@ -240,6 +241,12 @@ class Engine:
         F = w.shape[0]
         p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
         self._check(lib.pi05_op_linear(self._h, T, F, K, p(x), p(w), p(bias), p(res), p(gate), self.EPI[epi], p(out)))
+
+    def op_bench_linear(self, T, F, K, epi="store", reps=50):
+        """device microseconds per launch of one linear layer (graph-timed, weights streamed from HBM)"""
+        us = ctypes.c_float(0)
+        self._check(lib.pi05_op_bench_linear(self._h, T, F, K, self.EPI[epi], reps, ctypes.byref(us)))
+        return us.value
 
     def op_attention(self, q, k, v, out, splits=1):
         """q [b][T][ldq] (heads at column 0), k/v [b][S][256], out [b][T][2048]; all CUDA bf16 tensors."""

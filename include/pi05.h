@@ -153,6 +153,9 @@ PI05_API int pi05_op_linear(pi05_engine* e, int T, int F, int K, const void* x, 
                             const void* res, const void* gate, int epi, void* out);
 PI05_API int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, int ldq, const void* k,
                                const void* v, void* out, int splits);
+/* Device time (microseconds per launch) of pi05_op_linear on internal random operands: `reps` launches
+ * in one CUDA graph, rotating over enough weight copies (> 256 MB) that each launch reads HBM. */
+PI05_API int pi05_op_bench_linear(pi05_engine* e, int T, int F, int K, int epi, int reps, float* us_per_launch);
 
 /* Few-token linear layer that allocates nothing: out[T][F] = bf16(x[T][K] . w[F][K]^T + bias[F]), the
  * same kernel and tiling as the engine's weight-streaming path, for callers that cannot call
