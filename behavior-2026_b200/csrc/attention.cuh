@@ -43,19 +43,19 @@ struct AttnArgs {
   long lse_b;
 };
 
-template <int HD>
+template <int HD, int NW = 4>
 struct AttnCfg {
   static constexpr int HDP = (HD + 15) / 16 * 16;  // padded to the MMA K step
   static constexpr int LDS = HDP + 8;              // smem row stride (elements): conflict-free ldmatrix
-  static constexpr int ROWS = 64, KT = 64;
-  static constexpr int TILE_ELEMS = 64 * LDS;
-  static constexpr int SMEM = (3 * 2 - 1) * TILE_ELEMS * 2;  // Q + 2 x (K, V)
-  static constexpr int ND = HD / 8;                           // output n-tiles of 8
+  static constexpr int ROWS = 16 * NW, KT = 64;    // query rows per CTA (16 per warp), keys per tile
+  static constexpr int TILE_ELEMS = KT * LDS;      // one K or V tile
+  static constexpr int SMEM = (ROWS * LDS + 4 * TILE_ELEMS) * 2;  // Q + 2 x (K, V)
+  static constexpr int ND = HD / 8;                                // output n-tiles of 8
 };
 
 template <int HD>
 __device__ __forceinline__ void attn_load_kv(const AttnArgs& a, int b, int j0, int head_col, bf16* sK, bf16* sV) {
-  using C = AttnCfg<HD>;
+  using C = AttnCfg<HD, 4>;
   constexpr int CH = HD * 2 / 16;  // 16-byte chunks per row
   const int total = a.len1 + a.len2;
   for (int i = threadIdx.x; i < C::KT * CH; i += blockDim.x) {
@@ -79,13 +79,14 @@ __device__ __forceinline__ void attn_load_kv(const AttnArgs& a, int b, int j0, i
   }
 }
 
-template <int HD>
-__global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
-  using C = AttnCfg<HD>;
+template <int HD, int NW>
+__global__ void __launch_bounds__(32 * NW) attn_kernel(const AttnArgs a) {
+  using C = AttnCfg<HD, NW>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   bf16* sQ = reinterpret_cast<bf16*>(smem_raw);
-  bf16* sK[2] = {sQ + C::TILE_ELEMS, sQ + 2 * C::TILE_ELEMS};
-  bf16* sV[2] = {sQ + 3 * C::TILE_ELEMS, sQ + 4 * C::TILE_ELEMS};
+  bf16* kv0 = sQ + C::ROWS * C::LDS;
+  bf16* sK[2] = {kv0, kv0 + C::TILE_ELEMS};
+  bf16* sV[2] = {kv0 + 2 * C::TILE_ELEMS, kv0 + 3 * C::TILE_ELEMS};
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows_total = a.T * a.G;

@@ -39,6 +39,11 @@ __device__ __forceinline__ float2 unpack_bf2(uint32_t v) {
   return __bfloat1622float2(t);
 }
 
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y), c = unpack_bf2(u.z), d = unpack_bf2(u.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float c = 0.7978845608028654f;
   return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));

@@ -485,16 +485,21 @@ bool attention(pi05_engine* e, const AttnArgs& a0, int batch, int hd) {
     }
   }
   const int heads = a.G == 1 ? (hd == P5_SIG_HD ? P5_SIG_HEADS : 1) : 1;
-  dim3 grid((rows + 63) / 64, heads, batch * a.splits);
+  // 8 warps (128 query rows share each K/V tile) when that still gives two waves of CTAs, else 4
+  const bool wide = (long)((rows + 127) / 128) * heads * batch * a.splits >= 2L * e->num_sms;
+  dim3 grid((rows + (wide ? 127 : 63)) / (wide ? 128 : 64), heads, batch * a.splits);
   if (hd == P5_HD) {
-    if (!launch(e, attn_kernel<P5_HD>, grid, dim3(128), (size_t)AttnCfg<P5_HD>::SMEM, true, a)) return false;
+    const bool ok = wide ? launch(e, attn_kernel<P5_HD, 8>, grid, dim3(256), (size_t)AttnCfg<P5_HD, 8>::SMEM, true, a)
+                         : launch(e, attn_kernel<P5_HD, 4>, grid, dim3(128), (size_t)AttnCfg<P5_HD, 4>::SMEM, true, a);
+    if (!ok) return false;
     if (a.splits > 1) {
       const long n = (long)batch * rows * (P5_HD / 2);
       if (!launch(e, attn_combine_kernel<P5_HD>, dim3((n + 255) / 256), dim3(256), 0, true, a, batch)) return false;
     }
     return true;
   }
-  return launch(e, attn_kernel<P5_SIG_HD>, grid, dim3(128), (size_t)AttnCfg<P5_SIG_HD>::SMEM, true, a);
+  return wide ? launch(e, attn_kernel<P5_SIG_HD, 8>, grid, dim3(256), (size_t)AttnCfg<P5_SIG_HD, 8>::SMEM, true, a)
+              : launch(e, attn_kernel<P5_SIG_HD, 4>, grid, dim3(128), (size_t)AttnCfg<P5_SIG_HD, 4>::SMEM, true, a);
 }
 
 int rows_grid(long rows_warps) { return (int)((rows_warps * 32 + 255) / 256); }
@@ -952,9 +957,14 @@ bool create(pi05_engine* e) {
   if (!set_gemm_smem<64>(e) || !set_gemm_smem<128>(e) || !set_gemm_smem<256>(e)) return false;
   if (!set_gemm_smem_small<16>(e) || !set_gemm_smem_small<32>(e) || !set_gemm_smem_small<48>(e)) return false;
   if (!set_swap_cluster_smem<64>(e) || !set_swap_cluster_smem<128>(e)) return false;
-  CK(cudaFuncSetAttribute(attn_kernel<P5_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<P5_HD>::SMEM));
-  CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          AttnCfg<P5_SIG_HD>::SMEM));
+  CK(cudaFuncSetAttribute(attn_kernel<P5_HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          AttnCfg<P5_HD, 4>::SMEM));
+  CK(cudaFuncSetAttribute(attn_kernel<P5_HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          AttnCfg<P5_HD, 8>::SMEM));
+  CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          AttnCfg<P5_SIG_HD, 4>::SMEM));
+  CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          AttnCfg<P5_SIG_HD, 8>::SMEM));
 
   // weights
   e->warena = nullptr;

@@ -81,11 +81,6 @@ struct GemmCfg {
   static constexpr int CH = (BN % 32 == 0) ? 32 : 16;  // epilogue chunk (TMEM columns per tcgen05.ld)
 };
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y), c = unpack_bf2(u.z), d = unpack_bf2(u.w);
-  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
-}
-
 // ---- normal orientation: one token row t, 32 consecutive features f0..f0+31 ----
 template <int EPI>
 __device__ __forceinline__ void epi_row32(const GemmArgs& a, float (&v)[32], int t, int f0) {

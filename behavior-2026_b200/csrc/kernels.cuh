@@ -48,24 +48,56 @@ __global__ void patchify_kernel(const uint8_t* img, bf16* A, int n_img) {
 
 // ---------------------------------------------------------------- norms (one warp per row)
 // flax LayerNorm, eps 1e-6, two-pass statistics in fp32
+// The row is read once with 16-byte loads and kept in registers for both passes (D <= 8 * 256).
 __global__ void layernorm_kernel(const bf16* x, bf16* y, const bf16* s, const bf16* b, int T, int D) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   pdl_wait();
   if (warp >= T) return;
   const bf16* xr = x + (long)warp * D;
+  constexpr int MAXC = 8;  // 16-byte chunks per lane
+  float v[MAXC][8];
   float sum = 0.f;
-  for (int i = lane; i < D; i += 32) sum += bf(xr[i]);
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int i = (lane + 32 * c) * 8;
+    if (i < D) {
+      unpack8(*reinterpret_cast<const uint4*>(xr + i), v[c]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) sum += v[c][q];
+    }
+  }
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   const float mean = sum / (float)D;
   float var = 0.f;
-  for (int i = lane; i < D; i += 32) {
-    const float d = bf(xr[i]) - mean;
-    var += d * d;
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int i = (lane + 32 * c) * 8;
+    if (i < D) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float d = v[c][q] - mean;
+        var += d * d;
+      }
+    }
   }
   for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
   const float inv = 1.0f / sqrtf(var / (float)D + 1e-6f);
   bf16* yr = y + (long)warp * D;
-  for (int i = lane; i < D; i += 32) yr[i] = tobf((bf(xr[i]) - mean) * inv * bf(s[i]) + bf(b[i]));
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int i = (lane + 32 * c) * 8;
+    if (i < D) {
+      float sc[8], bb[8];
+      unpack8(*reinterpret_cast<const uint4*>(s + i), sc);
+      unpack8(*reinterpret_cast<const uint4*>(b + i), bb);
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        o[q] = pack_bf2((v[c][2 * q] - mean) * inv * sc[2 * q] + bb[2 * q],
+                        (v[c][2 * q + 1] - mean) * inv * sc[2 * q + 1] + bb[2 * q + 1]);
+      *reinterpret_cast<uint4*>(yr + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
   pdl_launch_dependents();
 }
 
