@@ -41,6 +41,7 @@ struct AttnArgs {
   int pdl;
   float* lse;       // optional (splits == 1): log-sum-exp per row, [b * lse_b + row]
   long lse_b;
+  int force_splits; // > 0: the tensor-core path uses this many key splits instead of choosing
 };
 
 template <int HD, int NW = 4>

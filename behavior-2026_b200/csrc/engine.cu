@@ -16,6 +16,7 @@
 
 #include "../../include/pi05.h"
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
@@ -96,6 +97,7 @@ struct pi05_engine {
   long launches = 0;  // kernels enqueued (counted at capture time)
   struct Trainer* tr = nullptr;  // LoRA train state (train.cuh), created by pi05_lora_init
   bool cluster_splitk = true;    // few-token split-K GEMMs reduce inside a cluster (PI05_CLUSTER_SPLITK=0: tickets)
+  bool attn_tc = true;           // head_dim-256 MQA attention on tcgen05 (PI05_ATTN_TC=0: the mma.sync kernel)
 };
 
 namespace {
@@ -231,6 +233,28 @@ bool make_tmap_box(pi05_engine* e, CUtensorMap* m, const bf16* base, long rows, 
   cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1, 1};
   CUresult r = e->encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16*>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_err(e, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return true;
+}
+
+// rank-3/4 map with 128-byte swizzle: dims[0] contiguous, strides in bytes for dims 1.., box per dim
+bool make_tmap_nd(pi05_engine* e, CUtensorMap* m, const bf16* base, int rank, const uint64_t* dims,
+                  const uint64_t* strides, const uint32_t* box) {
+  if ((uintptr_t)base & 15) return set_err(e, "tensor map: misaligned operand");
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) {
+      if (strides[i] % 16) return set_err(e, "tensor map: misaligned stride");
+      st[i] = strides[i];
+    }
+  }
+  CUresult r = e->encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<bf16*>(base), d, st, bx, es,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_err(e, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
@@ -467,7 +491,73 @@ bool linear(pi05_engine* e, const Lin& L) {
   return launch_gemm_bn<256>(e, ta, tb, ga);
 }
 
+// head_dim-256 MQA attention on tcgen05 (attn_tc_kernel).  Splits the key tiles over CTAs when one
+// CTA per 128-row block would leave SMs idle (never when the caller wants the log-sum-exp).
+bool attention_tc(pi05_engine* e, const AttnArgs& a0, int batch) {
+  using C = AttnTcCfg;
+  AttnArgs a = a0;
+  a.pdl = e->pdl ? 1 : 0;
+  const int rows = a.T * 8, rb = (rows + C::ROWS - 1) / C::ROWS;
+  const int ntiles = (a.len1 + C::KT - 1) / C::KT + (a.len2 + C::KT - 1) / C::KT;
+  const long ctas = (long)rb * batch;
+  int splits = 1;
+  if (a.force_splits > 0) {
+    splits = a.lse ? 1 : std::min(a.force_splits, ntiles);
+  } else if (!a.lse && ctas < e->num_sms) {
+    // waves x (tiles per CTA + ~2 tiles of fixed cost: Q load, epilogue), +1 for the combine pass
+    long best = -1;
+    for (int s = 1; s <= std::min(ntiles, 16); ++s) {
+      const int t = std::max((ntiles + s - 1) / s, s > 1 ? 2 : 1);
+      const int se = (ntiles + t - 1) / t;
+      const long cost = (ctas * se + e->num_sms - 1) / e->num_sms * (t + 2) + (se > 1 ? 1 : 0);
+      if (best < 0 || cost < best) {
+        best = cost;
+        splits = se;
+      }
+    }
+  }
+  while (splits > 1 && (size_t)batch * splits * rows > e->attn_ws_rows) --splits;
+  int tps = std::max((ntiles + splits - 1) / splits, splits > 1 ? 2 : 1);
+  a.splits = std::max(1, (ntiles + tps - 1) / tps);
+  if (a.splits == 1) tps = std::max(ntiles, 1);
+  a.keys_per_split = tps * C::KT;
+  if (a.splits > 1) {
+    a.ws_o = e->attn_ws_o;
+    a.ws_ml = e->attn_ws_ml;
+  }
+  CUtensorMap tq, tk1, tv1, tk2, tv2;
+  {
+    const uint64_t dims[4] = {P5_HD, 8, (uint64_t)a.T, (uint64_t)batch};
+    const uint64_t st[3] = {P5_HD * 2, (uint64_t)a.ldq * 2, (uint64_t)a.q_bstride * 2};
+    const uint32_t box[4] = {64, 8, 16, 1};
+    if (!make_tmap_nd(e, &tq, a.q, 4, dims, st, box)) return false;
+  }
+  auto kv_map = [&](CUtensorMap* m, const bf16* base, int len, int ld, long bstride) {
+    const uint64_t dims[3] = {P5_HD, (uint64_t)len, (uint64_t)batch};
+    const uint64_t st[2] = {(uint64_t)ld * 2, (uint64_t)bstride * 2};
+    const uint32_t box[3] = {64, C::KT, 1};
+    return make_tmap_nd(e, m, base, 3, dims, st, box);
+  };
+  if (!kv_map(&tk1, a.k1, a.len1, a.ld1, a.b1stride) || !kv_map(&tv1, a.v1, a.len1, a.ld1, a.b1stride)) return false;
+  if (a.len2 > 0) {
+    if (!kv_map(&tk2, a.k2, a.len2, a.ld2, a.b2stride) || !kv_map(&tv2, a.v2, a.len2, a.ld2, a.b2stride))
+      return false;
+  } else {
+    tk2 = tk1;
+    tv2 = tv1;
+  }
+  if (!launch(e, attn_tc_kernel, dim3(rb, 1, batch * a.splits), dim3(384), (size_t)C::SMEM, true, tq, tk1, tv1, tk2,
+              tv2, a, e->d_status))
+    return false;
+  if (a.splits > 1) {
+    const long n = (long)batch * rows * (P5_HD / 2);
+    if (!launch(e, attn_combine_kernel<P5_HD>, dim3((n + 255) / 256), dim3(256), 0, true, a, batch)) return false;
+  }
+  return true;
+}
+
 bool attention(pi05_engine* e, const AttnArgs& a0, int batch, int hd) {
+  if (hd == P5_HD && a0.G == 8 && a0.qdiv == 1.0f && e->attn_tc && a0.len1 > 0) return attention_tc(e, a0, batch);
   AttnArgs a = a0;
   a.pdl = e->pdl ? 1 : 0;
   const int rows = a.T * a.G;
@@ -947,6 +1037,7 @@ bool create(pi05_engine* e) {
   // PI05_PDL=0 launches without programmatic dependent launch (each kernel waits for the previous one)
   if (const char* s = getenv("PI05_PDL")) e->pdl = atoi(s) != 0;
   if (const char* s = getenv("PI05_CLUSTER_SPLITK")) e->cluster_splitk = atoi(s) != 0;
+  if (const char* s = getenv("PI05_ATTN_TC")) e->attn_tc = atoi(s) != 0;
   CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   cudaDriverEntryPointQueryResult q;
   void* fn = nullptr;
@@ -961,6 +1052,7 @@ bool create(pi05_engine* e) {
                           AttnCfg<P5_HD, 4>::SMEM));
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_HD, 8>::SMEM));
+  CK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_SIG_HD, 4>::SMEM));
   CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1459,6 +1551,7 @@ int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, in
   at.G = P5_NH;
   at.qdiv = 1.0f;
   at.splits = splits;
+  at.force_splits = splits;
   if (!attention(e, at, batch, P5_HD)) return fail_code(e);
   return PI05_OK;
 }

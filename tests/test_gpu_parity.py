@@ -85,12 +85,20 @@ def test_linear_epilogues_match_torch(pn, torch_cuda, epi, T):
     assert err <= 2e-2 * max(1.0, ref.abs().max().item()), (epi, err)
 
 
-@pytest.mark.parametrize("T,S,splits", [(50, 1018, 8), (50, 1018, 1), (968, 968, 1), (100, 2048, 4)])
-def test_attention_matches_torch(pn, torch_cuda, T, S, splits):
+@pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("T,S,splits,qscale", [(50, 1018, 8, 0.1), (50, 1018, 1, 0.1), (968, 968, 1, 0.1),
+                                               (100, 2048, 4, 0.1), (1, 1000, 3, 0.1), (33, 200, 1, 0.6),
+                                               (50, 1018, 5, 0.6)])
+def test_attention_matches_torch(pn, torch_cuda, monkeypatch, tc, T, S, splits, qscale):
+    """MQA head_dim-256 attention (8 heads folded into rows) against fp32 torch softmax attention.
+
+    Both kernels (tcgen05, and the mma.sync one kept for other head sizes) are checked; qscale 0.6
+    gives logits with std ~10, which exercises the tensor-core kernel's deferred rescaling of O."""
     torch = torch_cuda
+    monkeypatch.setenv("PI05_ATTN_TC", "1" if tc else "0")
     g = torch.Generator(device="cuda").manual_seed(T + S)
     b = 2
-    q = (torch.randn(b, T, 2560, device="cuda", generator=g) * 0.1).bfloat16()
+    q = (torch.randn(b, T, 2560, device="cuda", generator=g) * qscale).bfloat16()
     k = torch.randn(b, S, 256, device="cuda", generator=g).bfloat16()
     v = torch.randn(b, S, 256, device="cuda", generator=g).bfloat16()
     out = torch.empty(b, T, 2048, device="cuda", dtype=torch.bfloat16)
