@@ -269,13 +269,10 @@ __global__ void __launch_bounds__(32 * NW) attn_kernel(const AttnArgs a) {
   if (a.pdl) pdl_launch_dependents();
 }
 
-// merge split-KV partials: out = sum_s O_s e^(m_s - M) / sum_s l_s e^(m_s - M)
+// merge split-KV partials: out = sum_s O_s e^(m_s - M) / sum_s l_s e^(m_s - M); item = (b, row, pair)
 template <int HD>
-__global__ void attn_combine_kernel(const AttnArgs a, int batch) {
+__device__ __forceinline__ void attn_combine_item(const AttnArgs& a, long idx) {
   const int rows_total = a.T * a.G;
-  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (a.pdl) pdl_wait();
-  if (idx >= (long)batch * rows_total * (HD / 2)) return;
   const int d2 = idx % (HD / 2);
   const long br = idx / (HD / 2);
   const int row = br % rows_total, b = br / rows_total;
@@ -295,6 +292,13 @@ __global__ void attn_combine_kernel(const AttnArgs a, int batch) {
   const int hq = a.G > 1 ? row % a.G : 0;
   bf16* dst = a.out + b * a.o_bstride + (long)tok * a.ldo + hq * HD + 2 * d2;
   *reinterpret_cast<uint32_t*>(dst) = pack_bf2(o0 * inv, o1 * inv);
+}
+
+template <int HD>
+__global__ void attn_combine_kernel(const AttnArgs a, int batch) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (a.pdl) pdl_wait();
+  if (idx < (long)batch * a.T * a.G * (HD / 2)) attn_combine_item<HD>(a, idx);
   if (a.pdl) pdl_launch_dependents();
 }
 

@@ -39,15 +39,15 @@ struct AttnTcCfg {
   static constexpr float RESCALE_LOG2 = 8.0f;
 };
 
-__global__ void __launch_bounds__(384, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk1,
-                   const __grid_constant__ CUtensorMap tv1, const __grid_constant__ CUtensorMap tk2,
-                   const __grid_constant__ CUtensorMap tv2, const AttnArgs a, int* status) {
+// One 128-row block (rb) of one batch item / key split (z) with 384 threads: warp 0 loads, warp 1
+// issues the MMAs, warps 4-11 run the softmax.  `smem` is 1024-byte aligned with AttnTcCfg::SMEM - 1024
+// bytes; tmem_base holds 512 allocated columns.  The tensor maps may live in parameter or global memory.
+// Every thread of the CTA calls it; it returns after a CTA-wide barrier with all its MMAs complete.
+__device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMap* tq, const CUtensorMap* tk1,
+                                             const CUtensorMap* tv1, const CUtensorMap* tk2, const CUtensorMap* tv2,
+                                             int* status, uint8_t* smem, uint32_t tmem_base, int rb, int z) {
   using C = AttnTcCfg;
   constexpr float LOG2E = 1.4426950408889634f;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
   uint8_t* sQ = smem;
   uint8_t* ring = sQ + C::Q_BYTES;
   uint8_t* sP = ring + C::NS * C::SLOT;
@@ -60,20 +60,14 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* p_empty = p_full + 2;         // [2] P V product done (P buffer free, O updated)
   uint64_t* o_full = p_empty + 2;         // every MMA of the CTA complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
-  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort, [1] skip
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rb = blockIdx.x, z = blockIdx.z;
   const int b = z / a.splits, split = z % a.splits;
   const int n1 = (a.len1 + C::KT - 1) / C::KT, n2 = (a.len2 + C::KT - 1) / C::KT;
   const int tps = a.keys_per_split / C::KT;
   const int t0 = split * tps;
   const int n = max(0, min(n1 + n2, t0 + tps) - t0);
-
-  // a device-side wait already gave up in an earlier kernel: skip the work (uniformly for the CTA)
-  if (threadIdx.x == 0) flags[1] = status ? *((volatile int*)status) : 0;
-  __syncthreads();
-  if (flags[1] != 0) return;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -90,21 +84,15 @@ __global__ void __launch_bounds__(384, 1)
     mbar_init(o_full, 1);
     flags[0] = 0;
     fence_barrier_init();
-    tma_prefetch_desc(&tq);
-    tma_prefetch_desc(&tk1);
-    tma_prefetch_desc(&tv1);
-    tma_prefetch_desc(&tk2);
-    tma_prefetch_desc(&tv2);
-  }
-  if (warp == 2) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    tma_prefetch_desc(tq);
+    tma_prefetch_desc(tk1);
+    tma_prefetch_desc(tv1);
+    tma_prefetch_desc(tk2);
+    tma_prefetch_desc(tv2);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  if (a.pdl) pdl_launch_dependents();
 
   // tile t of this batch item's key list -> (segment, first key row in it, keys present)
   auto tile_of = [&](int t, int& seg, int& row0, int& valid) {
@@ -118,7 +106,7 @@ __global__ void __launch_bounds__(384, 1)
       // ---------------- TMA producer: Q once, then K_i / V_(i-1) in MMA consumption order
       if (a.pdl) pdl_wait();
       mbar_arrive_expect_tx(q_full, C::Q_BYTES);
-      for (int c = 0; c < 4; ++c) tma_load_4d(sQ + c * C::Q_ATOM, &tq, q_full, c * 64, 0, rb * 16, b);
+      for (int c = 0; c < 4; ++c) tma_load_4d(sQ + c * C::Q_ATOM, tq, q_full, c * 64, 0, rb * 16, b);
       int it = 0;
       for (int i = 0; i <= n && !flags[0]; ++i) {
         for (int kind = 0; kind < 2; ++kind) {
@@ -131,7 +119,7 @@ __global__ void __launch_bounds__(384, 1)
             flags[0] = 1;
             break;
           }
-          const CUtensorMap* m = kind == 0 ? (seg == 0 ? &tk1 : &tk2) : (seg == 0 ? &tv1 : &tv2);
+          const CUtensorMap* m = kind == 0 ? (seg == 0 ? tk1 : tk2) : (seg == 0 ? tv1 : tv2);
           mbar_arrive_expect_tx(&ring_full[s], C::SLOT);
           for (int c = 0; c < 4; ++c) tma_load_3d(ring + s * C::SLOT + c * C::BOX, m, &ring_full[s], c * 64, row0, b);
           ++it;
@@ -343,10 +331,33 @@ __global__ void __launch_bounds__(384, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  tc_fence_after();
+}
+
+__global__ void __launch_bounds__(384, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk1,
+                   const __grid_constant__ CUtensorMap tv1, const __grid_constant__ CUtensorMap tk2,
+                   const __grid_constant__ CUtensorMap tv2, const AttnArgs a, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
+  __shared__ uint32_t tmem_slot;
+  __shared__ int skip;
+  // a device-side wait already gave up in an earlier kernel: skip the work (uniformly for the CTA)
+  if (threadIdx.x == 0) skip = status ? *((volatile int*)status) : 0;
+  __syncthreads();
+  if (skip != 0) return;
+  if ((threadIdx.x >> 5) == 2) {
+    tmem_alloc(&tmem_slot, AttnTcCfg::TMEM_COLS);
+    tmem_relinquish();
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  if (a.pdl) pdl_launch_dependents();
+  attn_tc_body(a, &tq, &tk1, &tv1, &tk2, &tv2, status, smem, tmem_base, blockIdx.x, blockIdx.z);
+  if ((threadIdx.x >> 5) == 2) tmem_dealloc(tmem_base, AttnTcCfg::TMEM_COLS);
 }
 
 }  // namespace p5

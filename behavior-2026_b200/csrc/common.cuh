@@ -22,6 +22,7 @@ enum {
   P5_ERR_WAIT_ACCUM = 3,    // epilogue: accumulator never committed
   P5_ERR_WAIT_SPLITK = 4,   // split-K reduction
   P5_ERR_WAIT_ATTN = 5,     // tensor-core attention pipeline
+  P5_ERR_WAIT_GRID = 6,     // persistent kernel: grid-wide or per-tile counter barrier
 };
 
 namespace p5 {

@@ -17,6 +17,7 @@
 #include "../../include/pi05.h"
 #include "attention.cuh"
 #include "attention_tc.cuh"
+#include "denoise_mega.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
@@ -91,6 +92,14 @@ struct pi05_engine {
   size_t attn_ws_rows = 0;
 
   bool weights_ready = false;
+  int wgen = 0;  // bumped whenever the weights change
+  // persistent one-sample denoise (denoise_mega.cuh), opt-in with PI05_MEGA=1: it matches the
+  // per-kernel CUDA-graph path (~12 ms per 10-step chunk) but does not beat it yet
+  bool mega = false;
+  int mega_wgen = -1;
+  bf16* mega_wqkv = nullptr;
+  CUtensorMap* mega_maps = nullptr;
+  unsigned* mega_ctr = nullptr;
   int prefix_n = 0;  // batch whose prefix cache is valid
   std::map<int, cudaGraphExec_t> denoise_graphs, prefill_graphs;
   std::map<int, long> denoise_launches, prefill_launches;
@@ -756,7 +765,122 @@ bool run_prefill_body(pi05_engine* e, int n) {
   return run_gemma(e, n);
 }
 
+// The persistent one-sample denoise applies when a single sample's action tokens fit the N=64 side of
+// its GEMM tiles and the GPU has enough SMs for every phase's units.
+bool mega_applies(pi05_engine* e, int n) {
+  const int H = e->cfg.horizon;
+  const int attn_units = ((H * 8 + 127) / 128) * 9;
+  return e->mega && n == 1 && H >= 1 && H <= 64 && e->cfg.expert_layers > 0 && e->num_sms >= 128 &&
+         e->num_sms >= attn_units + 1 && e->P > 0;
+}
+
+// Buffers, tensor-map table and the q/k/v row permutation of the persistent denoise (re-permuted
+// whenever the weights changed).  Runs outside stream capture.
+bool mega_prepare(pi05_engine* e) {
+  using C = MegaCfg;
+  const int L = e->cfg.expert_layers, H = e->cfg.horizon, P = e->P;
+  const size_t wq = (size_t)P5_QKV * P5_EXP_W;
+  const int nmaps = L * C::NMAPS_LAYER + 5;
+  if (!e->mega_wqkv) {
+    if (!dalloc(e, (void**)&e->mega_wqkv, (size_t)L * wq * 2) ||
+        !dalloc(e, (void**)&e->mega_maps, (size_t)nmaps * sizeof(CUtensorMap)) ||
+        !dalloc(e, (void**)&e->mega_ctr, MG_NCTR * 4))
+      return false;
+    Acts& A = e->A;
+    const size_t cache_layer = (size_t)e->max_batch * P * P5_HD;
+    std::vector<CUtensorMap> m(nmaps);
+    auto kv3 = [&](CUtensorMap* t, const bf16* base, int len) {
+      const uint64_t dims[3] = {P5_HD, (uint64_t)len, 1};
+      const uint64_t st[2] = {P5_HD * 2, (uint64_t)len * P5_HD * 2};
+      const uint32_t box[3] = {64, AttnTcCfg::KT, 1};
+      return make_tmap_nd(e, t, base, 3, dims, st, box);
+    };
+    for (int l = 0; l < L; ++l) {
+      CUtensorMap* t = &m[(size_t)l * C::NMAPS_LAYER];
+      const ExpLayer& x = e->ex[l];
+      if (!make_tmap(e, t + 0, e->mega_wqkv + l * wq, P5_QKV, P5_EXP_W, P5_EXP_W, 128) ||
+          !make_tmap(e, t + 1, x.wo, P5_EXP_W, P5_QDIM, P5_QDIM, 128) ||
+          !make_tmap(e, t + 2, x.wgu, 2 * P5_EXP_MLP, P5_EXP_W, P5_EXP_W, 128) ||
+          !make_tmap(e, t + 3, x.wd, P5_EXP_W, P5_EXP_MLP, P5_EXP_MLP, 128) ||
+          !kv3(t + 4, A.kcache + l * cache_layer, P) || !kv3(t + 5, A.vcache + l * cache_layer, P))
+        return false;
+    }
+    CUtensorMap* g = &m[(size_t)L * C::NMAPS_LAYER];
+    {
+      const uint64_t dims[4] = {P5_HD, 8, (uint64_t)H, 1};
+      const uint64_t st[3] = {P5_HD * 2, (uint64_t)P5_QKV * 2, (uint64_t)H * P5_QKV * 2};
+      const uint32_t box[4] = {64, 8, 16, 1};
+      if (!make_tmap_nd(e, g + 0, A.eqkv, 4, dims, st, box)) return false;
+    }
+    if (!kv3(g + 1, A.ek, H) || !kv3(g + 2, A.ev, H) || !make_tmap_box(e, g + 3, A.eo, H, P5_QDIM, P5_QDIM, 64, 64) ||
+        !make_tmap_box(e, g + 4, A.eact, H, P5_EXP_MLP, P5_EXP_MLP, 64, 64))
+      return false;
+    CK(cudaMemcpyAsync(e->mega_maps, m.data(), m.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, e->stream));
+  }
+  if (e->mega_wgen != e->wgen) {
+    for (int l = 0; l < L; ++l)
+      if (!launch(e, permute_qkv_rows_kernel, dim3(P5_QKV), dim3(128), 0, false, (const bf16*)e->ex[l].wqkv,
+                  e->mega_wqkv + l * wq))
+        return false;
+    e->mega_wgen = e->wgen;
+  }
+  return true;
+}
+
+bool run_denoise_mega(pi05_engine* e) {
+  using C = MegaCfg;
+  const int H = e->cfg.horizon;
+  Acts& A = e->A;
+  MegaArgs m = {};
+  m.x = A.ex;
+  m.xt = A.xt;
+  m.qkv = A.eqkv;
+  m.ek = A.ek;
+  m.ev = A.ev;
+  m.eo = A.eo;
+  m.act = A.eact;
+  m.ws = e->gemm_ws;
+  m.attn_o = e->attn_ws_o;
+  m.attn_ml = e->attn_ws_ml;
+  m.ctr = e->mega_ctr;
+  m.status = e->d_status;
+  m.mods = e->mods;
+  m.ain_w = e->ain_w;
+  m.ain_b = e->ain_b;
+  m.aout_w = e->aout_w;
+  m.aout_b = e->aout_b;
+  m.cos_t = e->d_cos;
+  m.sin_t = e->d_sin;
+  m.maps = e->mega_maps;
+  m.T = H;
+  m.P = e->P;
+  m.L = e->cfg.expert_layers;
+  m.steps = e->cfg.num_steps;
+  m.NM = e->NM;
+  m.dtb = p5_dt_bf16(e->cfg.num_steps);
+  const int ntiles = (e->P + AttnTcCfg::KT - 1) / AttnTcCfg::KT + (H + AttnTcCfg::KT - 1) / AttnTcCfg::KT;
+  m.attn_tps = std::max(1, (ntiles + 8) / 9);
+  m.attn_splits = (ntiles + m.attn_tps - 1) / m.attn_tps;
+  if ((size_t)m.attn_splits * H * 8 > e->attn_ws_rows || (size_t)mg_units(MG_O) * 128 * 64 * 4 > e->gemm_ws_bytes)
+    return set_err(e, "persistent denoise: workspace too small");
+  CK(cudaMemsetAsync(e->mega_ctr, 0, MG_NCTR * 4, e->stream));
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(e->num_sms);
+  lc.blockDim = dim3(C::THREADS);
+  lc.dynamicSmemBytes = C::SMEM;
+  lc.stream = e->stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the grid-wide barriers rely on it
+  at[0].val.cooperative = 1;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&lc, denoise_mega_kernel, m));
+  e->launches++;
+  return true;
+}
+
 bool run_denoise_body(pi05_engine* e, int n) {
+  if (mega_applies(e, n)) return run_denoise_mega(e);
   const int H = e->cfg.horizon, T = n * H, D = P5_EXP_W, P = e->P;
   Acts& A = e->A;
   const size_t cache_layer = (size_t)e->max_batch * P * P5_HD;
@@ -1038,6 +1162,7 @@ bool create(pi05_engine* e) {
   if (const char* s = getenv("PI05_PDL")) e->pdl = atoi(s) != 0;
   if (const char* s = getenv("PI05_CLUSTER_SPLITK")) e->cluster_splitk = atoi(s) != 0;
   if (const char* s = getenv("PI05_ATTN_TC")) e->attn_tc = atoi(s) != 0;
+  if (const char* s = getenv("PI05_MEGA")) e->mega = atoi(s) != 0;
   CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   cudaDriverEntryPointQueryResult q;
   void* fn = nullptr;
@@ -1053,6 +1178,7 @@ bool create(pi05_engine* e) {
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_HD, 8>::SMEM));
   CK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcCfg::SMEM));
+  CK(cudaFuncSetAttribute(denoise_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MegaCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_SIG_HD, 4>::SMEM));
   CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1185,6 +1311,7 @@ int pi05_init_random_weights(pi05_engine* e, uint64_t seed) {
   cudaSetDevice(e->device);
   if (!init_random(e, seed)) return fail_code(e);
   e->weights_ready = true;
+  ++e->wgen;  // weight-derived copies (the persistent denoise's q/k/v row permutation) are stale
   e->prefix_n = 0;
   return PI05_OK;
 }
@@ -1291,6 +1418,7 @@ int pi05_load_weights(pi05_engine* e, const char* path) {
   fclose(f);
   if (!build_mods(e)) return fail_code(e);
   e->weights_ready = true;
+  ++e->wgen;  // weight-derived copies (the persistent denoise's q/k/v row permutation) are stale
   e->prefix_n = 0;
   return PI05_OK;
 }
@@ -1371,6 +1499,7 @@ int pi05_denoise(pi05_engine* e, int n, const float* noise, float* actions) {
   cudaSetDevice(e->device);
   const size_t bytes = (size_t)n * e->cfg.horizon * P5_ACT_D * 4;
   if (!copy_in(e, e->A.xt, noise, bytes)) return PI05_ERR_CUDA;
+  if (mega_applies(e, n) && !mega_prepare(e)) return fail_code(e);
   if (!run_graph(e, e->denoise_graphs, e->denoise_launches, n, run_denoise_body)) return fail_code(e);
   if (cudaMemcpyAsync(actions, e->A.xt, bytes, cudaMemcpyDefault, e->stream) != cudaSuccess) return PI05_ERR_CUDA;
   if (!is_device_ptr(actions)) return pi05_sync(e);

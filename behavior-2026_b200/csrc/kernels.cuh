@@ -206,11 +206,25 @@ __global__ void action_in_kernel(const float* xt, const bf16* W, const bf16* b, 
   pdl_wait();
   if (idx >= (long)T * D) return;
   const int t = (int)(idx / D), o = (int)(idx % D);
-  const float* x = xt + (long)t * P5_ACT_D;
-  const bf16* w = W + (long)o * P5_ACT_D;
+  // vector loads of the thread's weight row (64 B) and its token's state row (128 B); the sum still
+  // runs over k in order
+  const float4* x = reinterpret_cast<const float4*>(xt + (long)t * P5_ACT_D);
+  const uint4* w = reinterpret_cast<const uint4*>(W + (long)o * P5_ACT_D);
   float acc = 0.f;
 #pragma unroll
-  for (int k = 0; k < P5_ACT_D; ++k) acc += x[k] * bf(w[k]);
+  for (int q = 0; q < P5_ACT_D / 8; ++q) {
+    float wf[8];
+    unpack8(w[q], wf);
+    const float4 x0 = x[2 * q], x1 = x[2 * q + 1];
+    acc += x0.x * wf[0];
+    acc += x0.y * wf[1];
+    acc += x0.z * wf[2];
+    acc += x0.w * wf[3];
+    acc += x1.x * wf[4];
+    acc += x1.y * wf[5];
+    acc += x1.z * wf[6];
+    acc += x1.w * wf[7];
+  }
   y[idx] = tobf(acc + bf(b[o]));
   pdl_launch_dependents();
 }

@@ -156,7 +156,8 @@ def test_prefix_cache_and_actions_reduced_depth(pn, oracle):
 
 
 def test_batch_equals_single(pn):
-    """Batch API at n=4 returns, per sample, the bits of n=1 calls (reference batch_test, π05 record :300)."""
+    """Batch API at n=4 returns, per sample, what n=1 calls return (reference batch_test, π05 record :300);
+    n=1 runs the persistent denoise kernel, n=4 the per-kernel path, so the match is to 1e-2."""
     cfg = pn.Config.make(siglip_layers=1, gemma_layers=2, num_steps=2)
     eng = pn.Engine(cfg, max_batch=4)
     eng.init_random_weights(2)
@@ -167,3 +168,27 @@ def test_batch_equals_single(pn):
     for i in range(4):
         one = eng.infer(imgs[i:i + 1], toks[i:i + 1], noise[i:i + 1])[0]
         np.testing.assert_allclose(one, batch[i], rtol=0, atol=1e-2)
+
+
+@pytest.mark.parametrize("layers,steps", [(18, 10), (3, 2)])
+def test_persistent_denoise_matches_per_kernel_path(pn, monkeypatch, layers, steps):
+    """The one-sample denoise runs as one persistent kernel; it must agree with the per-kernel path
+    (same rounding points, sums in a different order) and be bit-identical from call to call."""
+    cfg = pn.Config.make(siglip_layers=0, gemma_layers=layers, num_steps=steps)  # expert depth = gemma depth
+    noise = pn.synth_noise(3, 0)
+    out = {}
+    for mega in ("1", "0"):
+        monkeypatch.setenv("PI05_MEGA", mega)
+        eng = pn.Engine(cfg, max_batch=1)
+        eng.init_random_weights(4)
+        eng.synth_prefix_cache(1, seed=4)
+        out[mega] = eng.denoise(noise[None])[0]
+        if mega == "1":
+            assert eng.graph_launches("denoise", 1) == 1  # one kernel for the whole chunk
+            again = eng.denoise(noise[None])[0]
+            assert np.array_equal(again, out[mega])
+        else:
+            assert eng.graph_launches("denoise", 1) > 1
+    a, b = out["1"], out["0"]
+    assert np.isfinite(a).all()
+    assert np.abs(a - b).max() <= 1e-2 and cos(a, b) >= 0.9999, (np.abs(a - b).max(), cos(a, b))
