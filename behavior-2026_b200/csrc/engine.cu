@@ -408,6 +408,7 @@ bool linear(pi05_engine* e, const Lin& L) {
   int BN;
   CUtensorMap ta, tb;
   const int kt = (L.K + 63) / 64;
+  int nsplit = 0;  // > 0: split count chosen with the tile width (non-swapped orientation)
   if (L.F <= 48 && !swap) {
     // small-N GEMMs of the LoRA path: U = x A^T, V = dy B, and the weight gradients (N = 16 per adapter)
     BN = (L.F + 15) / 16 * 16;
@@ -431,8 +432,21 @@ bool linear(pi05_engine* e, const Lin& L) {
     ga.tiles_n = 1;
     if (!make_tmap(e, &ta, L.w, L.F, L.K, L.ldw, 128) || !make_tmap(e, &tb, L.x, L.T, L.K, L.ldx, BN)) return false;
   } else {
+    // Measured on B200: the mainloop is bound by L2->shared-memory bandwidth, and a 128x256 tile
+    // loads 25% fewer bytes per MAC than 128x128, so BN=256 wins unless it leaves more than half of
+    // the SMs idle.  Split-K (partials through global memory) only pays for long K with few tiles.
     const int tm = (L.T + 127) / 128;
-    BN = (tm * ((L.F + 255) / 256) >= 2 * e->num_sms) ? 256 : 128;
+    const int t256 = tm * ((L.F + 255) / 256);
+    if (t256 >= e->num_sms / 2) {
+      BN = 256;
+      nsplit = 1;
+    } else if (kt >= 128 && 2 * t256 <= e->num_sms) {
+      BN = 256;
+      nsplit = 2;
+    } else {
+      BN = 128;
+      nsplit = 1;
+    }
     ga.M = L.T;
     ga.N = L.F;
     ga.tiles_m = tm;
@@ -446,7 +460,10 @@ bool linear(pi05_engine* e, const Lin& L) {
   ga.group_m = swap ? 1 : std::max(1, std::min(ga.tiles_m, (int)((48ull << 20) / (128ull * L.K * 2))));
   const int tiles = ga.tiles_m * ga.tiles_n;
   int splits = 1;
-  if (tiles < e->num_sms && kt >= 4) {
+  if (nsplit > 0) {
+    splits = nsplit;
+    while (splits > 1 && ((size_t)splits * tiles * 128 * BN * 4 > e->gemm_ws_bytes || tiles > e->n_counters)) --splits;
+  } else if (tiles < e->num_sms && kt >= 4) {
     splits = std::max(1, std::min(e->num_sms / tiles, kt / 2));
     const size_t need = (size_t)splits * tiles * 128 * BN * 4;
     while (splits > 1 && ((size_t)splits * tiles * 128 * BN * 4 > e->gemm_ws_bytes || tiles > e->n_counters)) --splits;

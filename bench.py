@@ -265,12 +265,14 @@ def gemm_roofline(pn, eng, M, N, K, epi, reps=5):
     x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
     w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16()
     out = torch.empty(M, N // 2 if epi == "geglu" else N, device="cuda", dtype=torch.bfloat16)
+    res = torch.randn(M, N, device="cuda", generator=g).bfloat16() if epi in ("resid", "gated") else None
+    gate = torch.randn(N, device="cuda", generator=g).bfloat16() if epi == "gated" else None
     torch.cuda.synchronize()
     for _ in range(2):
-        eng.op_linear(x, w, out, epi)
-    total, per = timed(eng, lambda: eng.op_linear(x, w, out, epi), reps)
+        eng.op_linear(x, w, out, epi, res=res, gate=gate)
+    total, per = timed(eng, lambda: eng.op_linear(x, w, out, epi, res=res, gate=gate), reps)
     ms = total / reps
-    del x, w, out
+    del x, w, out, res, gate
     torch.cuda.empty_cache()
     return ms
 
