@@ -1190,6 +1190,7 @@ bool create(pi05_engine* e) {
   if (!set_gemm_smem<64>(e) || !set_gemm_smem<128>(e) || !set_gemm_smem<256>(e)) return false;
   if (!set_gemm_smem_small<16>(e) || !set_gemm_smem_small<32>(e) || !set_gemm_smem_small<48>(e)) return false;
   if (!set_swap_cluster_smem<64>(e) || !set_swap_cluster_smem<128>(e)) return false;
+
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_HD, 4>::SMEM));
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,

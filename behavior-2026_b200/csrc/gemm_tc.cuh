@@ -552,19 +552,83 @@ __global__ void __launch_bounds__(256, 1)
 // [r*128/S, (r+1)*128/S) by reading the S partials over distributed shared memory in rank order
 // (deterministic), applies the epilogue and stores.  The partials never leave the chip and the
 // reduction is spread over all S CTAs instead of the last one.
+
+// Epilogue operands of one reduce item (weight row f, tokens t0..t0+3), loaded from global memory
+// before the partial sums are: they do not depend on them.
+struct SwapEpiOps {
+  float bias, res[4], gate[4];
+};
 template <int EPI>
-__device__ __forceinline__ float epi_swap_value(const GemmArgs& a, float v, int f, int t) {
-  float x = v * a.out_scale + (a.bias ? bf(a.bias[f]) : 0.f);
+__device__ __forceinline__ void swap_epi_load(const GemmArgs& a, int f, int t0, SwapEpiOps& o) {
+  o.bias = (f < a.M && a.bias) ? bf(a.bias[f]) : 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int t = t0 + q;
+    const bool valid = f < a.M && t < a.N;
+    o.res[q] = ((EPI == EPI_RESID || EPI == EPI_GATED) && valid) ? bf(a.res[(size_t)t * a.ld_res + f]) : 0.f;
+    o.gate[q] = (EPI == EPI_GATED && valid) ? bf(a.gate[(size_t)(t / a.gate_div) * a.ld_gate + f]) : 0.f;
+  }
+}
+template <int EPI>
+__device__ __forceinline__ float swap_epi_value(const GemmArgs& a, float v, const SwapEpiOps& o, int q) {
+  const float x = v * a.out_scale + o.bias;
   if (EPI == EPI_F32) return x;
   if (EPI == EPI_GELU) return gelu_tanh(rbf(x));
-  if (EPI == EPI_RESID) return bf(a.res[(size_t)t * a.ld_res + f]) + rbf(x);
-  if (EPI == EPI_GATED)
-    return bf(a.res[(size_t)t * a.ld_res + f]) + rbf(rbf(x) * bf(a.gate[(size_t)(t / a.gate_div) * a.ld_gate + f]));
+  if (EPI == EPI_RESID) return o.res[q] + rbf(x);
+  if (EPI == EPI_GATED) return o.res[q] + rbf(rbf(x) * o.gate[q]);
   return x;
 }
 
+// Cluster reduce of a swap-orientation tile: CTA `rank` of S owns rows [rank*R, rank*R+R), R = 128/S.
+// Items = (row, group of 4 tokens); consecutive threads take consecutive weight rows of one group, so
+// the stores of each token are contiguous across the warp (R*BN/4 is a multiple of 128).  An item's
+// epilogue operands (bias, residual, gate) are loaded from global memory before, and in flight with,
+// its S partial loads; the partials are summed in rank order (deterministic).  Measured in the
+// denoise graph: batching more items per pass, or fetching operands before the cluster barrier, costs
+// more (registers, and the next kernel's early start under programmatic dependent launch) than it saves.
+template <int BN, int EPI, int S>
+__device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_base, int rank, int m0, int rtid) {
+  constexpr int R = 128 / S, RED_LD = BN + 4, ITEMS = R * (BN / 4);
+#pragma unroll 1
+  for (int it = rtid; it < ITEMS; it += 128) {
+    const int lr = it % R, cg = it / R;
+    const int f = m0 + rank * R + lr;
+    SwapEpiOps o;
+    swap_epi_load<EPI>(args, f, cg * 4, o);
+    const uint32_t addr = red_base + (uint32_t)((rank * R + lr) * RED_LD + cg * 4) * 4u;
+    float4 pv[S];
+#pragma unroll
+    for (int p = 0; p < S; ++p) pv[p] = ld_peer_v4(map_peer(addr, (uint32_t)p));
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int p = 0; p < S; ++p) {
+      v[0] += pv[p].x;
+      v[1] += pv[p].y;
+      v[2] += pv[p].z;
+      v[3] += pv[p].w;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int t = cg * 4 + q;
+      const bool valid = f < args.M && t < args.N;
+      if (EPI == EPI_GEGLU) {
+        // rows (2j, 2j+1) = (gate_j, up_j) sit in neighbouring lanes (R is even)
+        const float mine = rbf(v[q] * args.out_scale + o.bias);
+        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+        if (valid && (f & 1) == 0) args.out[(size_t)t * args.ld_out + f / 2] = tobf(rbf(gelu_tanh(mine)) * other);
+      } else if (valid) {
+        const float x = swap_epi_value<EPI>(args, v[q], o, q);
+        if (EPI == EPI_F32)
+          args.out_f32[(size_t)t * args.ld_out_f32 + f] = x;
+        else
+          args.out[(size_t)t * args.ld_out + f] = tobf(x);
+      }
+    }
+  }
+}
+
 template <int BN, int EPI>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(256, 2)
     gemm_swap_cluster_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                              const GemmArgs args) {
   using C = GemmCfg<BN>;
@@ -677,46 +741,13 @@ __global__ void __launch_bounds__(256, 1)
 
   if (warp >= 4) {
     if (args.pdl) pdl_wait();
-    const int R = C::BM / S;  // rows this CTA reduces
-    const int tid = threadIdx.x - 128;
+    const int rtid = threadIdx.x - 128;
     const uint32_t red_base = smem_u32(red);
-    // items = (row, group of 4 tokens); consecutive threads take consecutive weight rows of one group,
-    // so the stores of each token are contiguous across the warp.  R*BN/4 is a multiple of 128.
-    for (int it = tid; it < R * (BN / 4); it += 128) {
-      const int lr = it % R, cg = it / R;
-      const int row = rank * R + lr;
-      const uint32_t addr = red_base + (uint32_t)(row * RED_LD + cg * 4) * 4u;
-      float4 pv[8];
-#pragma unroll
-      for (int p = 0; p < 8; ++p)  // all peers' loads in flight before the first add
-        pv[p] = p < S ? ld_peer_v4(map_peer(addr, (uint32_t)p)) : make_float4(0.f, 0.f, 0.f, 0.f);
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int p = 0; p < 8; ++p) {  // rank order: deterministic
-        v[0] += pv[p].x;
-        v[1] += pv[p].y;
-        v[2] += pv[p].z;
-        v[3] += pv[p].w;
-      }
-      const int f = m0 + row;
-      const float bias = (f < args.M && args.bias) ? bf(args.bias[f]) : 0.f;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int t = cg * 4 + q;
-        const bool valid = f < args.M && t < args.N;
-        if (EPI == EPI_GEGLU) {
-          // rows (2j, 2j+1) = (gate_j, up_j) sit in neighbouring lanes (R is even)
-          const float mine = rbf(v[q] * args.out_scale + bias);
-          const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
-          if (valid && (f & 1) == 0) args.out[(size_t)t * args.ld_out + f / 2] = tobf(rbf(gelu_tanh(mine)) * other);
-        } else if (valid) {
-          const float x = epi_swap_value<EPI>(args, v[q], f, t);
-          if (EPI == EPI_F32)
-            args.out_f32[(size_t)t * args.ld_out_f32 + f] = x;
-          else
-            args.out[(size_t)t * args.ld_out + f] = tobf(x);
-        }
-      }
+    switch (S) {
+      case 2: swap_reduce<BN, EPI, 2>(args, red_base, rank, m0, rtid); break;
+      case 4: swap_reduce<BN, EPI, 4>(args, red_base, rank, m0, rtid); break;
+      case 8: swap_reduce<BN, EPI, 8>(args, red_base, rank, m0, rtid); break;
+      default: swap_reduce<BN, EPI, 1>(args, red_base, rank, m0, rtid); break;
     }
   }
   cluster_sync();  // peers are done reading this CTA's partial tile
