@@ -13,8 +13,8 @@
 // with the accumulator in TMEM): a unit = (row tile, K split); each CTA computes one unit's partial
 // tile, the S CTAs of a tile meet at a counter in global memory, and each reduces 1/S of the tile's
 // outputs over the S partials in split order (deterministic) and applies the phase's epilogue:
-//   QKV  F=2560 K=1024 S=6   rows of each 256-wide head permuted so a tile holds both halves of its
-//                            RoPE pairs (i, i+128): RoPE, q*1/16 and the K/V writes happen in the reduce
+//   QKV  F=2560 K=1024 S=6   rows of each 256-wide head interleaved (2j = dim j, 2j+1 = dim j+128), so a
+//                            tile holds both halves of its RoPE pairs: RoPE, q*1/16 and K/V writes in the reduce
 //   O    F=1024 K=2048 S=16  x += R(R(acc) * gate1)
 //   GU   F=8192 K=1024 S=2   interleaved gate/up rows: act = R(R(gelu(R(g))) * R(u))
 //   DN   F=1024 K=4096 S=16  x += R(R(acc) * gate2)
@@ -314,13 +314,13 @@ struct MegaCtx {
     const float* part = a.ws + (size_t)tile * S * 128 * 64;
     const int T = a.T;
     if (P == MG_QKV) {
-      // pairs (r, r+64) of the permuted tile = head dims (j, j+128), j = (tile % 2) * 64 + r
+      // rows (2r, 2r+1) of the interleaved tile = head dims (j, j+128), j = (tile % 2) * 64 + r
       const int n = 64 * T, i0 = split * n / S, i1 = (split + 1) * n / S;
       const int hb = tile >> 1, j0 = (tile & 1) * 64;
       for (int i = i0 + tid; i < i1; i += C::THREADS) {
         const int r = i / T, t = i % T, j = j0 + r;
         float v0, v1;
-        psum2<S>(part, r, r + 64, t, v0, v1);
+        psum2<S>(part, 2 * r, 2 * r + 1, t, v0, v1);
         const float x1 = rbf(v0), x2 = rbf(v1);
         if (hb == 9) {
           a.ev[(long)t * P5_HD + j] = tobf(x1);
@@ -555,12 +555,12 @@ __global__ void __launch_bounds__(MegaCfg::THREADS, 1) denoise_mega_kernel(const
   }
 }
 
-// Row permutation of the q/k/v weight for the kernel above: tile t (128 rows) of head block hb = t/2
-// holds head dims [64a, 64a+64) then [128+64a, 128+64a+64) of that head, a = t % 2.
-__global__ void permute_qkv_rows_kernel(const bf16* src, bf16* dst) {
+// Row interleaving of the q/k/v weight for the fused-RoPE projections: within each 256-row head
+// block, row 2j takes head dim j and row 2j+1 head dim j+128.
+__global__ void interleave_qkv_rows_kernel(const bf16* src, bf16* dst) {
   const int drow = blockIdx.x;  // 0..2559
-  const int tile = drow >> 7, r = drow & 127, hb = tile >> 1, half = tile & 1;
-  const int srow = hb * 256 + (r < 64 ? half * 64 + r : 128 + half * 64 + (r - 64));
+  const int hb = drow >> 8, w = drow & 255;
+  const int srow = hb * 256 + (w >> 1) + (w & 1) * 128;
   const uint4* s = reinterpret_cast<const uint4*>(src + (long)srow * P5_EXP_W);
   uint4* d = reinterpret_cast<uint4*>(dst + (long)drow * P5_EXP_W);
   for (int i = threadIdx.x; i < P5_EXP_W / 8; i += blockDim.x) d[i] = s[i];

@@ -96,8 +96,9 @@ struct pi05_engine {
   // persistent one-sample denoise (denoise_mega.cuh), opt-in with PI05_MEGA=1: it matches the
   // per-kernel CUDA-graph path (~12 ms per 10-step chunk) but does not beat it yet
   bool mega = false;
-  int mega_wgen = -1;
-  bf16* mega_wqkv = nullptr;
+  // expert q/k/v weights with interleaved head rows (fused-RoPE projections), rebuilt when stale
+  int qkv_il_wgen = -1;
+  bf16* exp_wqkv_il = nullptr;
   CUtensorMap* mega_maps = nullptr;
   unsigned* mega_ctr = nullptr;
   int prefix_n = 0;  // batch whose prefix cache is valid
@@ -296,6 +297,12 @@ struct Lin {
   int ld_out_t = 0;
   int lg_mode = 0, lg_trans = 0, lg_K = 0;
   long lg_off[3] = {0, 0, 0};
+  // EPI_ROPE (few-token q/k/v projection with interleaved head rows; see GemmArgs rope_*)
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int rope_pos_off = 0, rope_per_sample = 1, rope_ld_kv = 0;
+  bf16* rope_k = nullptr;
+  bf16* rope_v = nullptr;
 };
 
 template <int BN>
@@ -346,6 +353,7 @@ bool launch_swap_cluster(pi05_engine* e, const CUtensorMap& ta, const CUtensorMa
     case EPI_RESID: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_RESID>, grid, dim3(256), sm, S, p, ta, tb, ga);
     case EPI_GATED: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_GATED>, grid, dim3(256), sm, S, p, ta, tb, ga);
     case EPI_GEGLU: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_GEGLU>, grid, dim3(256), sm, S, p, ta, tb, ga);
+    case EPI_ROPE: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_ROPE>, grid, dim3(256), sm, S, p, ta, tb, ga);
     case EPI_F32: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_F32>, grid, dim3(256), sm, S, p, ta, tb, ga);
     default: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_STORE>, grid, dim3(256), sm, S, p, ta, tb, ga);
   }
@@ -359,6 +367,7 @@ bool set_swap_cluster_smem(pi05_engine* e) {
   CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_GEGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   return true;
 }
@@ -494,6 +503,13 @@ bool linear(pi05_engine* e, const Lin& L) {
   ga.pdl = e->pdl ? 1 : 0;
   ga.out_t = L.out_t;
   ga.ld_out_t = L.ld_out_t;
+  ga.rope_cos = L.rope_cos;
+  ga.rope_sin = L.rope_sin;
+  ga.rope_pos_off = L.rope_pos_off;
+  ga.rope_per_sample = L.rope_per_sample;
+  ga.rope_ld_kv = L.rope_ld_kv;
+  ga.rope_k = L.rope_k;
+  ga.rope_v = L.rope_v;
   ga.lg_mode = L.lg_mode;
   ga.lg_trans = L.lg_trans;
   ga.lg_K = L.lg_K;
@@ -509,6 +525,7 @@ bool linear(pi05_engine* e, const Lin& L) {
       return BN == 64 ? launch_swap_cluster<64>(e, ta, tb, ga, S) : launch_swap_cluster<128>(e, ta, tb, ga, S);
     }
   }
+  if (L.epi == EPI_ROPE) return set_err(e, "fused RoPE epilogue needs the few-token cluster path");
   if (BN == 16) return launch_gemm_small<16>(e, ta, tb, ga, L.amn);
   if (BN == 32) return launch_gemm_small<32>(e, ta, tb, ga, L.amn);
   if (BN == 48) return launch_gemm_small<48>(e, ta, tb, ga, L.amn);
@@ -791,16 +808,35 @@ bool mega_applies(pi05_engine* e, int n) {
          e->num_sms >= attn_units + 1 && e->P > 0;
 }
 
-// Buffers, tensor-map table and the q/k/v row permutation of the persistent denoise (re-permuted
-// whenever the weights changed).  Runs outside stream capture.
+// Expert q/k/v weights with interleaved head rows for the fused-RoPE projections, rebuilt whenever
+// the weights changed.  Runs outside stream capture.
+bool qkv_interleave_prepare(pi05_engine* e) {
+  const int L = e->cfg.expert_layers;
+  const size_t wq = (size_t)P5_QKV * P5_EXP_W;
+  if (!e->exp_wqkv_il && !dalloc(e, (void**)&e->exp_wqkv_il, (size_t)std::max(L, 1) * wq * 2)) return false;
+  if (e->qkv_il_wgen != e->wgen) {
+    for (int l = 0; l < L; ++l)
+      if (!launch(e, interleave_qkv_rows_kernel, dim3(P5_QKV), dim3(128), 0, false, (const bf16*)e->ex[l].wqkv,
+                  e->exp_wqkv_il + l * wq))
+        return false;
+    e->qkv_il_wgen = e->wgen;
+  }
+  return true;
+}
+
+// The q/k/v projection of a denoise with n samples runs with RoPE fused when its few tokens take the
+// on-chip cluster split-K path.
+bool fused_rope_applies(pi05_engine* e, int n) { return e->cluster_splitk && n * e->cfg.horizon <= 64; }
+
+// Buffers and tensor-map table of the persistent denoise.  Runs outside stream capture.
 bool mega_prepare(pi05_engine* e) {
   using C = MegaCfg;
   const int L = e->cfg.expert_layers, H = e->cfg.horizon, P = e->P;
   const size_t wq = (size_t)P5_QKV * P5_EXP_W;
   const int nmaps = L * C::NMAPS_LAYER + 5;
-  if (!e->mega_wqkv) {
-    if (!dalloc(e, (void**)&e->mega_wqkv, (size_t)L * wq * 2) ||
-        !dalloc(e, (void**)&e->mega_maps, (size_t)nmaps * sizeof(CUtensorMap)) ||
+  if (!qkv_interleave_prepare(e)) return false;
+  if (!e->mega_maps) {
+    if (!dalloc(e, (void**)&e->mega_maps, (size_t)nmaps * sizeof(CUtensorMap)) ||
         !dalloc(e, (void**)&e->mega_ctr, MG_NCTR * 4))
       return false;
     Acts& A = e->A;
@@ -815,7 +851,7 @@ bool mega_prepare(pi05_engine* e) {
     for (int l = 0; l < L; ++l) {
       CUtensorMap* t = &m[(size_t)l * C::NMAPS_LAYER];
       const ExpLayer& x = e->ex[l];
-      if (!make_tmap(e, t + 0, e->mega_wqkv + l * wq, P5_QKV, P5_EXP_W, P5_EXP_W, 128) ||
+      if (!make_tmap(e, t + 0, e->exp_wqkv_il + l * wq, P5_QKV, P5_EXP_W, P5_EXP_W, 128) ||
           !make_tmap(e, t + 1, x.wo, P5_EXP_W, P5_QDIM, P5_QDIM, 128) ||
           !make_tmap(e, t + 2, x.wgu, 2 * P5_EXP_MLP, P5_EXP_W, P5_EXP_W, 128) ||
           !make_tmap(e, t + 3, x.wd, P5_EXP_W, P5_EXP_MLP, P5_EXP_MLP, 128) ||
@@ -833,13 +869,6 @@ bool mega_prepare(pi05_engine* e) {
         !make_tmap_box(e, g + 4, A.eact, H, P5_EXP_MLP, P5_EXP_MLP, 64, 64))
       return false;
     CK(cudaMemcpyAsync(e->mega_maps, m.data(), m.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, e->stream));
-  }
-  if (e->mega_wgen != e->wgen) {
-    for (int l = 0; l < L; ++l)
-      if (!launch(e, permute_qkv_rows_kernel, dim3(P5_QKV), dim3(128), 0, false, (const bf16*)e->ex[l].wqkv,
-                  e->mega_wqkv + l * wq))
-        return false;
-    e->mega_wgen = e->wgen;
   }
   return true;
 }
@@ -915,13 +944,28 @@ bool run_denoise_body(pi05_engine* e, int n) {
       const bf16* m2 = mrow + (size_t)(2 * l + 1) * 3 * D;
       if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m1, m1 + D, T, D, 1, 0, D))
         return false;
-      Lin q{A.eh, D, T, x.wqkv, D, P5_QKV, D};
-      q.out = A.eqkv;
-      q.ld_out = P5_QKV;
-      if (!linear(e, q)) return false;
-      if (!launch(e, rope_qkv_kernel, dim3(T), dim3(256), 0, true, A.eqkv, T, H, P, A.ek, A.ev, (const float*)e->d_cos,
-                  (const float*)e->d_sin, 256))
-        return false;
+      if (fused_rope_applies(e, n)) {
+        Lin q{A.eh, D, T, e->exp_wqkv_il + (size_t)l * P5_QKV * D, D, P5_QKV, D};
+        q.epi = EPI_ROPE;
+        q.out = A.eqkv;
+        q.ld_out = P5_QKV;
+        q.rope_cos = e->d_cos;
+        q.rope_sin = e->d_sin;
+        q.rope_pos_off = P;
+        q.rope_per_sample = H;
+        q.rope_ld_kv = P5_HD;
+        q.rope_k = A.ek;
+        q.rope_v = A.ev;
+        if (!linear(e, q)) return false;
+      } else {
+        Lin q{A.eh, D, T, x.wqkv, D, P5_QKV, D};
+        q.out = A.eqkv;
+        q.ld_out = P5_QKV;
+        if (!linear(e, q)) return false;
+        if (!launch(e, rope_qkv_kernel, dim3(T), dim3(256), 0, true, A.eqkv, T, H, P, A.ek, A.ev,
+                    (const float*)e->d_cos, (const float*)e->d_sin, 256))
+          return false;
+      }
       AttnArgs at = {};
       at.q = A.eqkv;
       at.ldq = P5_QKV;
@@ -1518,6 +1562,7 @@ int pi05_denoise(pi05_engine* e, int n, const float* noise, float* actions) {
   const size_t bytes = (size_t)n * e->cfg.horizon * P5_ACT_D * 4;
   if (!copy_in(e, e->A.xt, noise, bytes)) return PI05_ERR_CUDA;
   if (mega_applies(e, n) && !mega_prepare(e)) return fail_code(e);
+  if (fused_rope_applies(e, n) && !qkv_interleave_prepare(e)) return fail_code(e);
   if (!run_graph(e, e->denoise_graphs, e->denoise_launches, n, run_denoise_body)) return fail_code(e);
   if (cudaMemcpyAsync(actions, e->A.xt, bytes, cudaMemcpyDefault, e->stream) != cudaSuccess) return PI05_ERR_CUDA;
   if (!is_device_ptr(actions)) return pi05_sync(e);

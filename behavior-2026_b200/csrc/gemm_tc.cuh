@@ -31,6 +31,9 @@ enum EpiKind : int {
   // small-N epilogues of the LoRA path (normal orientation, BN <= 48)
   EPI_STORE_T = 6,    // x = R(v*out_scale): out[t][f] = x and out_t[f][t] = x (transposed copy)
   EPI_LORA_GRAD = 7,  // fp32 gradient accumulate: D[m][c] with adapter c/16 (see GemmArgs lg_*)
+  // few-token q/k/v projection (swap orientation, cluster reduce) with RoPE fused: the weight rows of
+  // each 256-wide head are interleaved (row 2j = dim j, row 2j+1 = dim j+128), see GemmArgs rope_*
+  EPI_ROPE = 8,
 };
 // v = acc * out_scale + bias[f] + addend[(t % add_mod)][f]
 
@@ -67,6 +70,15 @@ struct GemmArgs {
   // (2048 | 256 | 256); 2 interleaved gate/up rows (a = m % 2, r_a = m / 2).
   int lg_mode, lg_trans, lg_K;
   long lg_off[3];
+  // EPI_ROPE: token t sits at position rope_pos_off + t % rope_per_sample.  Head blocks 0..7 (q):
+  //   out[t][hb*256 + j], [.. + 128] = R(R(rope) / 16); block 8 (k): rope_k[t][j], [j+128] = R(rope);
+  //   block 9 (v): rope_v[t][j], [j+128] = R(v).  rope(x1, x2) = (x1 cos - x2 sin, x2 cos + x1 sin),
+  //   x1 = R(acc of dim j), x2 = R(acc of dim j+128), cos/sin tables [pos][128].
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_pos_off, rope_per_sample, rope_ld_kv;
+  bf16* rope_k;
+  bf16* rope_v;
 };
 
 template <int BN>
@@ -565,6 +577,12 @@ __device__ __forceinline__ void swap_epi_load(const GemmArgs& a, int f, int t0, 
   for (int q = 0; q < 4; ++q) {
     const int t = t0 + q;
     const bool valid = f < a.M && t < a.N;
+    if (EPI == EPI_ROPE) {  // res, gate carry cos, sin of the token's position for this row pair
+      const size_t ci = (size_t)(a.rope_pos_off + t % a.rope_per_sample) * 128 + ((f & 255) >> 1);
+      o.res[q] = valid ? a.rope_cos[ci] : 0.f;
+      o.gate[q] = valid ? a.rope_sin[ci] : 0.f;
+      continue;
+    }
     o.res[q] = ((EPI == EPI_RESID || EPI == EPI_GATED) && valid) ? bf(a.res[(size_t)t * a.ld_res + f]) : 0.f;
     o.gate[q] = (EPI == EPI_GATED && valid) ? bf(a.gate[(size_t)(t / a.gate_div) * a.ld_gate + f]) : 0.f;
   }
@@ -616,6 +634,28 @@ __device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_b
         const float mine = rbf(v[q] * args.out_scale + o.bias);
         const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
         if (valid && (f & 1) == 0) args.out[(size_t)t * args.ld_out + f / 2] = tobf(rbf(gelu_tanh(mine)) * other);
+      } else if (EPI == EPI_ROPE) {
+        // rows (2j, 2j+1) of a head block = dims (j, j+128), in neighbouring lanes
+        const float mine = rbf(v[q]);
+        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+        if (valid && (f & 1) == 0) {
+          const int hb = f >> 8, j = (f & 255) >> 1;
+          if (hb == 9) {
+            args.rope_v[(size_t)t * args.rope_ld_kv + j] = tobf(mine);
+            args.rope_v[(size_t)t * args.rope_ld_kv + j + 128] = tobf(other);
+          } else {
+            const float cs = o.res[q], sn = o.gate[q];
+            const float ra = rbf(mine * cs - other * sn);
+            const float rc = rbf(other * cs + mine * sn);
+            if (hb == 8) {
+              args.rope_k[(size_t)t * args.rope_ld_kv + j] = tobf(ra);
+              args.rope_k[(size_t)t * args.rope_ld_kv + j + 128] = tobf(rc);
+            } else {
+              args.out[(size_t)t * args.ld_out + hb * 256 + j] = tobf(ra * 0.0625f);
+              args.out[(size_t)t * args.ld_out + hb * 256 + j + 128] = tobf(rc * 0.0625f);
+            }
+          }
+        }
       } else if (valid) {
         const float x = swap_epi_value<EPI>(args, v[q], o, q);
         if (EPI == EPI_F32)
