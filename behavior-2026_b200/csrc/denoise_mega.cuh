@@ -555,15 +555,15 @@ __global__ void __launch_bounds__(MegaCfg::THREADS, 1) denoise_mega_kernel(const
   }
 }
 
-// Row interleaving of the q/k/v weight for the fused-RoPE projections: within each 256-row head
-// block, row 2j takes head dim j and row 2j+1 head dim j+128.
-__global__ void interleave_qkv_rows_kernel(const bf16* src, bf16* dst) {
+// Row interleaving of a q/k/v weight [2560][K] for the fused-RoPE projections: within each 256-row
+// head block, row 2j takes head dim j and row 2j+1 head dim j+128.
+__global__ void interleave_qkv_rows_kernel(const bf16* src, bf16* dst, int K) {
   const int drow = blockIdx.x;  // 0..2559
   const int hb = drow >> 8, w = drow & 255;
   const int srow = hb * 256 + (w >> 1) + (w & 1) * 128;
-  const uint4* s = reinterpret_cast<const uint4*>(src + (long)srow * P5_EXP_W);
-  uint4* d = reinterpret_cast<uint4*>(dst + (long)drow * P5_EXP_W);
-  for (int i = threadIdx.x; i < P5_EXP_W / 8; i += blockDim.x) d[i] = s[i];
+  const uint4* s = reinterpret_cast<const uint4*>(src + (long)srow * K);
+  uint4* d = reinterpret_cast<uint4*>(dst + (long)drow * K);
+  for (int i = threadIdx.x; i < K / 8; i += blockDim.x) d[i] = s[i];
 }
 
 }  // namespace p5

@@ -96,9 +96,10 @@ struct pi05_engine {
   // persistent one-sample denoise (denoise_mega.cuh), opt-in with PI05_MEGA=1: it matches the
   // per-kernel CUDA-graph path (~12 ms per 10-step chunk) but does not beat it yet
   bool mega = false;
-  // expert q/k/v weights with interleaved head rows (fused-RoPE projections), rebuilt when stale
+  // q/k/v weights with interleaved head rows (fused-RoPE projections), rebuilt when stale
   int qkv_il_wgen = -1;
   bf16* exp_wqkv_il = nullptr;
+  bf16* gem_wqkv_il = nullptr;
   CUtensorMap* mega_maps = nullptr;
   unsigned* mega_ctr = nullptr;
   int prefix_n = 0;  // batch whose prefix cache is valid
@@ -316,6 +317,7 @@ bool launch_gemm_bn(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb
     case EPI_RESID: return launch(e, gemm_tc_kernel<BN, EPI_RESID>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
     case EPI_GATED: return launch(e, gemm_tc_kernel<BN, EPI_GATED>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
     case EPI_GEGLU: return launch(e, gemm_tc_kernel<BN, EPI_GEGLU>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+    case EPI_ROPE: return launch(e, gemm_tc_kernel<BN, EPI_ROPE>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
     case EPI_F32: return launch(e, gemm_tc_kernel<BN, EPI_F32>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
     default: return launch(e, gemm_tc_kernel<BN, EPI_STORE>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
   }
@@ -407,6 +409,7 @@ bool set_gemm_smem(pi05_engine* e) {
   CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_GEGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   return true;
 }
@@ -525,7 +528,7 @@ bool linear(pi05_engine* e, const Lin& L) {
       return BN == 64 ? launch_swap_cluster<64>(e, ta, tb, ga, S) : launch_swap_cluster<128>(e, ta, tb, ga, S);
     }
   }
-  if (L.epi == EPI_ROPE) return set_err(e, "fused RoPE epilogue needs the few-token cluster path");
+  if (L.epi == EPI_ROPE && swap) return set_err(e, "fused RoPE epilogue: few-token projection without a cluster split");
   if (BN == 16) return launch_gemm_small<16>(e, ta, tb, ga, L.amn);
   if (BN == 32) return launch_gemm_small<32>(e, ta, tb, ga, L.amn);
   if (BN == 48) return launch_gemm_small<48>(e, ta, tb, ga, L.amn);
@@ -735,15 +738,22 @@ bool run_gemma(pi05_engine* e, int n) {
     if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.px, A.ph, g.rms1, (const bf16*)nullptr,
                 T, D, 1, 0, D))
       return false;
-    Lin q{A.ph, D, T, g.wqkv, D, P5_QKV, D};
-    q.out = A.pqkv;
-    q.ld_out = P5_QKV;
-    if (!linear(e, q)) return false;
     bf16* kc = A.kcache + l * cache_layer;
     bf16* vc = A.vcache + l * cache_layer;
-    if (!launch(e, rope_qkv_kernel, dim3(T), dim3(256), 0, true, A.pqkv, T, P, 0, kc, vc, (const float*)e->d_cos,
-                (const float*)e->d_sin, 256))
-      return false;
+    // q/k/v projection with RoPE (and the K/V cache write) in the epilogue
+    Lin q{A.ph, D, T, e->gem_wqkv_il + (size_t)l * P5_QKV * D, D, P5_QKV, D};
+    q.epi = EPI_ROPE;
+    q.no_swap = true;
+    q.out = A.pqkv;
+    q.ld_out = P5_QKV;
+    q.rope_cos = e->d_cos;
+    q.rope_sin = e->d_sin;
+    q.rope_pos_off = 0;
+    q.rope_per_sample = P;
+    q.rope_ld_kv = P5_HD;
+    q.rope_k = kc;
+    q.rope_v = vc;
+    if (!linear(e, q)) return false;
     if (l == e->cfg.gemma_layers - 1) break;  // later outputs of the last layer feed nothing
     AttnArgs at = {};
     at.q = A.pqkv;
@@ -811,22 +821,30 @@ bool mega_applies(pi05_engine* e, int n) {
 // Expert q/k/v weights with interleaved head rows for the fused-RoPE projections, rebuilt whenever
 // the weights changed.  Runs outside stream capture.
 bool qkv_interleave_prepare(pi05_engine* e) {
-  const int L = e->cfg.expert_layers;
-  const size_t wq = (size_t)P5_QKV * P5_EXP_W;
+  const int L = e->cfg.expert_layers, LG = e->cfg.gemma_layers;
+  const size_t wq = (size_t)P5_QKV * P5_EXP_W, wg = (size_t)P5_QKV * P5_GEM_W;
   if (!e->exp_wqkv_il && !dalloc(e, (void**)&e->exp_wqkv_il, (size_t)std::max(L, 1) * wq * 2)) return false;
+  if (!e->gem_wqkv_il && !dalloc(e, (void**)&e->gem_wqkv_il, (size_t)std::max(LG, 1) * wg * 2)) return false;
   if (e->qkv_il_wgen != e->wgen) {
     for (int l = 0; l < L; ++l)
       if (!launch(e, interleave_qkv_rows_kernel, dim3(P5_QKV), dim3(128), 0, false, (const bf16*)e->ex[l].wqkv,
-                  e->exp_wqkv_il + l * wq))
+                  e->exp_wqkv_il + l * wq, (int)P5_EXP_W))
+        return false;
+    for (int l = 0; l < LG; ++l)
+      if (!launch(e, interleave_qkv_rows_kernel, dim3(P5_QKV), dim3(128), 0, false, (const bf16*)e->gem[l].wqkv,
+                  e->gem_wqkv_il + l * wg, (int)P5_GEM_W))
         return false;
     e->qkv_il_wgen = e->wgen;
   }
   return true;
 }
 
-// The q/k/v projection of a denoise with n samples runs with RoPE fused when its few tokens take the
-// on-chip cluster split-K path.
-bool fused_rope_applies(pi05_engine* e, int n) { return e->cluster_splitk && n * e->cfg.horizon <= 64; }
+// The q/k/v projection of a denoise with n samples runs with RoPE fused: more than 64 tokens in the
+// normal orientation, up to 64 through the on-chip cluster split-K path.
+bool fused_rope_applies(pi05_engine* e, int n) {
+  const int T = n * e->cfg.horizon;
+  return T > 64 || e->cluster_splitk;  // > 64 tokens: normal orientation; <= 64: cluster split-K
+}
 
 // Buffers and tensor-map table of the persistent denoise.  Runs outside stream capture.
 bool mega_prepare(pi05_engine* e) {
@@ -946,6 +964,7 @@ bool run_denoise_body(pi05_engine* e, int n) {
         return false;
       if (fused_rope_applies(e, n)) {
         Lin q{A.eh, D, T, e->exp_wqkv_il + (size_t)l * P5_QKV * D, D, P5_QKV, D};
+        q.no_swap = T > 64;
         q.epi = EPI_ROPE;
         q.out = A.eqkv;
         q.ld_out = P5_QKV;
@@ -1498,6 +1517,7 @@ int pi05_prefill(pi05_engine* e, int n, const uint8_t* images, const int32_t* to
   const size_t ib = (size_t)n * e->cfg.n_cameras * P5_IMG * P5_IMG * 3;
   if (!copy_in(e, e->A.images, images, ib)) return PI05_ERR_CUDA;
   if (e->cfg.n_text > 0 && !copy_in(e, e->A.tokens, tokens, (size_t)n * e->cfg.n_text * 4)) return PI05_ERR_CUDA;
+  if (!qkv_interleave_prepare(e)) return fail_code(e);
   if (!run_graph(e, e->prefill_graphs, e->prefill_launches, n, run_prefill_body)) return fail_code(e);
   e->prefix_n = n;
   return PI05_OK;

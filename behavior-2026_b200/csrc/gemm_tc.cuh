@@ -31,8 +31,9 @@ enum EpiKind : int {
   // small-N epilogues of the LoRA path (normal orientation, BN <= 48)
   EPI_STORE_T = 6,    // x = R(v*out_scale): out[t][f] = x and out_t[f][t] = x (transposed copy)
   EPI_LORA_GRAD = 7,  // fp32 gradient accumulate: D[m][c] with adapter c/16 (see GemmArgs lg_*)
-  // few-token q/k/v projection (swap orientation, cluster reduce) with RoPE fused: the weight rows of
-  // each 256-wide head are interleaved (row 2j = dim j, row 2j+1 = dim j+128), see GemmArgs rope_*
+  // q/k/v projection with RoPE fused (normal orientation, or swap orientation through the cluster
+  // reduce): the weight rows of each 256-wide head are interleaved (row 2j = dim j, row 2j+1 = dim
+  // j+128), see GemmArgs rope_*
   EPI_ROPE = 8,
 };
 // v = acc * out_scale + bias[f] + addend[(t % add_mod)][f]
@@ -126,6 +127,50 @@ __device__ __forceinline__ void epi_row32(const GemmArgs& a, float (&v)[32], int
       float4* dst = reinterpret_cast<float4*>(a.out_f32 + (size_t)t * a.ld_out_f32 + f0);
 #pragma unroll
       for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      return;
+    }
+    if (EPI == EPI_ROPE) {
+      // columns (2j, 2j+1) of a 256-wide head block = head dims (j, j+128): 16 pairs, dims j0..j0+15
+      const int hb = f0 >> 8, j0 = (f0 & 255) >> 1;
+      uint32_t lo[8], hi[8];
+      if (hb == 9) {
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          lo[p] = pack_bf2(v[4 * p], v[4 * p + 2]);
+          hi[p] = pack_bf2(v[4 * p + 1], v[4 * p + 3]);
+        }
+      } else {
+        const size_t ci = (size_t)(a.rope_pos_off + t % a.rope_per_sample) * 128 + j0;
+        float cs[16], sn[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 c4 = reinterpret_cast<const float4*>(a.rope_cos + ci)[q];
+          const float4 s4 = reinterpret_cast<const float4*>(a.rope_sin + ci)[q];
+          cs[4 * q] = c4.x, cs[4 * q + 1] = c4.y, cs[4 * q + 2] = c4.z, cs[4 * q + 3] = c4.w;
+          sn[4 * q] = s4.x, sn[4 * q + 1] = s4.y, sn[4 * q + 2] = s4.z, sn[4 * q + 3] = s4.w;
+        }
+        const float sc = hb == 8 ? 1.0f : 0.0625f;
+        float ra[16], rc[16];
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+          const float x1 = rbf(v[2 * p]), x2 = rbf(v[2 * p + 1]);
+          ra[p] = rbf(x1 * cs[p] - x2 * sn[p]) * sc;
+          rc[p] = rbf(x2 * cs[p] + x1 * sn[p]) * sc;
+        }
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          lo[p] = pack_bf2(ra[2 * p], ra[2 * p + 1]);
+          hi[p] = pack_bf2(rc[2 * p], rc[2 * p + 1]);
+        }
+      }
+      bf16* base = hb == 9 ? a.rope_v + (size_t)t * a.rope_ld_kv
+                           : (hb == 8 ? a.rope_k + (size_t)t * a.rope_ld_kv : a.out + (size_t)t * a.ld_out + hb * 256);
+      uint4* d0 = reinterpret_cast<uint4*>(base + j0);
+      uint4* d1 = reinterpret_cast<uint4*>(base + 128 + j0);
+      d0[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      d0[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+      d1[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      d1[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
       return;
     }
     if (EPI == EPI_GEGLU) {
