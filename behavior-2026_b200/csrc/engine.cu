@@ -108,6 +108,7 @@ struct pi05_engine {
   long launches = 0;  // kernels enqueued (counted at capture time)
   struct Trainer* tr = nullptr;  // LoRA train state (train.cuh), created by pi05_lora_init
   bool cluster_splitk = true;    // few-token split-K GEMMs reduce inside a cluster (PI05_CLUSTER_SPLITK=0: tickets)
+  bool wide_swap = true;          // few M-tiles: weights-on-M cluster split-K (PI05_WIDE_SWAP=0: normal tiles)
   bool attn_tc = true;           // head_dim-256 MQA attention on tcgen05 (PI05_ATTN_TC=0: the mma.sync kernel)
 };
 
@@ -347,7 +348,7 @@ bool launch_cluster(pi05_engine* e, void (*kern)(KArgs...), dim3 grid, dim3 bloc
 
 template <int BN>
 bool launch_swap_cluster(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga, int S) {
-  const dim3 grid(ga.tiles_m * S);
+  const dim3 grid(ga.tiles_m * ga.tiles_n * S);
   const size_t sm = (size_t)GemmCfg<BN>::SMEM;
   const bool p = ga.pdl != 0;
   switch (ga.epi) {
@@ -414,9 +415,29 @@ bool set_gemm_smem(pi05_engine* e) {
   return true;
 }
 
+// Few M-tiles in the normal orientation (a few hundred to ~1000 tokens, e.g. SigLIP's 768 and Gemma's
+// 968 at batch 1): put the weights on the 128-row side with up to 256 tokens per tile and split K over
+// a cluster (on-chip reduction), when the normal tiling would leave more than half the SMs idle.
+int wide_swap_split(pi05_engine* e, const Lin& L) {
+  const int kt = (L.K + 63) / 64;
+  const bool epi_ok = L.epi == EPI_STORE || L.epi == EPI_GELU || L.epi == EPI_RESID || L.epi == EPI_GATED ||
+                      L.epi == EPI_GEGLU || L.epi == EPI_F32 || L.epi == EPI_ROPE;
+  // measured: it pays for long K only (SigLIP fc2 K=4304: 26.8 -> 22.0 µs; Gemma down K=16384: 78.3 -> 74.7 µs),
+  // and loses for K <= 2048 (the 128x256 partial tiles' DSMEM reduce costs more than the shorter K loop saves)
+  if (!e->wide_swap || !e->cluster_splitk || L.T <= 128 || L.amn || !epi_ok || L.addend || L.out_t || kt < 64) return 0;
+  const int t256 = ((L.T + 127) / 128) * ((L.F + 255) / 256);
+  if (t256 >= e->num_sms / 2) return 0;
+  const int tiles = ((L.F + 127) / 128) * ((L.T + 255) / 256);
+  const int want = std::min(8, std::min(e->num_sms / std::max(1, tiles), kt / 2));
+  int S = 1;
+  while (S * 2 <= want) S *= 2;
+  return S >= 2 ? S : 0;
+}
+
 bool linear(pi05_engine* e, const Lin& L) {
   GemmArgs ga = {};
-  const bool swap = L.T <= 128 && !L.no_swap && !L.amn;
+  const int wide_S = wide_swap_split(e, L);
+  const bool swap = (L.T <= 128 && !L.no_swap && !L.amn) || wide_S > 0;
   int BN;
   CUtensorMap ta, tb;
   const int kt = (L.K + 63) / 64;
@@ -437,11 +458,11 @@ bool linear(pi05_engine* e, const Lin& L) {
   } else if (L.amn) {
     return set_err(e, "MN-major A operand is only wired for N <= 48");
   } else if (swap) {
-    BN = L.T <= 64 ? 64 : 128;
+    BN = L.T <= 64 ? 64 : (L.T <= 128 ? 128 : 256);
     ga.M = L.F;
     ga.N = L.T;
     ga.tiles_m = (L.F + 127) / 128;
-    ga.tiles_n = 1;
+    ga.tiles_n = (L.T + BN - 1) / BN;
     if (!make_tmap(e, &ta, L.w, L.F, L.K, L.ldw, 128) || !make_tmap(e, &tb, L.x, L.T, L.K, L.ldx, BN)) return false;
   } else {
     // Measured on B200: the mainloop is bound by L2->shared-memory bandwidth, and a 128x256 tile
@@ -517,15 +538,20 @@ bool linear(pi05_engine* e, const Lin& L) {
   ga.lg_trans = L.lg_trans;
   ga.lg_K = L.lg_K;
   for (int i = 0; i < 3; ++i) ga.lg_off[i] = L.lg_off[i];
-  if (swap && splits > 1 && e->cluster_splitk) {
+  if (swap && (splits > 1 || wide_S > 0) && e->cluster_splitk) {
     // few tokens, K split: reduce the split partials on chip inside a cluster of S CTAs
-    int S = 1;
-    const int want = std::min(8, std::max(1, std::min(e->num_sms / ga.tiles_m, kt / 2)));
-    while (S * 2 <= want) S *= 2;
+    int S = wide_S;
+    if (S == 0) {
+      S = 1;
+      const int want = std::min(8, std::max(1, std::min(e->num_sms / ga.tiles_m, kt / 2)));
+      while (S * 2 <= want) S *= 2;
+    }
     if (S > 1) {
       ga.kt_per_split = (kt + S - 1) / S;
       ga.splits = S;
-      return BN == 64 ? launch_swap_cluster<64>(e, ta, tb, ga, S) : launch_swap_cluster<128>(e, ta, tb, ga, S);
+      return BN == 64    ? launch_swap_cluster<64>(e, ta, tb, ga, S)
+             : BN == 128 ? launch_swap_cluster<128>(e, ta, tb, ga, S)
+                         : launch_swap_cluster<256>(e, ta, tb, ga, S);
     }
   }
   if (L.epi == EPI_ROPE && swap) return set_err(e, "fused RoPE epilogue: few-token projection without a cluster split");
@@ -1242,6 +1268,7 @@ bool create(pi05_engine* e) {
   if (const char* s = getenv("PI05_PDL")) e->pdl = atoi(s) != 0;
   if (const char* s = getenv("PI05_CLUSTER_SPLITK")) e->cluster_splitk = atoi(s) != 0;
   if (const char* s = getenv("PI05_ATTN_TC")) e->attn_tc = atoi(s) != 0;
+  if (const char* s = getenv("PI05_WIDE_SWAP")) e->wide_swap = atoi(s) != 0;
   if (const char* s = getenv("PI05_MEGA")) e->mega = atoi(s) != 0;
   CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   cudaDriverEntryPointQueryResult q;
@@ -1252,7 +1279,7 @@ bool create(pi05_engine* e) {
 
   if (!set_gemm_smem<64>(e) || !set_gemm_smem<128>(e) || !set_gemm_smem<256>(e)) return false;
   if (!set_gemm_smem_small<16>(e) || !set_gemm_smem_small<32>(e) || !set_gemm_smem_small<48>(e)) return false;
-  if (!set_swap_cluster_smem<64>(e) || !set_swap_cluster_smem<128>(e)) return false;
+  if (!set_swap_cluster_smem<64>(e) || !set_swap_cluster_smem<128>(e) || !set_swap_cluster_smem<256>(e)) return false;
 
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_HD, 4>::SMEM));

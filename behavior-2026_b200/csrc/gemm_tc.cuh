@@ -604,7 +604,8 @@ __global__ void __launch_bounds__(256, 1)
 // ---------------------------------------------------------------------------------------------------
 // Few-token weight streaming with split-K inside a thread-block cluster (swap orientation only).
 //
-// A tile of 128 weight rows is split along K over the S CTAs of one cluster (S <= 8).  Each CTA
+// A tile of 128 weight rows x BN tokens (BN <= 256; several token tiles for up to ~1000 tokens) is
+// split along K over the S CTAs of one cluster (S <= 8).  Each CTA
 // stages its fp32 partial tile in its own shared memory; after a cluster barrier CTA r reduces rows
 // [r*128/S, (r+1)*128/S) by reading the S partials over distributed shared memory in rank order
 // (deterministic), applies the epilogue and stores.  The partials never leave the chip and the
@@ -650,14 +651,15 @@ __device__ __forceinline__ float swap_epi_value(const GemmArgs& a, float v, cons
 // denoise graph: batching more items per pass, or fetching operands before the cluster barrier, costs
 // more (registers, and the next kernel's early start under programmatic dependent launch) than it saves.
 template <int BN, int EPI, int S>
-__device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_base, int rank, int m0, int rtid) {
+__device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_base, int rank, int m0, int n0,
+                                            int rtid) {
   constexpr int R = 128 / S, RED_LD = BN + 4, ITEMS = R * (BN / 4);
 #pragma unroll 1
   for (int it = rtid; it < ITEMS; it += 128) {
     const int lr = it % R, cg = it / R;
     const int f = m0 + rank * R + lr;
     SwapEpiOps o;
-    swap_epi_load<EPI>(args, f, cg * 4, o);
+    swap_epi_load<EPI>(args, f, n0 + cg * 4, o);
     const uint32_t addr = red_base + (uint32_t)((rank * R + lr) * RED_LD + cg * 4) * 4u;
     float4 pv[S];
 #pragma unroll
@@ -672,7 +674,7 @@ __device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_b
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int t = cg * 4 + q;
+      const int t = n0 + cg * 4 + q;
       const bool valid = f < args.M && t < args.N;
       if (EPI == EPI_GEGLU) {
         // rows (2j, 2j+1) = (gate_j, up_j) sit in neighbouring lanes (R is even)
@@ -733,8 +735,9 @@ __global__ void __launch_bounds__(256, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = (int)cluster_size(), rank = (int)cluster_rank();
-  const int tm = blockIdx.x / S;
-  const int m0 = tm * C::BM;
+  const int tile = blockIdx.x / S;  // clusters walk the weight tiles first, then the token tiles
+  const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
+  const int m0 = tm * C::BM, n0 = tn * BN;
   const int kt_total = (args.K + C::BK - 1) / C::BK;
   const int kt0 = rank * args.kt_per_split;
   const int nkt = max(0, min(kt_total, kt0 + args.kt_per_split) - kt0);
@@ -777,7 +780,7 @@ __global__ void __launch_bounds__(256, 2)
           pdl_wait();
           waited = true;
         }
-        tma_load_2d(sB + s * C::B_BYTES, &tma_b, &full_bar[s], (kt0 + i) * C::BK, 0);
+        tma_load_2d(sB + s * C::B_BYTES, &tma_b, &full_bar[s], (kt0 + i) * C::BK, n0);
       }
     }
     __syncwarp();
@@ -829,10 +832,10 @@ __global__ void __launch_bounds__(256, 2)
     const int rtid = threadIdx.x - 128;
     const uint32_t red_base = smem_u32(red);
     switch (S) {
-      case 2: swap_reduce<BN, EPI, 2>(args, red_base, rank, m0, rtid); break;
-      case 4: swap_reduce<BN, EPI, 4>(args, red_base, rank, m0, rtid); break;
-      case 8: swap_reduce<BN, EPI, 8>(args, red_base, rank, m0, rtid); break;
-      default: swap_reduce<BN, EPI, 1>(args, red_base, rank, m0, rtid); break;
+      case 2: swap_reduce<BN, EPI, 2>(args, red_base, rank, m0, n0, rtid); break;
+      case 4: swap_reduce<BN, EPI, 4>(args, red_base, rank, m0, n0, rtid); break;
+      case 8: swap_reduce<BN, EPI, 8>(args, red_base, rank, m0, n0, rtid); break;
+      default: swap_reduce<BN, EPI, 1>(args, red_base, rank, m0, n0, rtid); break;
     }
   }
   cluster_sync();  // peers are done reading this CTA's partial tile
