@@ -17,6 +17,7 @@
 #include "../../include/pi05.h"
 #include "attention.cuh"
 #include "attention_tc.cuh"
+#include "attention_sig.cuh"
 #include "denoise_mega.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
@@ -630,6 +631,14 @@ bool attention_tc(pi05_engine* e, const AttnArgs& a0, int batch) {
 
 bool attention(pi05_engine* e, const AttnArgs& a0, int batch, int hd) {
   if (hd == P5_HD && a0.G == 8 && a0.qdiv == 1.0f && e->attn_tc && a0.len1 > 0) return attention_tc(e, a0, batch);
+  if (hd == P5_SIG_HD && a0.G == 1 && e->attn_tc && a0.T == AttnSigCfg::ROWS * 2 && a0.len1 == AttnSigCfg::KEYS &&
+      a0.len2 == 0 && !a0.lse) {
+    // SigLIP: one CTA per (128 queries, head, image) on tcgen05
+    AttnArgs a = a0;
+    a.pdl = e->pdl ? 1 : 0;
+    return launch(e, attn_sig_kernel, dim3(2, P5_SIG_HEADS, batch), dim3(384), (size_t)AttnSigCfg::SMEM, true, a,
+                  e->d_status);
+  }
   AttnArgs a = a0;
   a.pdl = e->pdl ? 1 : 0;
   const int rows = a.T * a.G;
@@ -1286,6 +1295,7 @@ bool create(pi05_engine* e) {
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_HD, 8>::SMEM));
   CK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcCfg::SMEM));
+  CK(cudaFuncSetAttribute(attn_sig_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSigCfg::SMEM));
   CK(cudaFuncSetAttribute(denoise_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MegaCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_kernel<P5_SIG_HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_SIG_HD, 4>::SMEM));
@@ -1792,6 +1802,31 @@ int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, in
   at.splits = splits;
   at.force_splits = splits;
   if (!attention(e, at, batch, P5_HD)) return fail_code(e);
+  return PI05_OK;
+}
+
+int pi05_op_siglip_attention(pi05_engine* e, int images, const void* qkv, void* out) {
+  if (!e || images < 1 || images > 65535 || !qkv || !out) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  AttnArgs at = {};
+  at.q = (const bf16*)qkv;
+  at.ldq = P5_SIG_QKV;
+  at.q_bstride = (long)P5_SIG_TOK * P5_SIG_QKV;
+  at.out = (bf16*)out;
+  at.ldo = P5_SIG_W;
+  at.o_bstride = (long)P5_SIG_TOK * P5_SIG_W;
+  at.k1 = (const bf16*)qkv + P5_SIG_W;
+  at.v1 = (const bf16*)qkv + 2 * P5_SIG_W;
+  at.ld1 = P5_SIG_QKV;
+  at.len1 = P5_SIG_TOK;
+  at.b1stride = (long)P5_SIG_TOK * P5_SIG_QKV;
+  at.k2 = at.k1;
+  at.v2 = at.v1;
+  at.T = P5_SIG_TOK;
+  at.G = 1;
+  at.qdiv = P5_SIG_QDIV;
+  at.splits = 1;
+  if (!attention(e, at, images, P5_SIG_HD)) return fail_code(e);
   return PI05_OK;
 }
 

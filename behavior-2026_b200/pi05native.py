@@ -23,7 +23,7 @@ EXPORTS = [
     "pi05_save_weights", "pi05_load_weights", "pi05_prefill", "pi05_set_prefix_cache", "pi05_get_prefix_cache",
     "pi05_denoise", "pi05_infer", "pi05_stream", "pi05_sync", "pi05_prefix_len", "pi05_graph_launches",
     "pi05_synth_images", "pi05_synth_tokens", "pi05_synth_noise", "pi05_synth_prefix_cache", "pi05_create_batch",
-    "pi05_infer_batch", "pi05_set_stage", "pi05_op_linear", "pi05_op_attention", "pi05_linear_static",
+    "pi05_infer_batch", "pi05_set_stage", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
 ]
 
 
@@ -95,6 +95,7 @@ def _load():
     L.pi05_set_stage.argtypes = [vp, i32, i32, i32]
     L.pi05_op_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp]
     L.pi05_op_attention.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32]
+    L.pi05_op_siglip_attention.argtypes = [vp, i32, vp, vp]
     L.pi05_linear_static.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_char_p, ctypes.c_size_t]
     L.pi05_lora_default_config.argtypes = [P(LoraConfig)]
     L.pi05_lora_default_config.restype = None
@@ -254,6 +255,12 @@ class Engine:
         S = k.shape[1]
         p = lambda t: ctypes.c_void_p(t.data_ptr())
         self._check(lib.pi05_op_attention(self._h, b, T, S, p(q), ldq, p(k), p(v), p(out), splits))
+
+    def op_siglip_attention(self, qkv, out):
+        """qkv [images*256][3456] (q | k | v, 16 heads x 72), out [images*256][1152]; CUDA bf16 tensors."""
+        images = qkv.shape[0] // 256
+        p = lambda t: ctypes.c_void_p(t.data_ptr())
+        self._check(lib.pi05_op_siglip_attention(self._h, images, p(qkv), p(out)))
 
     # -- LoRA fine-tuning (reference: LoraTrainer::accumulate / finalize_grads / opt_step)
     def lora_init(self, seed=0, micro_batch=8, **kw):

@@ -153,6 +153,11 @@ PI05_API int pi05_op_linear(pi05_engine* e, int T, int F, int K, const void* x, 
                             const void* res, const void* gate, int epi, void* out);
 PI05_API int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, int ldq, const void* k,
                                const void* v, void* out, int splits);
+/* SigLIP attention of `images` 256-token images: qkv [images*256][3*1152] (q | k | v, 16 heads x 72
+ * each), out [images*256][1152] = softmax(R(q / sqrt(72)) k^T) v per head and image.  The vision
+ * tower's own attention step (reference: SigLIP block in the pi05 engine, π05_네이티브엔진.md); exposed as
+ * an operator for tests and benchmarks.  Asynchronous; call pi05_sync. */
+PI05_API int pi05_op_siglip_attention(pi05_engine* e, int images, const void* qkv, void* out);
 /* Device time (microseconds per launch) of pi05_op_linear on internal random operands: `reps` launches
  * in one CUDA graph, rotating over enough weight copies (> 256 MB) that each launch reads HBM. */
 PI05_API int pi05_op_bench_linear(pi05_engine* e, int T, int F, int K, int epi, int reps, float* us_per_launch);

@@ -85,6 +85,38 @@ def test_linear_epilogues_match_torch(pn, torch_cuda, epi, T):
     assert err <= 2e-2 * max(1.0, ref.abs().max().item()), (epi, err)
 
 
+@pytest.mark.parametrize("epi", ["gelu", "resid", "gated", "geglu", "f32"])
+def test_linear_long_k_few_tiles_epilogues(pn, torch_cuda, epi):
+    """768 tokens x K=4096: few 128-row tiles, so the weights go on the 128-row side with 256-token
+    tiles and K is split over a cluster (on-chip reduction); every fused epilogue against torch."""
+    torch = torch_cuda
+    T, F, K = 768, 1024, 4096
+    g = torch.Generator(device="cuda").manual_seed(23)
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(F, K, device="cuda", generator=g) * 0.02).bfloat16()
+    res = torch.randn(T, F, device="cuda", generator=g).bfloat16()
+    gate = torch.randn(F, device="cuda", generator=g).bfloat16()
+    eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), max_batch=1)
+    acc = x.float() @ w.float().t()
+    rb = lambda t: t.bfloat16().float()
+    if epi == "geglu":
+        out = torch.empty(T, F // 2, device="cuda", dtype=torch.bfloat16)
+        ref = rb(torch.nn.functional.gelu(rb(acc[:, 0::2]), approximate="tanh")) * rb(acc[:, 1::2])
+    elif epi == "f32":
+        out = torch.empty(T, F, device="cuda", dtype=torch.float32)
+        ref = acc
+    else:
+        out = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+        ref = {"gelu": lambda: torch.nn.functional.gelu(rb(acc), approximate="tanh"),
+               "resid": lambda: res.float() + rb(acc),
+               "gated": lambda: res.float() + rb(rb(acc) * gate.float())}[epi]()
+    eng.op_linear(x, w, out, epi, res=res if epi in ("resid", "gated") else None,
+                  gate=gate if epi == "gated" else None)
+    eng.sync()
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2 * max(1.0, ref.abs().max().item()), (epi, err)
+
+
 @pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("T,S,splits,qscale", [(50, 1018, 8, 0.1), (50, 1018, 1, 0.1), (968, 968, 1, 0.1),
                                                (100, 2048, 4, 0.1), (1, 1000, 3, 0.1), (33, 200, 1, 0.6),
@@ -109,6 +141,27 @@ def test_attention_matches_torch(pn, torch_cuda, monkeypatch, tc, T, S, splits, 
     logits = torch.einsum("bthd,bsd->bhts", qh, k.float())
     p = torch.softmax(logits, -1)
     ref = torch.einsum("bhts,bsd->bthd", p, v.float()).reshape(b, T, 2048)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 3e-2, err
+
+
+@pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("images", [1, 5])
+def test_siglip_attention_matches_torch(pn, torch_cuda, monkeypatch, tc, images):
+    """SigLIP MHA (16 heads x 72 per 256-token image, q rounded after / 8.5) against fp32 torch."""
+    torch = torch_cuda
+    monkeypatch.setenv("PI05_ATTN_TC", "1" if tc else "0")
+    g = torch.Generator(device="cuda").manual_seed(31 + images)
+    qkv = torch.randn(images * 256, 3 * 1152, device="cuda", generator=g).bfloat16()
+    out = torch.empty(images * 256, 1152, device="cuda", dtype=torch.bfloat16)
+    eng = pn.Engine(pn.Config.make(siglip_layers=1, gemma_layers=1, num_steps=1), max_batch=1)
+    eng.op_siglip_attention(qkv, out)
+    eng.sync()
+    x = qkv.view(images, 256, 3, 16, 72)
+    q = (x[:, :, 0].float() / 8.5).bfloat16().float()
+    k, v = x[:, :, 1].float(), x[:, :, 2].float()
+    p = torch.softmax(torch.einsum("bthd,bshd->bhts", q, k), -1)
+    ref = torch.einsum("bhts,bshd->bthd", p, v).reshape(images * 256, 1152)
     err = (out.float() - ref).abs().max().item()
     assert err < 3e-2, err
 
