@@ -18,6 +18,7 @@
 #include "attention.cuh"
 #include "attention_tc.cuh"
 #include "attention_sig.cuh"
+#include "gemm_wide.cuh"
 #include "denoise_mega.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
@@ -109,6 +110,7 @@ struct pi05_engine {
   long launches = 0;  // kernels enqueued (counted at capture time)
   struct Trainer* tr = nullptr;  // LoRA train state (train.cuh), created by pi05_lora_init
   bool cluster_splitk = true;    // few-token split-K GEMMs reduce inside a cluster (PI05_CLUSTER_SPLITK=0: tickets)
+  bool gemm_wide = true;          // 256x256 tiles for large GEMMs (PI05_GEMM_WIDE=0: 128x256)
   bool wide_swap = true;          // few M-tiles: weights-on-M cluster split-K (PI05_WIDE_SWAP=0: normal tiles)
   bool attn_tc = true;           // head_dim-256 MQA attention on tcgen05 (PI05_ATTN_TC=0: the mma.sync kernel)
 };
@@ -307,6 +309,31 @@ struct Lin {
   bf16* rope_k = nullptr;
   bf16* rope_v = nullptr;
 };
+
+bool launch_gemm_wide(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga) {
+  const dim3 grid(std::min(ga.tiles_m * ga.tiles_n, e->num_sms));
+  const size_t sm = (size_t)GemmWideCfg::SMEM;
+  const bool p = ga.pdl != 0;
+  switch (ga.epi) {
+    case EPI_GELU: return launch(e, gemm_wide_kernel<EPI_GELU>, grid, dim3(384), sm, p, ta, tb, ga);
+    case EPI_RESID: return launch(e, gemm_wide_kernel<EPI_RESID>, grid, dim3(384), sm, p, ta, tb, ga);
+    case EPI_GATED: return launch(e, gemm_wide_kernel<EPI_GATED>, grid, dim3(384), sm, p, ta, tb, ga);
+    case EPI_GEGLU: return launch(e, gemm_wide_kernel<EPI_GEGLU>, grid, dim3(384), sm, p, ta, tb, ga);
+    case EPI_F32: return launch(e, gemm_wide_kernel<EPI_F32>, grid, dim3(384), sm, p, ta, tb, ga);
+    case EPI_ROPE: return launch(e, gemm_wide_kernel<EPI_ROPE>, grid, dim3(384), sm, p, ta, tb, ga);
+    default: return launch(e, gemm_wide_kernel<EPI_STORE>, grid, dim3(384), sm, p, ta, tb, ga);
+  }
+}
+
+bool set_gemm_wide_smem(pi05_engine* e) {
+  const int sm = GemmWideCfg::SMEM;
+  void (*k[])(CUtensorMap, CUtensorMap, GemmArgs) = {gemm_wide_kernel<EPI_STORE>, gemm_wide_kernel<EPI_GELU>,
+                                                     gemm_wide_kernel<EPI_RESID>, gemm_wide_kernel<EPI_GATED>,
+                                                     gemm_wide_kernel<EPI_GEGLU>, gemm_wide_kernel<EPI_F32>,
+                                                     gemm_wide_kernel<EPI_ROPE>};
+  for (auto f : k) CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  return true;
+}
 
 template <int BN>
 bool launch_gemm_bn(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga) {
@@ -556,6 +583,23 @@ bool linear(pi05_engine* e, const Lin& L) {
     }
   }
   if (L.epi == EPI_ROPE && swap) return set_err(e, "fused RoPE epilogue: few-token projection without a cluster split");
+  if (!swap && BN == 256 && splits == 1 && !L.amn && e->gemm_wide && L.epi != EPI_STORE_T && L.epi != EPI_LORA_GRAD &&
+      kt >= 64) {
+    // at least a full wave of 256x256 tiles and K >= 4096: the wider tile loads a third fewer bytes per
+    // MAC, but its single accumulator set leaves the epilogue unoverlapped, which only a long K loop
+    // amortises (measured: Gemma down 3.67 -> 3.20 ms, SigLIP fc2 550 -> 451 µs at bs64; K = 2048
+    // shapes 4-20 % slower)
+    const int wtm = (L.T + 255) / 256, wtn = (L.F + 255) / 256;
+    if ((long)wtm * wtn >= e->num_sms) {
+      GemmArgs gw = ga;
+      gw.tiles_m = wtm;
+      gw.tiles_n = wtn;
+      gw.splits = 1;
+      gw.kt_per_split = kt;
+      gw.group_m = std::max(1, std::min(wtm, (int)((48ull << 20) / (256ull * L.K * 2))));
+      return launch_gemm_wide(e, ta, tb, gw);
+    }
+  }
   if (BN == 16) return launch_gemm_small<16>(e, ta, tb, ga, L.amn);
   if (BN == 32) return launch_gemm_small<32>(e, ta, tb, ga, L.amn);
   if (BN == 48) return launch_gemm_small<48>(e, ta, tb, ga, L.amn);
@@ -1278,6 +1322,7 @@ bool create(pi05_engine* e) {
   if (const char* s = getenv("PI05_CLUSTER_SPLITK")) e->cluster_splitk = atoi(s) != 0;
   if (const char* s = getenv("PI05_ATTN_TC")) e->attn_tc = atoi(s) != 0;
   if (const char* s = getenv("PI05_WIDE_SWAP")) e->wide_swap = atoi(s) != 0;
+  if (const char* s = getenv("PI05_GEMM_WIDE")) e->gemm_wide = atoi(s) != 0;
   if (const char* s = getenv("PI05_MEGA")) e->mega = atoi(s) != 0;
   CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   cudaDriverEntryPointQueryResult q;
@@ -1289,6 +1334,7 @@ bool create(pi05_engine* e) {
   if (!set_gemm_smem<64>(e) || !set_gemm_smem<128>(e) || !set_gemm_smem<256>(e)) return false;
   if (!set_gemm_smem_small<16>(e) || !set_gemm_smem_small<32>(e) || !set_gemm_smem_small<48>(e)) return false;
   if (!set_swap_cluster_smem<64>(e) || !set_swap_cluster_smem<128>(e) || !set_swap_cluster_smem<256>(e)) return false;
+  if (!set_gemm_wide_smem(e)) return false;
 
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_HD, 4>::SMEM));

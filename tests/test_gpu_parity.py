@@ -44,6 +44,7 @@ def test_linear_store_matches_torch(pn, torch_cuda, T, F, K):
     b = (torch.randn(F, device="cuda", generator=g) * 0.02).bfloat16()
     eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), max_batch=1)
     out = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()  # inputs and reference come from torch's stream; the engine has its own
     eng.op_linear(x, w, out, "store", bias=b)
     eng.sync()
     ref = (x.float() @ w.float().t() + b.float())
@@ -78,6 +79,7 @@ def test_linear_epilogues_match_torch(pn, torch_cuda, epi, T):
             ref = res.float() + rb(acc)
         else:
             ref = res.float() + rb(rb(acc) * gate.float())
+    torch.cuda.synchronize()  # inputs and reference come from torch's stream; the engine has its own
     eng.op_linear(x, w, out, epi, res=res if epi in ("resid", "gated") else None,
                   gate=gate if epi == "gated" else None)
     eng.sync()
@@ -85,12 +87,14 @@ def test_linear_epilogues_match_torch(pn, torch_cuda, epi, T):
     assert err <= 2e-2 * max(1.0, ref.abs().max().item()), (epi, err)
 
 
-@pytest.mark.parametrize("epi", ["gelu", "resid", "gated", "geglu", "f32"])
-def test_linear_long_k_few_tiles_epilogues(pn, torch_cuda, epi):
-    """768 tokens x K=4096: few 128-row tiles, so the weights go on the 128-row side with 256-token
-    tiles and K is split over a cluster (on-chip reduction); every fused epilogue against torch."""
+@pytest.mark.parametrize("shape", [(768, 1024, 4096), (4096, 2560, 1024)], ids=["long_k_few_tiles", "wide_tiles"])
+@pytest.mark.parametrize("epi", ["store", "gelu", "resid", "gated", "geglu", "f32"])
+def test_linear_tile_shapes_epilogues(pn, torch_cuda, epi, shape):
+    """Every fused epilogue on the two other GEMM layouts: 768 tokens x K=4096 (few 128-row tiles: the
+    weights go on the 128-row side with 256-token tiles and K is split over a cluster, on-chip
+    reduction) and 4096 x 2560 (a full wave of 256x256 tiles, two M=128 MMAs per B tile)."""
     torch = torch_cuda
-    T, F, K = 768, 1024, 4096
+    T, F, K = shape
     g = torch.Generator(device="cuda").manual_seed(23)
     x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
     w = (torch.randn(F, K, device="cuda", generator=g) * 0.02).bfloat16()
@@ -107,9 +111,11 @@ def test_linear_long_k_few_tiles_epilogues(pn, torch_cuda, epi):
         ref = acc
     else:
         out = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
-        ref = {"gelu": lambda: torch.nn.functional.gelu(rb(acc), approximate="tanh"),
+        ref = {"store": lambda: acc,
+               "gelu": lambda: torch.nn.functional.gelu(rb(acc), approximate="tanh"),
                "resid": lambda: res.float() + rb(acc),
                "gated": lambda: res.float() + rb(rb(acc) * gate.float())}[epi]()
+    torch.cuda.synchronize()  # inputs and reference come from torch's stream; the engine has its own
     eng.op_linear(x, w, out, epi, res=res if epi in ("resid", "gated") else None,
                   gate=gate if epi == "gated" else None)
     eng.sync()
@@ -135,6 +141,7 @@ def test_attention_matches_torch(pn, torch_cuda, monkeypatch, tc, T, S, splits, 
     v = torch.randn(b, S, 256, device="cuda", generator=g).bfloat16()
     out = torch.empty(b, T, 2048, device="cuda", dtype=torch.bfloat16)
     eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), max_batch=1)
+    torch.cuda.synchronize()  # inputs and reference come from torch's stream; the engine has its own
     eng.op_attention(q, k, v, out, splits)
     eng.sync()
     qh = q[:, :, :2048].float().view(b, T, 8, 256)
@@ -155,6 +162,7 @@ def test_siglip_attention_matches_torch(pn, torch_cuda, monkeypatch, tc, images)
     qkv = torch.randn(images * 256, 3 * 1152, device="cuda", generator=g).bfloat16()
     out = torch.empty(images * 256, 1152, device="cuda", dtype=torch.bfloat16)
     eng = pn.Engine(pn.Config.make(siglip_layers=1, gemma_layers=1, num_steps=1), max_batch=1)
+    torch.cuda.synchronize()  # inputs and reference come from torch's stream; the engine has its own
     eng.op_siglip_attention(qkv, out)
     eng.sync()
     x = qkv.view(images, 256, 3, 16, 72)

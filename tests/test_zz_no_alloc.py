@@ -22,6 +22,7 @@ def test_static_scratch_linear_matches_engine_linear(pn):
         w = (torch.randn(F, K, device="cuda", generator=g) * 0.02).bfloat16()
         b = (torch.randn(F, device="cuda", generator=g) * 0.02).bfloat16()
         ref = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+        torch.cuda.synchronize()  # x, w, b come from torch's stream; the engine runs on its own
         eng.op_linear(x, w, ref, "store", bias=b)
         eng.sync()
         fp32 = x.float() @ w.float().t() + b.float()
