@@ -645,7 +645,8 @@ __device__ __forceinline__ float swap_epi_value(const GemmArgs& a, float v, cons
 
 // Cluster reduce of a swap-orientation tile: CTA `rank` of S owns rows [rank*R, rank*R+R), R = 128/S.
 // Items = (row, group of 4 tokens); consecutive threads take consecutive weight rows of one group, so
-// the stores of each token are contiguous across the warp (R*BN/4 is a multiple of 128).  An item's
+// the stores of each token are contiguous across the warp (R*BN/4 is a multiple of 256: all eight
+// warps of the CTA take part).  An item's
 // epilogue operands (bias, residual, gate) are loaded from global memory before, and in flight with,
 // its S partial loads; the partials are summed in rank order (deterministic).  Measured in the
 // denoise graph: batching more items per pass, or fetching operands before the cluster barrier, costs
@@ -655,7 +656,7 @@ __device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_b
                                             int rtid) {
   constexpr int R = 128 / S, RED_LD = BN + 4, ITEMS = R * (BN / 4);
 #pragma unroll 1
-  for (int it = rtid; it < ITEMS; it += 128) {
+  for (int it = rtid; it < ITEMS; it += 256) {
     const int lr = it % R, cg = it / R;
     const int f = m0 + rank * R + lr;
     SwapEpiOps o;
@@ -827,9 +828,9 @@ __global__ void __launch_bounds__(256, 2)
   tc_fence_before();
   cluster_sync();  // every partial tile of the cluster is in shared memory
 
-  if (warp >= 4) {
+  {  // all eight warps reduce (the producer and MMA warps are done by now)
     if (args.pdl) pdl_wait();
-    const int rtid = threadIdx.x - 128;
+    const int rtid = threadIdx.x;
     const uint32_t red_base = smem_u32(red);
     switch (S) {
       case 2: swap_reduce<BN, EPI, 2>(args, red_base, rank, m0, n0, rtid); break;
