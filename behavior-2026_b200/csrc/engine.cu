@@ -113,6 +113,10 @@ struct pi05_engine {
   bool gemm_wide = true;          // 256x256 tiles for large GEMMs (PI05_GEMM_WIDE=0: 128x256)
   bool wide_swap = true;          // few M-tiles: weights-on-M cluster split-K (PI05_WIDE_SWAP=0: normal tiles)
   bool attn_tc = true;           // head_dim-256 MQA attention on tcgen05 (PI05_ATTN_TC=0: the mma.sync kernel)
+  // few-token denoise: adaRMSNorm folded into the q/k/v and gate/up cluster GEMMs, fed by per-token
+  // sum-of-squares partials from the producers of x (PI05_FUSE_NORM=0: separate rmsnorm launches)
+  bool fuse_norm = true;
+  float* nrm_ss = nullptr;  // 2 buffers of [P5_EXP_W / 16 parts][64 tokens]
 };
 
 namespace {
@@ -308,6 +312,13 @@ struct Lin {
   int rope_pos_off = 0, rope_per_sample = 1, rope_ld_kv = 0;
   bf16* rope_k = nullptr;
   bf16* rope_v = nullptr;
+  // fused adaRMSNorm of x (few-token cluster path; see GemmArgs nrm_*) and sum-of-squares partials out
+  const float* nrm_ss = nullptr;
+  int nrm_ss_ld = 0, nrm_parts = 0, nrm_D = 0;
+  const bf16* nrm_scale = nullptr;
+  const bf16* nrm_shift = nullptr;
+  float* ss_out = nullptr;
+  int ss_ld = 0;
 };
 
 bool launch_gemm_wide(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga) {
@@ -377,7 +388,7 @@ bool launch_cluster(pi05_engine* e, void (*kern)(KArgs...), dim3 grid, dim3 bloc
 template <int BN>
 bool launch_swap_cluster(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga, int S) {
   const dim3 grid(ga.tiles_m * ga.tiles_n * S);
-  const size_t sm = (size_t)GemmCfg<BN>::SMEM;
+  const size_t sm = (size_t)GemmCfg<BN>::SMEM + SWAP_NRM_BYTES;
   const bool p = ga.pdl != 0;
   switch (ga.epi) {
     case EPI_GELU: return launch_cluster(e, gemm_swap_cluster_kernel<BN, EPI_GELU>, grid, dim3(256), sm, S, p, ta, tb, ga);
@@ -392,7 +403,7 @@ bool launch_swap_cluster(pi05_engine* e, const CUtensorMap& ta, const CUtensorMa
 
 template <int BN>
 bool set_swap_cluster_smem(pi05_engine* e) {
-  const int sm = GemmCfg<BN>::SMEM;
+  const int sm = GemmCfg<BN>::SMEM + SWAP_NRM_BYTES;
   CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   CK(cudaFuncSetAttribute(gemm_swap_cluster_kernel<BN, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
@@ -566,6 +577,15 @@ bool linear(pi05_engine* e, const Lin& L) {
   ga.lg_trans = L.lg_trans;
   ga.lg_K = L.lg_K;
   for (int i = 0; i < 3; ++i) ga.lg_off[i] = L.lg_off[i];
+  ga.nrm_ss = L.nrm_ss;
+  ga.nrm_ss_ld = L.nrm_ss_ld;
+  ga.nrm_parts = L.nrm_parts;
+  ga.nrm_D = L.nrm_D;
+  ga.nrm_scale = L.nrm_scale;
+  ga.nrm_shift = L.nrm_shift;
+  ga.ss_out = L.ss_out;
+  ga.ss_ld = L.ss_ld;
+  const bool fused_nrm = L.nrm_ss || L.ss_out;
   if (swap && (splits > 1 || wide_S > 0) && e->cluster_splitk) {
     // few tokens, K split: reduce the split partials on chip inside a cluster of S CTAs
     int S = wide_S;
@@ -577,12 +597,18 @@ bool linear(pi05_engine* e, const Lin& L) {
     if (S > 1) {
       ga.kt_per_split = (kt + S - 1) / S;
       ga.splits = S;
+      if (L.nrm_ss && (BN != 64 || L.K % 64 != 0 || ga.kt_per_split * 64 > SWAP_NRM_KMAX || L.T > L.nrm_ss_ld ||
+                       L.nrm_parts % 2 != 0 || ((uintptr_t)L.nrm_scale | (uintptr_t)L.nrm_shift) % 16 != 0))
+        return set_err(e, "fused adaRMSNorm: unsupported shape");
+      if (L.ss_out && (L.epi != EPI_GATED || S > 8 || L.F % 16 != 0 || L.T > L.ss_ld))
+        return set_err(e, "sum-of-squares output: unsupported shape");
       return BN == 64    ? launch_swap_cluster<64>(e, ta, tb, ga, S)
              : BN == 128 ? launch_swap_cluster<128>(e, ta, tb, ga, S)
                          : launch_swap_cluster<256>(e, ta, tb, ga, S);
     }
   }
   if (L.epi == EPI_ROPE && swap) return set_err(e, "fused RoPE epilogue: few-token projection without a cluster split");
+  if (fused_nrm) return set_err(e, "fused adaRMSNorm / sum-of-squares output: not a few-token cluster projection");
   if (!swap && BN == 256 && splits == 1 && !L.amn && e->gemm_wide && L.epi != EPI_STORE_T && L.epi != EPI_LORA_GRAD &&
       kt >= 64) {
     // at least a full wave of 256x256 tiles and K >= 4096: the wider tile loads a third fewer bytes per
@@ -925,6 +951,12 @@ bool fused_rope_applies(pi05_engine* e, int n) {
   return T > 64 || e->cluster_splitk;  // > 64 tokens: normal orientation; <= 64: cluster split-K
 }
 
+// adaRMSNorm folded into the few-token q/k/v and gate/up cluster GEMMs (one 64-token tile)
+bool fused_norm_applies(pi05_engine* e, int n) {
+  const int T = n * e->cfg.horizon;
+  return e->fuse_norm && e->cluster_splitk && T <= 64 && P5_EXP_W % 32 == 0;
+}
+
 // Buffers and tensor-map table of the persistent denoise.  Runs outside stream capture.
 bool mega_prepare(pi05_engine* e) {
   using C = MegaCfg;
@@ -1030,19 +1062,36 @@ bool run_denoise_body(pi05_engine* e, int n) {
   const int MW = e->NM * 3 * D;  // modulation row width
   const float dtb = p5_dt_bf16(e->cfg.num_steps);
   const int attn_splits = n <= 4 ? 8 : 1;
+  // fused adaRMSNorm: x's producers (action_in, O and down projections) write per-token sums of squares
+  // over 16-feature groups; the q/k/v and gate/up projections read x and normalise it on chip
+  const bool fnorm = fused_norm_applies(e, n);
+  constexpr int NP = P5_EXP_W / 16, SSLD = 64;
+  float* ss_attn = e->nrm_ss;              // written by O (x after attention), read by gate/up
+  float* ss_mlp = e->nrm_ss + NP * SSLD;  // written by action_in / down (x after the MLP), read by q/k/v
+  auto fuse = [&](Lin& L, const float* ss, const bf16* mod) {
+    L.x = A.ex;
+    L.nrm_ss = ss;
+    L.nrm_ss_ld = SSLD;
+    L.nrm_parts = NP;
+    L.nrm_D = D;
+    L.nrm_scale = mod;
+    L.nrm_shift = mod + D;
+  };
   for (int s = 0; s < e->cfg.num_steps; ++s) {
     const bf16* mrow = e->mods + (size_t)s * MW;
     if (!launch(e, action_in_kernel, dim3((T * D + 255) / 256), dim3(256), 0, true, (const float*)A.xt,
-                (const bf16*)e->ain_w, (const bf16*)e->ain_b, A.ex, T, D))
+                (const bf16*)e->ain_w, (const bf16*)e->ain_b, A.ex, T, D, fnorm ? ss_mlp : (float*)nullptr, SSLD))
       return false;
     for (int l = 0; l < e->cfg.expert_layers; ++l) {
       const ExpLayer& x = e->ex[l];
       const bf16* m1 = mrow + (size_t)(2 * l) * 3 * D;
       const bf16* m2 = mrow + (size_t)(2 * l + 1) * 3 * D;
-      if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m1, m1 + D, T, D, 1, 0, D))
+      if (!fnorm &&
+          !launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m1, m1 + D, T, D, 1, 0, D))
         return false;
       if (fused_rope_applies(e, n)) {
         Lin q{A.eh, D, T, e->exp_wqkv_il + (size_t)l * P5_QKV * D, D, P5_QKV, D};
+        if (fnorm) fuse(q, ss_mlp, m1);
         q.no_swap = T > 64;
         q.epi = EPI_ROPE;
         q.out = A.eqkv;
@@ -1095,10 +1144,16 @@ bool run_denoise_body(pi05_engine* e, int n) {
       o.gate = m1 + 2 * D;
       o.ld_gate = 0;
       o.gate_div = 1;
+      if (fnorm) {
+        o.ss_out = ss_attn;
+        o.ss_ld = SSLD;
+      }
       if (!linear(e, o)) return false;
-      if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m2, m2 + D, T, D, 1, 0, D))
+      if (!fnorm &&
+          !launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, m2, m2 + D, T, D, 1, 0, D))
         return false;
       Lin gu{A.eh, D, T, x.wgu, D, 2 * P5_EXP_MLP, D};
+      if (fnorm) fuse(gu, ss_attn, m2);
       gu.epi = EPI_GEGLU;
       gu.out = A.eact;
       gu.ld_out = P5_EXP_MLP;
@@ -1112,6 +1167,10 @@ bool run_denoise_body(pi05_engine* e, int n) {
       dn.gate = m2 + 2 * D;
       dn.ld_gate = 0;
       dn.gate_div = 1;
+      if (fnorm && l + 1 < e->cfg.expert_layers) {
+        dn.ss_out = ss_mlp;
+        dn.ss_ld = SSLD;
+      }
       if (!linear(e, dn)) return false;
     }
     const bf16* mf = mrow + (size_t)(e->NM - 1) * 3 * D;
@@ -1324,6 +1383,7 @@ bool create(pi05_engine* e) {
   if (const char* s = getenv("PI05_WIDE_SWAP")) e->wide_swap = atoi(s) != 0;
   if (const char* s = getenv("PI05_GEMM_WIDE")) e->gemm_wide = atoi(s) != 0;
   if (const char* s = getenv("PI05_MEGA")) e->mega = atoi(s) != 0;
+  if (const char* s = getenv("PI05_FUSE_NORM")) e->fuse_norm = atoi(s) != 0;
   CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   cudaDriverEntryPointQueryResult q;
   void* fn = nullptr;
@@ -1393,6 +1453,7 @@ bool create(pi05_engine* e) {
   if (!al((void**)&e->attn_ws_o, e->attn_ws_rows * P5_HD * 4) || !al((void**)&e->attn_ws_ml, e->attn_ws_rows * 2 * 4))
     return false;
   if (!al((void**)&e->d_status, 64)) return false;
+  if (!al((void**)&e->nrm_ss, (size_t)2 * (P5_EXP_W / 16) * 64 * 4)) return false;
   CK(cudaStreamSynchronize(e->stream));
   return true;
 }

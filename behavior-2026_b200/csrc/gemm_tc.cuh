@@ -80,7 +80,25 @@ struct GemmArgs {
   int rope_pos_off, rope_per_sample, rope_ld_kv;
   bf16* rope_k;
   bf16* rope_v;
+  // Fused adaRMSNorm of the few-token operand (swap cluster kernel, 64-token tiles): the B tiles hold the
+  // residual stream x and are normalised in shared memory before the MMAs read them,
+  //   h[t][k] = R(x[t][k] * inv[t] * R(1 + nrm_scale[k]) + nrm_shift[k]),  inv[t] = 1 / sqrt(ss[t] / nrm_D + 1e-6),
+  //   ss[t] = sum over p < nrm_parts of nrm_ss[p * nrm_ss_ld + t] (in order),
+  // the same arithmetic as rmsnorm_kernel with its sum of squares taken from the producer's partials.
+  const float* nrm_ss;
+  int nrm_ss_ld, nrm_parts, nrm_D;
+  const bf16* nrm_scale;
+  const bf16* nrm_shift;
+  // EPI_GATED in the swap cluster kernel: per-token partial sums of squares of the stored outputs, one
+  // partial per 16 output features, ss_out[(f / 16) * ss_ld + t] = sum of R(out[t][f])^2.
+  float* ss_out;
+  int ss_ld;
 };
+
+// Extra shared memory of gemm_swap_cluster_kernel for the fused adaRMSNorm: inv[64], half sums[128],
+// scale and shift of the CTA's K slice (bf16, up to 1024 features each).
+constexpr int SWAP_NRM_BYTES = 256 + 512 + 2 * 1024 * 2;
+constexpr int SWAP_NRM_KMAX = 1024;
 
 template <int BN>
 struct GemmCfg {
@@ -665,7 +683,7 @@ __device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_b
     float4 pv[S];
 #pragma unroll
     for (int p = 0; p < S; ++p) pv[p] = ld_peer_v4(map_peer(addr, (uint32_t)p));
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    float v[4] = {0.f, 0.f, 0.f, 0.f}, sq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int p = 0; p < S; ++p) {
       v[0] += pv[p].x;
@@ -706,10 +724,28 @@ __device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_b
         }
       } else if (valid) {
         const float x = swap_epi_value<EPI>(args, v[q], o, q);
-        if (EPI == EPI_F32)
+        if (EPI == EPI_F32) {
           args.out_f32[(size_t)t * args.ld_out_f32 + f] = x;
-        else
-          args.out[(size_t)t * args.ld_out + f] = tobf(x);
+        } else {
+          const bf16 xb = tobf(x);
+          args.out[(size_t)t * args.ld_out + f] = xb;
+          sq[q] = bf(xb) * bf(xb);
+        }
+      }
+    }
+    if (EPI == EPI_GATED && args.ss_out) {
+      // 16 consecutive lanes hold 16 consecutive features f of the same 4 tokens (R >= 16)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int o2 = 8; o2; o2 >>= 1) sq[q] += __shfl_xor_sync(0xffffffffu, sq[q], o2);
+      }
+      if ((rtid & 15) == 0 && f < args.M) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int t = n0 + cg * 4 + q;
+          if (t < args.N) args.ss_out[(size_t)(f >> 4) * args.ss_ld + t] = sq[q];
+        }
       }
     }
   }
@@ -731,8 +767,14 @@ __global__ void __launch_bounds__(256, 2)
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
   uint64_t* empty_bar = full_bar + C::STAGES;
   uint64_t* accum_bar = empty_bar + C::STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+  uint64_t* ready_bar = accum_bar + 1;  // fused adaRMSNorm: B stage normalised in place
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ready_bar + C::STAGES);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* nrm_inv = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + 256);  // [64]
+  float* nrm_half = nrm_inv + 64;                                                      // [2][64]
+  bf16* nrm_sc = reinterpret_cast<bf16*>(nrm_half + 128);                              // [SWAP_NRM_KMAX]
+  bf16* nrm_sh = nrm_sc + SWAP_NRM_KMAX;
+  const bool nrm = BN == 64 && args.nrm_ss != nullptr;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = (int)cluster_size(), rank = (int)cluster_rank();
@@ -750,6 +792,8 @@ __global__ void __launch_bounds__(256, 2)
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(accum_bar, 1);
+    if (nrm)
+      for (int s = 0; s < C::STAGES; ++s) mbar_init(&ready_bar[s], 128);
     flags[0] = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tma_a);
@@ -791,7 +835,7 @@ __global__ void __launch_bounds__(256, 2)
       for (int i = 0; i < nkt && !flags[0]; ++i) {
         const int s = i % C::STAGES;
         const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
-        if (!mbar_wait(&full_bar[s], ph, args.status, P5_ERR_WAIT_FULL)) {
+        if (!mbar_wait(nrm ? &ready_bar[s] : &full_bar[s], ph, args.status, P5_ERR_WAIT_FULL)) {
           flags[0] = 1;
           break;
         }
@@ -807,6 +851,63 @@ __global__ void __launch_bounds__(256, 2)
     }
     __syncwarp();
   } else if (warp >= 4) {
+    if (nrm) {
+      // ---- fused adaRMSNorm: per-token inverse RMS from the producer's partials, then each B stage
+      // (64 token rows x 64 features, 128-byte swizzled rows) is normalised in place before the MMAs
+      const int nt = threadIdx.x - 128, tt = nt & 63, half = nt >> 6;
+      if (args.pdl) pdl_wait();
+      const int kbase = kt0 * C::BK;
+      for (int c = nt; c < nkt * C::BK / 8; c += 128) {
+        reinterpret_cast<uint4*>(nrm_sc)[c] = reinterpret_cast<const uint4*>(args.nrm_scale + kbase)[c];
+        reinterpret_cast<uint4*>(nrm_sh)[c] = reinterpret_cast<const uint4*>(args.nrm_shift + kbase)[c];
+      }
+      float acc = 0.f;
+      if (n0 + tt < args.N) {
+        const int hp = args.nrm_parts / 2, p0 = half * hp;
+        const float* src = args.nrm_ss + (size_t)p0 * args.nrm_ss_ld + n0 + tt;
+#pragma unroll 16
+        for (int p = 0; p < hp; ++p) acc += src[(size_t)p * args.nrm_ss_ld];
+      }
+      nrm_half[nt] = acc;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (nt < 64)
+        nrm_inv[nt] = n0 + nt < args.N ? 1.0f / sqrtf((nrm_half[nt] + nrm_half[64 + nt]) / (float)args.nrm_D + 1e-6f)
+                                       : 0.f;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      // thread nt owns 16-byte chunk position pc of rows r0 + 16j; with the 128-byte swizzle those hold
+      // the same 8 features lc of every K block
+      const int pc = nt & 7, r0 = nt >> 3, lc = pc ^ (r0 & 7);
+      for (int i = 0; i < nkt && !flags[0]; ++i) {
+        const int s = i % C::STAGES;
+        if (!mbar_wait(&full_bar[s], (uint32_t)(i / C::STAGES) & 1u, args.status, P5_ERR_WAIT_FULL)) {
+          flags[0] = 1;
+          break;
+        }
+        float sc[8], sh[8];
+        unpack8(reinterpret_cast<const uint4*>(nrm_sc)[i * 8 + lc], sc);
+        unpack8(reinterpret_cast<const uint4*>(nrm_sh)[i * 8 + lc], sh);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) sc[q] = rbf(1.0f + sc[q]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int r = r0 + 16 * j;
+          uint4* ptr = reinterpret_cast<uint4*>(sB + s * C::B_BYTES + r * 128 + pc * 16);
+          float xv[8];
+          unpack8(*ptr, xv);
+          const float inv = nrm_inv[r];
+          uint32_t w[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float a0 = xv[2 * q] * inv * sc[2 * q] + sh[2 * q];
+            const float a1 = xv[2 * q + 1] * inv * sc[2 * q + 1] + sh[2 * q + 1];
+            w[q] = inv != 0.f ? pack_bf2(a0, a1) : 0u;
+          }
+          *ptr = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+        mbar_arrive(&ready_bar[s]);
+      }
+    }
     // partial tile -> own shared memory (zeros when this split had no K-tiles or gave up)
     const int sub = warp & 3;
     const bool ok = mbar_wait(accum_bar, 0, args.status, P5_ERR_WAIT_ACCUM) && !flags[0] && nkt > 0;

@@ -201,7 +201,11 @@ __global__ void embed_text_kernel(const int32_t* tokens, const bf16* table, bf16
 
 // ---------------------------------------------------------------- action projections (fp32 math)
 // action_in_proj: y[t][o] = R(sum_k x[t][k] W[o][k] + b[o]), x fp32 [T][32] (nnx.Linear in fp32)
-__global__ void action_in_kernel(const float* xt, const bf16* W, const bf16* b, bf16* y, int T, int D) {
+// ss_out (optional): per-token partial sums of squares of the stored outputs, one per 16 output
+// features, ss_out[(o / 16) * ss_ld + t] (the fused adaRMSNorm of the next projection reads them);
+// requires D % 32 == 0 so that every warp is whole.
+__global__ void action_in_kernel(const float* xt, const bf16* W, const bf16* b, bf16* y, int T, int D,
+                                 float* ss_out, int ss_ld) {
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   pdl_wait();
   if (idx >= (long)T * D) return;
@@ -225,7 +229,14 @@ __global__ void action_in_kernel(const float* xt, const bf16* W, const bf16* b, 
     acc += x1.z * wf[6];
     acc += x1.w * wf[7];
   }
-  y[idx] = tobf(acc + bf(b[o]));
+  const bf16 yb = tobf(acc + bf(b[o]));
+  y[idx] = yb;
+  if (ss_out) {
+    float sq = bf(yb) * bf(yb);
+#pragma unroll
+    for (int o2 = 8; o2; o2 >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o2);
+    if ((threadIdx.x & 15) == 0) ss_out[(size_t)(o >> 4) * ss_ld + t] = sq;
+  }
   pdl_launch_dependents();
 }
 

@@ -386,7 +386,7 @@ bool micro_step(pi05_engine* e, int nb, const float* h_t) {
     const long n = (long)Rs * P5_ACT_D;
     flow_inputs_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(T->d_eps, T->d_act, T->d_t, T->d_xt, T->d_u, H, nb);
     if (!launch(e, action_in_kernel, dim3((Rs * P5_EXP_W + 255) / 256), dim3(256), 0, false, (const float*)T->d_xt,
-                (const bf16*)e->ain_w, (const bf16*)e->ain_b, T->ss[0].xin, Rs, P5_EXP_W))
+                (const bf16*)e->ain_w, (const bf16*)e->ain_b, T->ss[0].xin, Rs, P5_EXP_W, (float*)nullptr, 0))
       return false;
   }
   // ---------------- forward

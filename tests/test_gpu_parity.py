@@ -253,3 +253,26 @@ def test_persistent_denoise_matches_per_kernel_path(pn, monkeypatch, layers, ste
     a, b = out["1"], out["0"]
     assert np.isfinite(a).all()
     assert np.abs(a - b).max() <= 1e-2 and cos(a, b) >= 0.9999, (np.abs(a - b).max(), cos(a, b))
+
+
+@pytest.mark.parametrize("layers,steps", [(2, 2), (18, 10)])
+def test_fused_norm_denoise_matches_separate_norm(pn, monkeypatch, layers, steps):
+    """One-sample denoise with adaRMSNorm folded into the q/k/v and gate/up cluster GEMMs (sums of
+    squares from the producers' epilogues, normalisation of the token tile in shared memory) against
+    the separate rmsnorm launches: same rounding points, sums of squares in a different order."""
+    cfg = pn.Config.make(siglip_layers=0, gemma_layers=layers, num_steps=steps)
+    noise = pn.synth_noise(5, 0)
+    out, launches = {}, {}
+    for fuse in ("1", "0"):
+        monkeypatch.setenv("PI05_FUSE_NORM", fuse)
+        eng = pn.Engine(cfg, max_batch=1)
+        eng.init_random_weights(6)
+        eng.synth_prefix_cache(1, seed=6)
+        out[fuse] = eng.denoise(noise[None])[0]
+        launches[fuse] = eng.graph_launches("denoise", 1)
+        if fuse == "1":
+            assert np.array_equal(eng.denoise(noise[None])[0], out[fuse])  # deterministic
+    assert launches["0"] - launches["1"] == 2 * layers * steps, launches
+    a, b = out["1"], out["0"]
+    assert np.isfinite(a).all()
+    assert np.abs(a - b).max() <= 1e-2 and cos(a, b) >= 0.9999, (np.abs(a - b).max(), cos(a, b))
