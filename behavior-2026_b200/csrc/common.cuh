@@ -159,6 +159,19 @@ __device__ __forceinline__ uint32_t cluster_size() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// split form of cluster_sync: arrive now, wait later (all threads of every CTA execute both)
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from this CTA's shared memory
+// into the shared memory of a CTA of the cluster (`dst`, `bar`: shared::cluster addresses from map_peer);
+// the bytes are counted on that CTA's mbarrier.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "r"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
 // shared::cluster address of the same shared variable in CTA `rank` of this cluster
 __device__ __forceinline__ uint32_t map_peer(uint32_t saddr, uint32_t rank) {
   uint32_t r;

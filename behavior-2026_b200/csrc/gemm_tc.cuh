@@ -664,25 +664,41 @@ __device__ __forceinline__ float swap_epi_value(const GemmArgs& a, float v, cons
 // Cluster reduce of a swap-orientation tile: CTA `rank` of S owns rows [rank*R, rank*R+R), R = 128/S.
 // Items = (row, group of 4 tokens); consecutive threads take consecutive weight rows of one group, so
 // the stores of each token are contiguous across the warp (R*BN/4 is a multiple of 256: all eight
-// warps of the CTA take part).  An item's
-// epilogue operands (bias, residual, gate) are loaded from global memory before, and in flight with,
-// its S partial loads; the partials are summed in rank order (deterministic).  Measured in the
-// denoise graph: batching more items per pass, or fetching operands before the cluster barrier, costs
-// more (registers, and the next kernel's early start under programmatic dependent launch) than it saves.
-template <int BN, int EPI, int S>
-__device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_base, int rank, int m0, int n0,
+// warps of the CTA take part).  The partials are summed in rank order (deterministic).
+//   PUSH: every CTA has already sent row slice p of its partial tile to CTA p with one bulk copy
+//     (recv slot = source rank); an item's epilogue operands (bias, residual, gate) are requested from
+//     global memory, then the thread waits for the S-1 incoming slices (first item only), arrives on the
+//     cluster barrier that guards the copies' source buffers, and sums from its own shared memory.
+//     Measured on B200: S scattered 16-byte loads per thread from the peers' shared memory are bound
+//     by the request rate (~6,000 cycles for S = 8); S-1 bulk copies of R rows each are not.
+//   otherwise (tiles too wide for a second partial buffer): S direct loads from the peers' memory.
+template <int BN, int EPI, int S, bool PUSH>
+__device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_base, const float* red,
+                                            const float* recv, uint64_t* recv_bar, int rank, int m0, int n0,
                                             int rtid) {
   constexpr int R = 128 / S, RED_LD = BN + 4, ITEMS = R * (BN / 4);
+  static_assert(ITEMS >= 256, "every thread must take a first item (it arrives on the cluster barrier there)");
 #pragma unroll 1
   for (int it = rtid; it < ITEMS; it += 256) {
     const int lr = it % R, cg = it / R;
     const int f = m0 + rank * R + lr;
     SwapEpiOps o;
     swap_epi_load<EPI>(args, f, n0 + cg * 4, o);
-    const uint32_t addr = red_base + (uint32_t)((rank * R + lr) * RED_LD + cg * 4) * 4u;
     float4 pv[S];
+    if (PUSH) {
+      if (it == rtid) {
+        mbar_wait(recv_bar, 0, args.status, P5_ERR_WAIT_FULL);
+        cluster_arrive_release();  // the copies into this CTA have landed
+      }
 #pragma unroll
-    for (int p = 0; p < S; ++p) pv[p] = ld_peer_v4(map_peer(addr, (uint32_t)p));
+      for (int p = 0; p < S; ++p)
+        pv[p] = p == rank ? *reinterpret_cast<const float4*>(red + (rank * R + lr) * RED_LD + cg * 4)
+                          : *reinterpret_cast<const float4*>(recv + (p * R + lr) * RED_LD + cg * 4);
+    } else {
+      const uint32_t addr = red_base + (uint32_t)((rank * R + lr) * RED_LD + cg * 4) * 4u;
+#pragma unroll
+      for (int p = 0; p < S; ++p) pv[p] = ld_peer_v4(map_peer(addr, (uint32_t)p));
+    }
     float v[4] = {0.f, 0.f, 0.f, 0.f}, sq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int p = 0; p < S; ++p) {
@@ -758,6 +774,8 @@ __global__ void __launch_bounds__(256, 2)
   using C = GemmCfg<BN>;
   constexpr int RED_LD = BN + 4;  // fp32 partial row stride: 16-byte rows, 8 rows hit 8 distinct 16-byte slots
   static_assert(128 * RED_LD * 4 <= C::STAGES * C::STAGE_BYTES, "partial tile must fit in the stage buffers");
+  // second tile-sized buffer (received slices) behind the partial tile, also in the stage buffers
+  constexpr bool PUSH = 2 * 128 * RED_LD * 4 <= C::STAGES * C::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
@@ -768,7 +786,8 @@ __global__ void __launch_bounds__(256, 2)
   uint64_t* empty_bar = full_bar + C::STAGES;
   uint64_t* accum_bar = empty_bar + C::STAGES;
   uint64_t* ready_bar = accum_bar + 1;  // fused adaRMSNorm: B stage normalised in place
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ready_bar + C::STAGES);
+  uint64_t* recv_bar = ready_bar + C::STAGES;  // partial-tile slices from the other CTAs of the cluster
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* nrm_inv = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + 256);  // [64]
   float* nrm_half = nrm_inv + 64;                                                      // [2][64]
@@ -794,8 +813,10 @@ __global__ void __launch_bounds__(256, 2)
     mbar_init(accum_bar, 1);
     if (nrm)
       for (int s = 0; s < C::STAGES; ++s) mbar_init(&ready_bar[s], 128);
+    mbar_init(recv_bar, 1);
     flags[0] = 0;
     fence_barrier_init();
+    if (PUSH) mbar_arrive_expect_tx(recv_bar, (uint32_t)(S - 1) * (128 / S) * RED_LD * 4);
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
   }
@@ -925,22 +946,35 @@ __global__ void __launch_bounds__(256, 2)
                                   __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
                     : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    if (PUSH) fence_proxy_async_smem();  // the partial tile is the source of bulk copies
   }
   tc_fence_before();
-  cluster_sync();  // every partial tile of the cluster is in shared memory
+  cluster_sync();  // every partial tile of the cluster is in shared memory, every CTA's MMAs are done
 
+  const uint32_t red_base = smem_u32(red);
+  const float* recv = red + 128 * RED_LD;
+  if (PUSH && warp == 0 && lane < S && lane != rank) {
+    // rows [lane*R, lane*R+R) of this CTA's partial -> slot `rank` of CTA `lane`'s receive buffer
+    const uint32_t slice = (uint32_t)(128 / S) * RED_LD * 4;
+    bulk_copy_to_peer(map_peer(smem_u32(recv) + (uint32_t)rank * slice, (uint32_t)lane),
+                      red_base + (uint32_t)lane * slice, slice, map_peer(smem_u32(recv_bar), (uint32_t)lane));
+  }
   {  // all eight warps reduce (the producer and MMA warps are done by now)
     if (args.pdl) pdl_wait();
     const int rtid = threadIdx.x;
-    const uint32_t red_base = smem_u32(red);
     switch (S) {
-      case 2: swap_reduce<BN, EPI, 2>(args, red_base, rank, m0, n0, rtid); break;
-      case 4: swap_reduce<BN, EPI, 4>(args, red_base, rank, m0, n0, rtid); break;
-      case 8: swap_reduce<BN, EPI, 8>(args, red_base, rank, m0, n0, rtid); break;
-      default: swap_reduce<BN, EPI, 1>(args, red_base, rank, m0, n0, rtid); break;
+      case 2: swap_reduce<BN, EPI, 2, PUSH>(args, red_base, red, recv, recv_bar, rank, m0, n0, rtid); break;
+      case 4: swap_reduce<BN, EPI, 4, PUSH>(args, red_base, red, recv, recv_bar, rank, m0, n0, rtid); break;
+      case 8: swap_reduce<BN, EPI, 8, PUSH>(args, red_base, red, recv, recv_bar, rank, m0, n0, rtid); break;
+      default: swap_reduce<BN, EPI, 1, PUSH>(args, red_base, red, recv, recv_bar, rank, m0, n0, rtid); break;
     }
   }
-  cluster_sync();  // peers are done reading this CTA's partial tile
+  // PUSH: every CTA's incoming copies have landed, so this CTA's outgoing copies have read their source;
+  // otherwise: the peers are done reading this CTA's partial tile
+  if (PUSH)
+    cluster_wait_acquire();
+  else
+    cluster_sync();
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TCOLS);
