@@ -37,6 +37,10 @@ struct AttnTcCfg {
   static constexpr int BAR_OFF = Q_BYTES + NS * SLOT + 2 * P_BYTES;
   static constexpr int SMEM = 1024 + BAR_OFF + 256;
   static constexpr float RESCALE_LOG2 = 8.0f;
+  // split-partial staging rows (fp32, 1 KB + 16 B pitch: eight consecutive rows hit distinct 16-byte
+  // bank groups), over the Q and K/V ring buffers once every MMA is done
+  static constexpr int STG_PITCH = HD * 4 + 16;
+  static_assert(ROWS * STG_PITCH <= Q_BYTES + NS * SLOT, "staging must fit in the Q and ring buffers");
 };
 
 // One 128-row block (rb) of one batch item / key split (z) with 384 threads: warp 0 loads, warp 1
@@ -314,9 +318,20 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
                               pack_bf2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
                               pack_bf2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
       } else {
-        uint4* dst = reinterpret_cast<uint4*>(a.ws_o + base * C::HD + col);
+        // split partial: staged in the (now idle) Q / K / V buffers, written out by row below
+        uint4* dst = reinterpret_cast<uint4*>(smem + r * C::STG_PITCH + col * 4);
 #pragma unroll
         for (int q = 0; q < 8; ++q) dst[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+      }
+    }
+    if (a.splits > 1) {
+      // one 1 KB bulk copy per row: a thread's own row is 1 KB away from its lane neighbours', so
+      // direct stores would be 32 separate segments per warp instruction
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // both warpgroups' halves of every row are staged
+      if (store && g == 0) {
+        bulk_store_global(a.ws_o + base * C::HD, smem_u32(smem + r * C::STG_PITCH), C::HD * 4);
+        bulk_store_wait();
       }
     }
     if (store && g == 0) {
