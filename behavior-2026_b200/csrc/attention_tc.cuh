@@ -331,7 +331,7 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
       asm volatile("bar.sync 1, 256;" ::: "memory");  // both warpgroups' halves of every row are staged
       if (store && g == 0) {
         bulk_store_global(a.ws_o + base * C::HD, smem_u32(smem + r * C::STG_PITCH), C::HD * 4);
-        bulk_store_wait();
+        bulk_store_wait_read();  // the staging buffer must outlive the copy's reads
       }
     }
     if (store && g == 0) {

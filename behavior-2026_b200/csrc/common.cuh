@@ -160,17 +160,22 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from this CTA's shared memory
-// to global memory, tracked in the thread's bulk async-group (bulk_store_wait waits for completion).
+// to global memory, tracked in the thread's bulk async-group (bulk_store_wait_read waits until the source
+// has been read; the writes themselves are complete, and visible to dependent grids, when the grid is).
 __device__ __forceinline__ void bulk_store_global(void* gdst, uint32_t src, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(gdst)),
                "r"(src), "r"(bytes)
                : "memory");
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
-__device__ __forceinline__ void bulk_store_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-// split form of cluster_sync: arrive now, wait later (all threads of every CTA execute both)
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+__device__ __forceinline__ void bulk_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// split form of cluster_sync: arrive now, wait later (all threads of every CTA execute both).  The
+// relaxed arrive orders none of the thread's memory accesses: for signalling what an mbarrier already
+// made known (e.g. incoming bulk copies have landed).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 // Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from this CTA's shared memory

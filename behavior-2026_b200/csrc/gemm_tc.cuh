@@ -691,7 +691,7 @@ __device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_b
     if (PUSH) {
       if (it == rtid) {
         mbar_wait(recv_bar, 0, args.status, P5_ERR_WAIT_FULL);
-        cluster_arrive_release();  // the copies into this CTA have landed
+        cluster_arrive_relaxed();  // the copies into this CTA have landed
       }
 #pragma unroll
       for (int p = 0; p < S; ++p)
