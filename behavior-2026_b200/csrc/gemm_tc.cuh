@@ -681,6 +681,80 @@ __device__ __forceinline__ void swap_reduce(const GemmArgs& args, uint32_t red_b
                                             int rtid) {
   constexpr int R = 128 / S, RED_LD = BN + 4, ITEMS = R * (BN / 4);
   static_assert(ITEMS >= 256, "every thread must take a first item (it arrives on the cluster barrier there)");
+  // GeGLU (gate, up) and RoPE (dim j, dim j+128) rows come in neighbouring pairs: one item per pair and
+  // 4 tokens when that still gives every thread a first item (no shuffles, every lane stores)
+  constexpr int RP = R / 2, ITEMS_P = RP * (BN / 4);
+  constexpr bool PAIR = (EPI == EPI_GEGLU || EPI == EPI_ROPE) && ITEMS_P >= 256;
+  if (PAIR) {
+#pragma unroll 1
+    for (int it = rtid; it < ITEMS_P; it += 256) {
+      const int lp = it % RP, cg = it / RP;
+      const int lr = 2 * lp, f = m0 + rank * R + lr;  // even row of the pair
+      SwapEpiOps o;
+      swap_epi_load<EPI>(args, f, n0 + cg * 4, o);
+      const float bias1 = (EPI == EPI_GEGLU && args.bias) ? bf(args.bias[min(f + 1, args.M - 1)]) : 0.f;
+      float4 pa[S], pb[S];
+      if (PUSH) {
+        if (it == rtid) {
+          mbar_wait(recv_bar, 0, args.status, P5_ERR_WAIT_FULL);
+          cluster_arrive_relaxed();  // the copies into this CTA have landed
+        }
+#pragma unroll
+        for (int p = 0; p < S; ++p) {
+          const float* src = p == rank ? red + (rank * R + lr) * RED_LD : recv + (p * R + lr) * RED_LD;
+          pa[p] = *reinterpret_cast<const float4*>(src + cg * 4);
+          pb[p] = *reinterpret_cast<const float4*>(src + RED_LD + cg * 4);
+        }
+      } else {
+        const uint32_t addr = red_base + (uint32_t)((rank * R + lr) * RED_LD + cg * 4) * 4u;
+#pragma unroll
+        for (int p = 0; p < S; ++p) {
+          pa[p] = ld_peer_v4(map_peer(addr, (uint32_t)p));
+          pb[p] = ld_peer_v4(map_peer(addr + RED_LD * 4u, (uint32_t)p));
+        }
+      }
+      float va[4] = {0.f, 0.f, 0.f, 0.f}, vb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < S; ++p) {
+        va[0] += pa[p].x;
+        va[1] += pa[p].y;
+        va[2] += pa[p].z;
+        va[3] += pa[p].w;
+        vb[0] += pb[p].x;
+        vb[1] += pb[p].y;
+        vb[2] += pb[p].z;
+        vb[3] += pb[p].w;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int t = n0 + cg * 4 + q;
+        if (f >= args.M || t >= args.N) continue;
+        if (EPI == EPI_GEGLU) {
+          const float gt = rbf(va[q] * args.out_scale + o.bias), up = rbf(vb[q] * args.out_scale + bias1);
+          args.out[(size_t)t * args.ld_out + f / 2] = tobf(rbf(gelu_tanh(gt)) * up);
+        } else {
+          const float x1 = rbf(va[q]), x2 = rbf(vb[q]);
+          const int hb = f >> 8, j = (f & 255) >> 1;
+          if (hb == 9) {
+            args.rope_v[(size_t)t * args.rope_ld_kv + j] = tobf(x1);
+            args.rope_v[(size_t)t * args.rope_ld_kv + j + 128] = tobf(x2);
+          } else {
+            const float cs = o.res[q], sn = o.gate[q];
+            const float ra = rbf(x1 * cs - x2 * sn);
+            const float rc = rbf(x2 * cs + x1 * sn);
+            if (hb == 8) {
+              args.rope_k[(size_t)t * args.rope_ld_kv + j] = tobf(ra);
+              args.rope_k[(size_t)t * args.rope_ld_kv + j + 128] = tobf(rc);
+            } else {
+              args.out[(size_t)t * args.ld_out + hb * 256 + j] = tobf(ra * 0.0625f);
+              args.out[(size_t)t * args.ld_out + hb * 256 + j + 128] = tobf(rc * 0.0625f);
+            }
+          }
+        }
+      }
+    }
+    return;
+  }
 #pragma unroll 1
   for (int it = rtid; it < ITEMS; it += 256) {
     const int lr = it % R, cg = it / R;

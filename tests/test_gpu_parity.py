@@ -87,6 +87,27 @@ def test_linear_epilogues_match_torch(pn, torch_cuda, epi, T):
     assert err <= 2e-2 * max(1.0, ref.abs().max().item()), (epi, err)
 
 
+@pytest.mark.parametrize("T", [50, 64, 100])
+def test_linear_geglu_row_pairs_match_torch(pn, torch_cuda, T):
+    """Few-token gate/up projection of the action expert (8192 interleaved rows): the cluster reduce
+    takes one (gate, up) row pair per item."""
+    torch = torch_cuda
+    F, K = 8192, 1024
+    g = torch.Generator(device="cuda").manual_seed(29 + T)
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(F, K, device="cuda", generator=g) * 0.03).bfloat16()
+    eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), max_batch=1)
+    acc = x.float() @ w.float().t()
+    rb = lambda t: t.bfloat16().float()
+    ref = rb(torch.nn.functional.gelu(rb(acc[:, 0::2]), approximate="tanh")) * rb(acc[:, 1::2])
+    out = torch.empty(T, F // 2, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()  # inputs and reference come from torch's stream; the engine has its own
+    eng.op_linear(x, w, out, "geglu")
+    eng.sync()
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2 * max(1.0, ref.abs().max().item()), err
+
+
 @pytest.mark.parametrize("shape", [(768, 1024, 4096), (4096, 2560, 1024)], ids=["long_k_few_tiles", "wide_tiles"])
 @pytest.mark.parametrize("epi", ["store", "gelu", "resid", "gated", "geglu", "f32"])
 def test_linear_tile_shapes_epilogues(pn, torch_cuda, epi, shape):
