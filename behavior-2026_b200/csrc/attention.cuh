@@ -276,16 +276,38 @@ __device__ __forceinline__ void attn_combine_item(const AttnArgs& a, long idx) {
   const int d2 = idx % (HD / 2);
   const long br = idx / (HD / 2);
   const int row = br % rows_total, b = br / rows_total;
-  float M = -1e30f;
-  for (int s = 0; s < a.splits; ++s) M = fmaxf(M, a.ws_ml[(((long)b * a.splits + s) * rows_total + row) * 2]);
-  float L = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
-    const long base = ((long)b * a.splits + s) * rows_total + row;
-    const float w = __expf(a.ws_ml[base * 2] - M);
-    L += a.ws_ml[base * 2 + 1] * w;
-    const float2 p = *reinterpret_cast<const float2*>(a.ws_o + base * HD + 2 * d2);
-    o0 += p.x * w;
-    o1 += p.y * w;
+  float M = -1e30f, L = 0.f, o0 = 0.f, o1 = 0.f;
+  constexpr int SMAX = 16;
+  if (a.splits <= SMAX) {
+    // every split's loads in flight together: indices past the split count re-read the last split
+    // (weight 0), so the loads carry no conditions; the sums still run in split order
+    float2 ml[SMAX], ov[SMAX];
+#pragma unroll
+    for (int k = 0; k < SMAX; ++k) {
+      const long base = ((long)b * a.splits + min(k, a.splits - 1)) * rows_total + row;
+      ml[k] = *reinterpret_cast<const float2*>(a.ws_ml + base * 2);
+      ov[k] = *reinterpret_cast<const float2*>(a.ws_o + base * HD + 2 * d2);
+    }
+#pragma unroll
+    for (int k = 0; k < SMAX; ++k) M = k < a.splits ? fmaxf(M, ml[k].x) : M;
+#pragma unroll
+    for (int k = 0; k < SMAX; ++k) {
+      if (k >= a.splits) break;
+      const float w = __expf(ml[k].x - M);
+      L += ml[k].y * w;
+      o0 += ov[k].x * w;
+      o1 += ov[k].y * w;
+    }
+  } else {
+    for (int s = 0; s < a.splits; ++s) M = fmaxf(M, a.ws_ml[(((long)b * a.splits + s) * rows_total + row) * 2]);
+    for (int s = 0; s < a.splits; ++s) {
+      const long base = ((long)b * a.splits + s) * rows_total + row;
+      const float w = __expf(a.ws_ml[base * 2] - M);
+      L += a.ws_ml[base * 2 + 1] * w;
+      const float2 p = *reinterpret_cast<const float2*>(a.ws_o + base * HD + 2 * d2);
+      o0 += p.x * w;
+      o1 += p.y * w;
+    }
   }
   const float inv = L > 0.f ? 1.0f / L : 0.f;
   const int tok = a.G > 1 ? row / a.G : row;

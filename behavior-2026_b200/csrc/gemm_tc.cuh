@@ -954,27 +954,30 @@ __global__ void __launch_bounds__(256, 2)
       // (64 token rows x 64 features, 128-byte swizzled rows) is normalised in place before the MMAs
       const int nt = threadIdx.x - 128, tt = nt & 63, half = nt >> 6;
       if (args.pdl) pdl_wait();
-      const int kbase = kt0 * C::BK;
-      for (int c = nt; c < nkt * C::BK / 8; c += 128) {
-        reinterpret_cast<uint4*>(nrm_sc)[c] = reinterpret_cast<const uint4*>(args.nrm_scale + kbase)[c];
-        reinterpret_cast<uint4*>(nrm_sh)[c] = reinterpret_cast<const uint4*>(args.nrm_shift + kbase)[c];
-      }
+      // every global load is issued before the first shared-memory store (the compiler cannot tell
+      // them apart, so a store in between would hold the later loads back by a round trip); tokens
+      // past the tile's extent read the last token's partials (never used), so the loads carry no
+      // conditions.  The K slice has at most SWAP_NRM_KMAX features: one 8-feature chunk per thread.
+      const int kbase = kt0 * C::BK, nch = nkt * C::BK / 8;
+      const int hp = args.nrm_parts / 2, p0 = half * hp;
+      const float* src = args.nrm_ss + (size_t)p0 * args.nrm_ss_ld + min(n0 + tt, args.N - 1);
       float acc = 0.f;
-      {
-        // tokens past the tile's extent read the last token's partials (never used): no conditions,
-        // so a half's 32 loads are in flight together
-        const int hp = args.nrm_parts / 2, p0 = half * hp;
-        const float* src = args.nrm_ss + (size_t)p0 * args.nrm_ss_ld + min(n0 + tt, args.N - 1);
-        if (hp == 32) {
-          float v[32];
+      const int kb = nch > 0 ? kbase : 0, cc = nch > 0 ? min(nt, nch - 1) : 0;  // a split without K tiles reads chunk 0
+      const uint4 scv = reinterpret_cast<const uint4*>(args.nrm_scale + kb)[cc];
+      const uint4 shv = reinterpret_cast<const uint4*>(args.nrm_shift + kb)[cc];
+      if (hp == 32) {
+        float v[32];
 #pragma unroll
-          for (int p = 0; p < 32; ++p) v[p] = src[(size_t)p * args.nrm_ss_ld];
+        for (int p = 0; p < 32; ++p) v[p] = src[(size_t)p * args.nrm_ss_ld];
 #pragma unroll
-          for (int p = 0; p < 32; ++p) acc += v[p];
-        } else {
+        for (int p = 0; p < 32; ++p) acc += v[p];
+      } else {
 #pragma unroll 8
-          for (int p = 0; p < hp; ++p) acc += src[(size_t)p * args.nrm_ss_ld];
-        }
+        for (int p = 0; p < hp; ++p) acc += src[(size_t)p * args.nrm_ss_ld];
+      }
+      if (nt < nch) {
+        reinterpret_cast<uint4*>(nrm_sc)[nt] = scv;
+        reinterpret_cast<uint4*>(nrm_sh)[nt] = shv;
       }
       nrm_half[nt] = acc;
       asm volatile("bar.sync 1, 128;" ::: "memory");
