@@ -1886,7 +1886,7 @@ int pi05_op_bench_linear(pi05_engine* e, int T, int F, int K, int epi, int reps,
 
 int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, int ldq, const void* k, const void* v,
                       void* out, int splits) {
-  if (!e || batch < 1 || T < 1 || S < 1 || ldq < P5_QDIM || ldq % 8 || !q || !k || !v || !out || splits < 1)
+  if (!e || batch < 1 || T < 1 || S < 1 || ldq < P5_QDIM || ldq % 8 || !q || !k || !v || !out || splits < 0)
     return PI05_ERR_ARG;
   cudaSetDevice(e->device);
   AttnArgs at = {};
@@ -1906,8 +1906,8 @@ int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, in
   at.T = T;
   at.G = P5_NH;
   at.qdiv = 1.0f;
-  at.splits = splits;
-  at.force_splits = splits;
+  at.splits = splits > 0 ? splits : 8;
+  at.force_splits = splits;  // 0: chosen by the engine
   if (!attention(e, at, batch, P5_HD)) return fail_code(e);
   return PI05_OK;
 }

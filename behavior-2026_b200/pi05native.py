@@ -250,7 +250,8 @@ class Engine:
         return us.value
 
     def op_attention(self, q, k, v, out, splits=1):
-        """q [b][T][ldq] (heads at column 0), k/v [b][S][256], out [b][T][2048]; all CUDA bf16 tensors."""
+        """q [b][T][ldq] (heads at column 0), k/v [b][S][256], out [b][T][2048]; all CUDA bf16 tensors.
+        splits = 0 lets the engine choose the key splits (as inside pi05_denoise)."""
         b, T, ldq = q.shape
         S = k.shape[1]
         p = lambda t: ctypes.c_void_p(t.data_ptr())

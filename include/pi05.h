@@ -148,7 +148,8 @@ PI05_API int pi05_lora_load_state(pi05_engine* e, const char* path);
  *   (w rows interleaved gate/up, F' = F/2), 5 fp32 out.  bias[F] optional (NULL).
  *   No counterpart in the reference's ABI: its GEMM (src/gemm.cuh, π05_네이티브엔진.md:102-105) was internal.
  * pi05_op_attention: out[b][t][8*256] = softmax(q k^T) v with q [b][T][ldq] (8 heads x 256 at column 0,
- *   already scaled), keys/values [b][S][256] bf16.  Asynchronous; call pi05_sync. */
+ *   already scaled), keys/values [b][S][256] bf16; `splits` key splits (0: the engine chooses, as inside
+ *   pi05_denoise).  Asynchronous; call pi05_sync. */
 PI05_API int pi05_op_linear(pi05_engine* e, int T, int F, int K, const void* x, const void* w, const void* bias,
                             const void* res, const void* gate, int epi, void* out);
 PI05_API int pi05_op_attention(pi05_engine* e, int batch, int T, int S, const void* q, int ldq, const void* k,
