@@ -310,7 +310,8 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
       const int col = g * (C::HD / 2) + c;
       if (!store) {
       } else if (a.splits == 1) {
-        uint4* dst = reinterpret_cast<uint4*>(a.out + b * a.o_bstride + (long)tok * a.ldo + hq * C::HD + col);
+        // the normalised bf16 row, staged like the split partials and written out by row below
+        uint4* dst = reinterpret_cast<uint4*>(smem + r * C::STG_PITCH + col * 2);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
           dst[q] = make_uint4(pack_bf2(__uint_as_float(o[8 * q]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
@@ -324,13 +325,17 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
         for (int q = 0; q < 8; ++q) dst[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
       }
     }
-    if (a.splits > 1) {
-      // one 1 KB bulk copy per row: a thread's own row is 1 KB away from its lane neighbours', so
-      // direct stores would be 32 separate segments per warp instruction
+    {
+      // one bulk copy per row (512 B of bf16 output, or the 1 KB fp32 split partial): a thread's own
+      // row is far from its lane neighbours', so direct stores would be 32 segments per warp instruction
       fence_proxy_async_smem();
       asm volatile("bar.sync 1, 256;" ::: "memory");  // both warpgroups' halves of every row are staged
       if (store && g == 0) {
-        bulk_store_global(a.ws_o + base * C::HD, smem_u32(smem + r * C::STG_PITCH), C::HD * 4);
+        if (a.splits == 1)
+          bulk_store_global(a.out + b * a.o_bstride + (long)tok * a.ldo + hq * C::HD, smem_u32(smem + r * C::STG_PITCH),
+                            C::HD * 2);
+        else
+          bulk_store_global(a.ws_o + base * C::HD, smem_u32(smem + r * C::STG_PITCH), C::HD * 4);
         bulk_store_wait_read();  // the staging buffer must outlive the copy's reads
       }
     }

@@ -647,12 +647,16 @@ bool attention_tc(pi05_engine* e, const AttnArgs& a0, int batch) {
   if (a.force_splits > 0) {
     splits = a.lse ? 1 : std::min(a.force_splits, ntiles);
   } else if (!a.lse && ctas < e->num_sms) {
-    // waves x (tiles per CTA + ~2 tiles of fixed cost: Q load, epilogue), +1 for the combine pass
+    // waves x (tiles per CTA + ~2 tiles of fixed cost: Q load, epilogue); a split adds the fp32 partial
+    // epilogue (~2 tiles) and the merge pass, whose traffic grows with rows x splits (measured in the
+    // CUDA graph: 968-token prefix 15.10 -> 14.84 ms at bs1 without its 2 splits; the 50-token
+    // expert keeps its 9)
     long best = -1;
     for (int s = 1; s <= std::min(ntiles, 16); ++s) {
       const int t = std::max((ntiles + s - 1) / s, s > 1 ? 2 : 1);
       const int se = (ntiles + t - 1) / t;
-      const long cost = (ctas * se + e->num_sms - 1) / e->num_sms * (t + 2) + (se > 1 ? 1 : 0);
+      const long merge = se > 1 ? 2 + (long)rows * se / 2048 : 0;
+      const long cost = (ctas * se + e->num_sms - 1) / e->num_sms * (t + 2) + merge;
       if (best < 0 || cost < best) {
         best = cost;
         splits = se;
