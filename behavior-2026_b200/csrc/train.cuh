@@ -14,6 +14,7 @@
 // Activations of every layer are kept (B200 has the memory), so nothing is recomputed.
 #pragma once
 #include "attention_bwd.cuh"
+#include "attention_bwd_tc.cuh"
 #include "train_kernels.cuh"
 
 namespace {
@@ -95,6 +96,40 @@ void lora_layout(pi05_engine* e, Trainer* T) {
 }
 
 bool talloc(pi05_engine* e, void** p, size_t bytes) { return dalloc(e, p, bytes); }
+
+// dQ of the attention backward for the query segment a.qs of nb batch items: the tcgen05 kernel
+// (attention_bwd_tc.cuh), or the mma.sync one when PI05_ATTN_TC=0.
+bool attn_bwd_dq(pi05_engine* e, const AttnBwdArgs& a, int nb) {
+  const int rows = a.qs.T * P5_NH;
+  if (!e->attn_tc)
+    return launch(e, attn_bwd_dq_kernel, dim3((rows + 63) / 64, 1, nb), dim3(128), (size_t)ABW_SMEM_DQ, false, a);
+  using C = AttnBwdTcCfg;
+  CUtensorMap tq, tdo, tk1, tv1, tk2, tv2;
+  auto row_map = [&](CUtensorMap* m, const bf16* base, int ld, long bstride) {
+    const uint64_t dims[4] = {P5_HD, 8, (uint64_t)a.qs.T, (uint64_t)nb};
+    const uint64_t st[3] = {P5_HD * 2, (uint64_t)ld * 2, (uint64_t)bstride * 2};
+    const uint32_t box[4] = {64, 8, 16, 1};
+    return make_tmap_nd(e, m, base, 4, dims, st, box);
+  };
+  auto kv_map = [&](CUtensorMap* m, const bf16* base, int len, int ld, long bstride) {
+    const uint64_t dims[3] = {P5_HD, (uint64_t)len, (uint64_t)nb};
+    const uint64_t st[2] = {(uint64_t)ld * 2, (uint64_t)bstride * 2};
+    const uint32_t box[3] = {64, C::KT, 1};
+    return make_tmap_nd(e, m, base, 3, dims, st, box);
+  };
+  if (!row_map(&tq, a.qs.q, a.qs.ldq, a.qs.qb) || !row_map(&tdo, a.qs.dO, a.qs.ldo, a.qs.ob)) return false;
+  if (!kv_map(&tk1, a.k1, a.len1, a.ld1, a.b1stride) || !kv_map(&tv1, a.v1, a.len1, a.ld1, a.b1stride)) return false;
+  if (a.len2 > 0) {
+    if (!kv_map(&tk2, a.k2, a.len2, a.ld2, a.b2stride) || !kv_map(&tv2, a.v2, a.len2, a.ld2, a.b2stride)) return false;
+  } else {
+    tk2 = tk1;
+    tv2 = tv1;
+  }
+  if ((a.ld_dq * 2) % 16 || (a.dq_b * 2) % 16 || ((uintptr_t)a.dq & 15))
+    return set_err(e, "attention backward: dq rows must be 16-byte aligned");
+  return launch(e, attn_bwd_dq_tc_kernel, dim3((rows + C::ROWS - 1) / C::ROWS, 1, nb), dim3(384), (size_t)C::SMEM, false,
+                tq, tdo, tk1, tv1, tk2, tv2, a, e->d_status);
+}
 // token-major transposes ([16n][R]) are TMA operands: rows padded to 16 bytes
 inline long pad8(long r) { return (r + 7) & ~7L; }
 
@@ -209,6 +244,7 @@ bool lora_create(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
       !talloc(e, (void**)&T->dqkv_s, Rs * (P5_QKV + 48) * 2) || !talloc(e, (void**)&T->vT, 48 * pad8(std::max(Rp, Rs)) * 2))
     return false;
   CK(cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DQ));
+  CK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdTcCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_bwd_dkv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DKV));
   CK(cudaFuncSetAttribute(attn_bwd_dkv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DKV));
   CK(cudaStreamSynchronize(e->stream));
@@ -490,7 +526,8 @@ bool micro_step(pi05_engine* e, int nb, const float* h_t) {
       da.out = dact;
       da.ld_out = F;
       if (!linear(e, da)) return false;
-      const long ng = (long)R * F;
+      static_assert(P5_GEM_MLP % 8 == 0 && P5_EXP_MLP % 8 == 0, "geglu_bwd_kernel takes 8 pairs per thread");
+      const long ng = (long)R * (F / 8);
       if (!launch(e, geglu_bwd_kernel, dim3((ng + 255) / 256), dim3(256), 0, false, (const bf16*)S.gu,
                   (const bf16*)dact, F, dgu, 2 * F + 32, R, F))
         return false;
@@ -535,18 +572,14 @@ bool micro_step(pi05_engine* e, int nb, const float* h_t) {
     ab.dq = T->dqkv_s;
     ab.ld_dq = P5_QKV + 48;
     ab.dq_b = (long)H * (P5_QKV + 48);
-    if (!launch(e, attn_bwd_dq_kernel, dim3((Rs / nb * P5_NH + 63) / 64, 1, nb), dim3(128), (size_t)ABW_SMEM_DQ, false,
-                ab))
-      return false;
+    if (!attn_bwd_dq(e, ab, nb)) return false;
     if (!last) {  // dq of the prefix queries (keys: prefix only)
       AttnBwdArgs ap = ab;
       ap.len2 = 0;
       ap.qs = qs_p;
       ap.dq = T->dqkv_p;
       ap.dq_b = (long)P * (P5_QKV + 48);
-      if (!launch(e, attn_bwd_dq_kernel, dim3((P * P5_NH + 63) / 64, 1, nb), dim3(128), (size_t)ABW_SMEM_DQ, false,
-                  ap))
-        return false;
+      if (!attn_bwd_dq(e, ap, nb)) return false;
     } else {
       CK(cudaMemset2DAsync(T->dqkv_p, (size_t)(P5_QKV + 48) * 2, 0, (size_t)P5_QDIM * 2, Rp, e->stream));
     }

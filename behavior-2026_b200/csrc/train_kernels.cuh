@@ -133,17 +133,34 @@ __global__ void grad_to_bf16_kernel(const float* g, bf16* out, int ld_out, const
 }
 
 // GeGLU backward: gu interleaved [T][2F] (gate 2j, up 2j+1), dact [T][F] (ld) -> dgu [T][2F] (ld)
+// 8 consecutive (gate, up) pairs per thread (F % 8 == 0): 32-byte gate/up loads, 16-byte dact loads and
+// stores, one tanh per pair for both the GELU value and its derivative.
 __global__ void geglu_bwd_kernel(const bf16* gu, const bf16* dact, int ld_dact, bf16* dgu, int ld_dgu, int T,
                                  int F) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long)T * F) return;
-  const int t = (int)(i / F), j = (int)(i % F);
-  const float2 p = unpack_bf2(*reinterpret_cast<const uint32_t*>(gu + (long)t * 2 * F + 2 * j));
-  const float g = p.x, u = p.y;
-  const float da = bf(dact[(long)t * ld_dact + j]);
-  const float dg = da * u * gelu_tanh_grad(g);
-  const float du = da * rbf(gelu_tanh(g));
-  *reinterpret_cast<uint32_t*>(dgu + (long)t * ld_dgu + 2 * j) = pack_bf2(dg, du);
+  const int fc = F / 8;
+  if (i >= (long)T * fc) return;
+  const int t = (int)(i / fc), j0 = (int)(i % fc) * 8;
+  const uint4* g4 = reinterpret_cast<const uint4*>(gu + (long)t * 2 * F + 2 * j0);
+  const uint4 ga = g4[0], gb = g4[1];
+  const uint4 dv = *reinterpret_cast<const uint4*>(dact + (long)t * ld_dact + j0);
+  const uint32_t gw[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+  float da[8];
+  unpack8(dv, da);
+  uint32_t o[8];
+  const float c = 0.7978845608028654f, a = 0.044715f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float2 p = unpack_bf2(gw[k]);
+    const float g = p.x, u = p.y;
+    const float th = tanhf(c * (g + a * g * g * g));
+    const float grad = 0.5f * (1.0f + th) + 0.5f * g * (1.0f - th * th) * c * (1.0f + 3.0f * a * g * g);
+    const float gel = 0.5f * g * (1.0f + th);
+    o[k] = pack_bf2(da[k] * u * grad, da[k] * rbf(gel));
+  }
+  uint4* dst = reinterpret_cast<uint4*>(dgu + (long)t * ld_dgu + 2 * j0);
+  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
 // RoPE backward on the attention gradients in dqkv (ld): q part was R(rope(q))*1/16, k part R(rope(k)).
