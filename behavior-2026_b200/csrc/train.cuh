@@ -58,6 +58,9 @@ struct Trainer {
   // backward workspaces
   float *gx_p, *gx_s, *Dp, *Ds;
   bf16 *dy_p, *dy_s, *dact_p, *dact_s, *dgu_p, *dgu_s, *dh_p, *dh_s, *do_p, *do_s, *dqkv_p, *dqkv_s, *vT;
+  // fp32 query-split partials of the tensor-core dK / dV kernels: [mb][key blocks][splits][128][256]
+  float* dkv_ws = nullptr;
+  size_t dkv_ws_rows = 0;  // capacity in 256-float rows
 };
 
 namespace {
@@ -129,6 +132,67 @@ bool attn_bwd_dq(pi05_engine* e, const AttnBwdArgs& a, int nb) {
     return set_err(e, "attention backward: dq rows must be 16-byte aligned");
   return launch(e, attn_bwd_dq_tc_kernel, dim3((rows + C::ROWS - 1) / C::ROWS, 1, nb), dim3(384), (size_t)C::SMEM, false,
                 tq, tdo, tk1, tv1, tk2, tv2, a, e->d_status);
+}
+
+// dK and dV of the keys of segment a.kseg against the query segments a.qa (and a.qbseg), for nb batch
+// items: the tcgen05 kernels (query tiles split over CTAs so that ~2 waves of CTAs run, partials
+// summed by attn_bwd_dkv_reduce_kernel), or the mma.sync ones when PI05_ATTN_TC=0.
+bool attn_bwd_dkv(pi05_engine* e, Trainer* T, const AttnBwdArgs& a, int nb) {
+  const int seg_len = a.kseg == 1 ? a.len1 : a.len2;
+  if (!e->attn_tc) {
+    const dim3 g((seg_len + 63) / 64, 1, nb);
+    return launch(e, attn_bwd_dkv_kernel<true>, g, dim3(128), (size_t)ABW_SMEM_DKV, false, a) &&
+           launch(e, attn_bwd_dkv_kernel<false>, g, dim3(128), (size_t)ABW_SMEM_DKV, false, a);
+  }
+  using C = AttnBwdKvCfg;
+  CUtensorMap tk, tv, tqa, tdoa, tqb, tdob;
+  auto key_map = [&](CUtensorMap* m, const bf16* base, int ld, long bstride) {
+    const uint64_t dims[3] = {P5_HD, (uint64_t)seg_len, (uint64_t)nb};
+    const uint64_t st[2] = {(uint64_t)ld * 2, (uint64_t)bstride * 2};
+    const uint32_t box[3] = {64, C::KEYS, 1};
+    return make_tmap_nd(e, m, base, 3, dims, st, box);
+  };
+  auto row_map = [&](CUtensorMap* m, const QSeg& q, bool dO) {
+    const uint64_t dims[4] = {P5_HD, 8, (uint64_t)q.T, (uint64_t)nb};
+    const uint64_t st[3] = {P5_HD * 2, (uint64_t)(dO ? q.ldo : q.ldq) * 2, (uint64_t)(dO ? q.ob : q.qb) * 2};
+    const uint32_t box[4] = {64, 8, 8, 1};  // 8 tokens x 8 heads = one 64-row query tile
+    return make_tmap_nd(e, m, dO ? q.dO : q.q, 4, dims, st, box);
+  };
+  const bf16* kb = a.kseg == 1 ? a.k1 : a.k2;
+  const bf16* vb = a.kseg == 1 ? a.v1 : a.v2;
+  const int ld = a.kseg == 1 ? a.ld1 : a.ld2;
+  const long bs = a.kseg == 1 ? a.b1stride : a.b2stride;
+  if (!key_map(&tk, kb, ld, bs) || !key_map(&tv, vb, ld, bs) || !row_map(&tqa, a.qa, false) ||
+      !row_map(&tdoa, a.qa, true))
+    return false;
+  if (a.nq > 1) {
+    if (!row_map(&tqb, a.qbseg, false) || !row_map(&tdob, a.qbseg, true)) return false;
+  } else {
+    tqb = tqa;
+    tdob = tdoa;
+  }
+  if ((a.ld_dkv * 2) % 16 || (a.dkv_b * 2) % 16 || ((uintptr_t)a.dk & 15) || ((uintptr_t)a.dv & 15))
+    return set_err(e, "attention backward: dk / dv rows must be 16-byte aligned");
+  const int kblocks = (seg_len + C::KEYS - 1) / C::KEYS;
+  const int nt = (a.qa.T + 7) / 8 + (a.nq > 1 ? (a.qbseg.T + 7) / 8 : 0);
+  int splits = std::max(1, (2 * e->num_sms + kblocks * nb - 1) / (kblocks * nb));
+  splits = std::min(std::min(splits, (int)ABW_KV_MAX_SPLITS), std::max(1, nt / 4));
+  while (splits > 1 && (size_t)nb * kblocks * splits * C::KEYS > T->dkv_ws_rows) --splits;
+  const dim3 grid(kblocks, splits, nb);
+  for (int dk = 1; dk >= 0; --dk) {
+    const bool ok = dk ? launch(e, attn_bwd_dkv_tc_kernel<true>, grid, dim3(384), (size_t)C::SMEM, false, tk, tv, tqa,
+                                tdoa, tqb, tdob, a, T->dkv_ws, e->d_status)
+                       : launch(e, attn_bwd_dkv_tc_kernel<false>, grid, dim3(384), (size_t)C::SMEM, false, tk, tv, tqa,
+                                tdoa, tqb, tdob, a, T->dkv_ws, e->d_status);
+    if (!ok) return false;
+    if (splits > 1) {
+      const long n = (long)nb * seg_len * 32;
+      if (!launch(e, attn_bwd_dkv_reduce_kernel, dim3((n + 255) / 256), dim3(256), 0, false, (const float*)T->dkv_ws,
+                  kblocks, splits, seg_len, nb, dk ? a.dk : a.dv, a.ld_dkv, a.dkv_b))
+        return false;
+    }
+  }
+  return true;
 }
 // token-major transposes ([16n][R]) are TMA operands: rows padded to 16 bytes
 inline long pad8(long r) { return (r + 7) & ~7L; }
@@ -243,8 +307,12 @@ bool lora_create(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
       !talloc(e, (void**)&T->do_s, Rs * P5_QDIM * 2) || !talloc(e, (void**)&T->dqkv_p, Rp * (P5_QKV + 48) * 2) ||
       !talloc(e, (void**)&T->dqkv_s, Rs * (P5_QKV + 48) * 2) || !talloc(e, (void**)&T->vT, 48 * pad8(std::max(Rp, Rs)) * 2))
     return false;
+  T->dkv_ws_rows = (size_t)mb * ((P + AttnBwdKvCfg::KEYS - 1) / AttnBwdKvCfg::KEYS) * ABW_KV_MAX_SPLITS * AttnBwdKvCfg::KEYS;
+  if (!talloc(e, (void**)&T->dkv_ws, T->dkv_ws_rows * P5_HD * 4)) return false;
   CK(cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DQ));
   CK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdTcCfg::SMEM));
+  CK(cudaFuncSetAttribute(attn_bwd_dkv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdKvCfg::SMEM));
+  CK(cudaFuncSetAttribute(attn_bwd_dkv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdKvCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_bwd_dkv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DKV));
   CK(cudaFuncSetAttribute(attn_bwd_dkv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DKV));
   CK(cudaStreamSynchronize(e->stream));
@@ -593,10 +661,7 @@ bool micro_step(pi05_engine* e, int nb, const float* h_t) {
     ak.dkv_b = (long)P * (P5_QKV + 48);
     ak.dk = T->dqkv_p + P5_QDIM;
     ak.dv = T->dqkv_p + P5_QDIM + P5_HD;
-    const dim3 gk((P + 63) / 64, 1, nb);
-    if (!launch(e, attn_bwd_dkv_kernel<true>, gk, dim3(128), (size_t)ABW_SMEM_DKV, false, ak) ||
-        !launch(e, attn_bwd_dkv_kernel<false>, gk, dim3(128), (size_t)ABW_SMEM_DKV, false, ak))
-      return false;
+    if (!attn_bwd_dkv(e, T, ak, nb)) return false;
     // dK, dV of the suffix keys: action queries only
     AttnBwdArgs as = ab;
     as.kseg = 2;
@@ -606,10 +671,7 @@ bool micro_step(pi05_engine* e, int nb, const float* h_t) {
     as.dkv_b = (long)H * (P5_QKV + 48);
     as.dk = T->dqkv_s + P5_QDIM;
     as.dv = T->dqkv_s + P5_QDIM + P5_HD;
-    const dim3 gs((H + 63) / 64, 1, nb);
-    if (!launch(e, attn_bwd_dkv_kernel<true>, gs, dim3(128), (size_t)ABW_SMEM_DKV, false, as) ||
-        !launch(e, attn_bwd_dkv_kernel<false>, gs, dim3(128), (size_t)ABW_SMEM_DKV, false, as))
-      return false;
+    if (!attn_bwd_dkv(e, T, as, nb)) return false;
     // RoPE backward, then the q/k/v projections of both stacks
     if (!launch(e, rope_bwd_kernel, dim3(Rs), dim3(256), 0, false, T->dqkv_s, P5_QKV + 48, Rs, H, P,
                 (const float*)e->d_cos, (const float*)e->d_sin, 1) ||
