@@ -380,8 +380,27 @@ bool rms(pi05_engine* e, const bf16* x, bf16* y, int ld_y, const bf16* scale, co
 }
 bool rms_bwd(pi05_engine* e, const bf16* x, const bf16* dy, int ld_dy, const bf16* scale, int rows_per_mod,
              int mod_ld, float* gx, int R, int D) {
+  const bool vec = ld_dy % 8 == 0 && mod_ld % 8 == 0 && (((uintptr_t)x | (uintptr_t)dy | (uintptr_t)scale) & 15) == 0;
+  if (vec && D == 2048)
+    return launch(e, rmsnorm_bwd_vec_kernel<8>, dim3(rows_grid(R)), dim3(256), 0, false, x, dy, ld_dy, scale,
+                  rows_per_mod, mod_ld, gx, R);
+  if (vec && D == 1024)
+    return launch(e, rmsnorm_bwd_vec_kernel<4>, dim3(rows_grid(R)), dim3(256), 0, false, x, dy, ld_dy, scale,
+                  rows_per_mod, mod_ld, gx, R);
   return launch(e, rmsnorm_bwd_kernel, dim3(rows_grid(R)), dim3(256), 0, false, x, dy, ld_dy, scale, rows_per_mod,
                 mod_ld, gx, R, D);
+}
+// fp32 residual-stream gradient -> bf16 rows of ld_out (times the per-sample gate when given)
+bool grad_bf16(pi05_engine* e, const float* g, bf16* out, int ld_out, const bf16* gate, int rows_per_gate, int gate_ld,
+               int R, int D) {
+  if (D % 8 == 0 && ld_out % 8 == 0 && gate_ld % 8 == 0 && (((uintptr_t)out | (uintptr_t)gate) & 15) == 0) {
+    const long n = (long)R * (D / 8);
+    return launch(e, grad_to_bf16_vec_kernel, dim3((n + 255) / 256), dim3(256), 0, false, g, out, ld_out, gate,
+                  rows_per_gate, gate_ld, R, D);
+  }
+  const long n = (long)R * D;
+  return launch(e, grad_to_bf16_kernel, dim3((n + 255) / 256), dim3(256), 0, false, g, out, ld_out, gate, rows_per_gate,
+                gate_ld, R, D);
 }
 
 // ------------------------------------------------------------------ forward of one stack-layer
@@ -584,10 +603,7 @@ bool micro_step(pi05_engine* e, int nb, const float* h_t) {
       bf16* dO = prefix ? T->do_p : T->do_s;
       const int rpg = prefix ? 1 : H, gld = prefix ? 0 : MW;
       // down projection (gated for the suffix)
-      const long n = (long)R * D;
-      if (!launch(e, grad_to_bf16_kernel, dim3((n + 255) / 256), dim3(256), 0, false, (const float*)gx, dy, D + 16,
-                  prefix ? (const bf16*)nullptr : m2 + 2 * D, rpg, gld, R, D))
-        return false;
+      if (!grad_bf16(e, gx, dy, D + 16, prefix ? (const bf16*)nullptr : m2 + 2 * D, rpg, gld, R, D)) return false;
       if (!lora_v(e, t.dn, dy, R, T->vT) || !lora_wgrad(e, T, t.dn, dy, S.act, S.uT_dn, T->vT, R)) return false;
       Lin da{dy, t.dn.ldb(), R, t.dn.Wb, t.dn.ldb(), F, t.dn.ldb()};
       da.no_swap = true;
@@ -603,9 +619,7 @@ bool micro_step(pi05_engine* e, int nb, const float* h_t) {
       if (!lora_dx(e, t.gu, dgu, R, dh)) return false;
       if (!rms_bwd(e, S.xmid, dh, D, prefix ? e->gem[l].rms2 : m2, rpg, gld, gx, R, D)) return false;
       // output projection
-      if (!launch(e, grad_to_bf16_kernel, dim3((n + 255) / 256), dim3(256), 0, false, (const float*)gx, dy, D + 16,
-                  prefix ? (const bf16*)nullptr : m1 + 2 * D, rpg, gld, R, D))
-        return false;
+      if (!grad_bf16(e, gx, dy, D + 16, prefix ? (const bf16*)nullptr : m1 + 2 * D, rpg, gld, R, D)) return false;
       if (!lora_v(e, t.o, dy, R, T->vT) || !lora_wgrad(e, T, t.o, dy, S.o, S.uT_o, T->vT, R)) return false;
       Lin dov{dy, t.o.ldb(), R, t.o.Wb, t.o.ldb(), P5_QDIM, t.o.ldb()};
       dov.no_swap = true;

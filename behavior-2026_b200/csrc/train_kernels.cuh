@@ -121,6 +121,94 @@ __global__ void rmsnorm_bwd_kernel(const bf16* x, const bf16* dy, int ld_dy, con
   }
 }
 
+// The same for D = 256 * CH: a warp keeps its row in registers (8 consecutive elements per lane and
+// chunk, 16-byte loads; x is read once instead of three times) and updates dx_acc with 16-byte stores.
+template <int CH>
+__global__ void rmsnorm_bwd_vec_kernel(const bf16* x, const bf16* dy, int ld_dy, const bf16* scale, int rows_per_mod,
+                                       int mod_ld, float* dx_acc, int T) {
+  constexpr int D = 256 * CH;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const bf16* xr = x + (long)warp * D;
+  const bf16* dr = dy + (long)warp * ld_dy;
+  const bf16* sc = scale + (mod_ld ? (long)(warp / rows_per_mod) * mod_ld : 0);
+  uint4 xv[CH], dv[CH], sv[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int i = (c * 32 + lane) * 8;
+    xv[c] = *reinterpret_cast<const uint4*>(xr + i);
+    dv[c] = *reinterpret_cast<const uint4*>(dr + i);
+    sv[c] = *reinterpret_cast<const uint4*>(sc + i);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    float xf[8];
+    unpack8(xv[c], xf);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss += xf[k] * xf[k];
+  }
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rstd = 1.0f / sqrtf(ss / (float)D + 1e-6f);
+  float dot = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    float xf[8], df[8], sf[8];
+    unpack8(xv[c], xf);
+    unpack8(dv[c], df);
+    unpack8(sv[c], sf);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dot += df[k] * rbf(1.0f + sf[k]) * xf[k] * rstd;
+  }
+  for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  const float m = dot / (float)D;
+  float* out = dx_acc + (long)warp * D;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int i = (c * 32 + lane) * 8;
+    float xf[8], df[8], sf[8];
+    unpack8(xv[c], xf);
+    unpack8(dv[c], df);
+    unpack8(sv[c], sf);
+    float4* o4 = reinterpret_cast<float4*>(out + i);
+    float4 a0 = o4[0], a1 = o4[1];
+    float r[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) r[k] = rstd * (df[k] * rbf(1.0f + sf[k]) - xf[k] * rstd * m);
+    a0.x += r[0];
+    a0.y += r[1];
+    a0.z += r[2];
+    a0.w += r[3];
+    a1.x += r[4];
+    a1.y += r[5];
+    a1.z += r[6];
+    a1.w += r[7];
+    o4[0] = a0;
+    o4[1] = a1;
+  }
+}
+
+// fp32 residual-stream gradient -> bf16, 8 elements per thread (D % 8 == 0), optionally times the
+// per-sample gate (gated residual backward)
+__global__ void grad_to_bf16_vec_kernel(const float* g, bf16* out, int ld_out, const bf16* gate, int rows_per_gate,
+                                        int gate_ld, int T, int D) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int dc = D / 8;
+  if (i >= (long)T * dc) return;
+  const int t = (int)(i / dc), k = (int)(i % dc) * 8;
+  const float4* src = reinterpret_cast<const float4*>(g + (long)t * D + k);
+  const float4 u = src[0], w = src[1];
+  float v[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+  if (gate) {
+    float gf[8];
+    unpack8(*reinterpret_cast<const uint4*>(gate + (long)(t / rows_per_gate) * gate_ld + k), gf);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] *= gf[q];
+  }
+  *reinterpret_cast<uint4*>(out + (long)t * ld_out + k) =
+      make_uint4(pack_bf2(v[0], v[1]), pack_bf2(v[2], v[3]), pack_bf2(v[4], v[5]), pack_bf2(v[6], v[7]));
+}
+
 // fp32 residual-stream gradient -> bf16 (optionally times the per-sample gate: gated residual backward)
 __global__ void grad_to_bf16_kernel(const float* g, bf16* out, int ld_out, const bf16* gate, int rows_per_gate,
                                     int gate_ld, int T, int D) {
