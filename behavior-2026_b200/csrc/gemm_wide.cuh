@@ -6,7 +6,7 @@
 // fewer bytes per MAC.  The price: the two 128x256 fp32 accumulators fill all 512 TMEM columns, so
 // there is no second accumulator to overlap the epilogue with the next tile's MMAs; eight epilogue
 // warps (two per TMEM lane quarter, one per accumulator half) keep that drain short.  Three 64 KB
-// stages of TMA (no multicast), same fused epilogues as gemm_tc_kernel (epi_row32), persistent CTAs
+// stages of plain per-CTA TMA loads, same fused epilogues as gemm_tc_kernel (epi_row32), persistent CTAs
 // walking the tiles in L2-sized groups of M tiles.  Used for K >= 4096, where the longer K loop
 // amortises the unoverlapped drain.
 #pragma once
