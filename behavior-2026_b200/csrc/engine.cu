@@ -116,6 +116,9 @@ struct pi05_engine {
   // few-token denoise: adaRMSNorm folded into the q/k/v and gate/up cluster GEMMs, fed by per-token
   // sum-of-squares partials from the producers of x (PI05_FUSE_NORM=0: separate rmsnorm launches)
   bool fuse_norm = true;
+  // receding-horizon stepping (pi05_act_batch): per slot the last chunk and the next row to execute
+  std::vector<std::vector<float>> act_chunk;
+  std::vector<int> act_next;
   float* nrm_ss = nullptr;  // 2 buffers of [P5_EXP_W / 16 parts][64 tokens]
 };
 
@@ -1960,6 +1963,69 @@ int pi05_infer_batch(pi05_engine* e, int n, const uint8_t* images, const int32_t
 
 int pi05_set_stage(pi05_engine* e, int slot, int stage, int mode) {
   if (!e || slot < 0 || slot >= e->max_batch || stage < 0 || mode < 0 || mode > 1) return PI05_ERR_ARG;
+  return PI05_OK;
+}
+
+// Receding-horizon stepping over environment slots (reference pi05_act_batch, π05_네이티브엔진.md:292-296
+// and :33: the chunk is re-planned after a fixed number of executed steps).  Host-side bookkeeping
+// over pi05_infer: one batched inference for the listed slots that need a new chunk.
+int pi05_act_batch(pi05_engine* e, int n, const int* slots, const uint8_t* images, const int32_t* tokens,
+                   const float* noise, int replan, int act_dim, float* out) {
+  if (!e || n < 1 || n > e->max_batch || !slots || !images || !tokens || !noise || !out) return PI05_ERR_ARG;
+  const int H = e->cfg.horizon;
+  if (replan < 1 || replan > H || act_dim < 1 || act_dim > P5_ACT_D) return PI05_ERR_ARG;
+  if (is_device_ptr(images) || is_device_ptr(tokens) || is_device_ptr(noise) || is_device_ptr(out)) {
+    set_err(e, "pi05_act_batch: inputs and output are host buffers");
+    return PI05_ERR_ARG;
+  }
+  if ((int)e->act_chunk.size() != e->max_batch) {
+    e->act_chunk.assign(e->max_batch, std::vector<float>());
+    e->act_next.assign(e->max_batch, 0);
+  }
+  std::vector<int> need;  // positions in the call whose slot re-plans
+  for (int i = 0; i < n; ++i) {
+    const int sl = slots[i];
+    if (sl < 0 || sl >= e->max_batch) return PI05_ERR_ARG;
+    for (int j = 0; j < i; ++j)
+      if (slots[j] == sl) return PI05_ERR_ARG;  // a slot steps at most once per call
+    if (e->act_chunk[sl].empty() || e->act_next[sl] >= replan) need.push_back(i);
+  }
+  if (!need.empty()) {
+    const size_t img = (size_t)e->cfg.n_cameras * P5_IMG * P5_IMG * 3, tok = (size_t)e->cfg.n_text,
+                 nz = (size_t)H * P5_ACT_D;
+    const int m = (int)need.size();
+    std::vector<uint8_t> bi(img * m);
+    std::vector<int32_t> bt(tok * m);
+    std::vector<float> bn(nz * m), ba(nz * m);
+    for (int k = 0; k < m; ++k) {
+      const int i = need[k];
+      memcpy(bi.data() + img * k, images + img * i, img);
+      memcpy(bt.data() + tok * k, tokens + tok * i, tok * sizeof(int32_t));
+      memcpy(bn.data() + nz * k, noise + nz * i, nz * sizeof(float));
+    }
+    const int rc = pi05_infer(e, m, bi.data(), bt.data(), bn.data(), ba.data());
+    if (rc != PI05_OK) return rc;
+    for (int k = 0; k < m; ++k) {
+      const int sl = slots[need[k]];
+      e->act_chunk[sl].assign(ba.begin() + nz * k, ba.begin() + nz * (k + 1));
+      e->act_next[sl] = 0;
+    }
+  }
+  for (int i = 0; i < n; ++i) {
+    const int sl = slots[i];
+    memcpy(out + (size_t)i * act_dim, e->act_chunk[sl].data() + (size_t)e->act_next[sl] * P5_ACT_D,
+           act_dim * sizeof(float));
+    ++e->act_next[sl];
+  }
+  return PI05_OK;
+}
+
+int pi05_reset_slot(pi05_engine* e, int slot) {
+  if (!e || slot < 0 || slot >= e->max_batch) return PI05_ERR_ARG;
+  if ((int)e->act_chunk.size() == e->max_batch) {
+    e->act_chunk[slot].clear();
+    e->act_next[slot] = 0;
+  }
   return PI05_OK;
 }
 

@@ -23,7 +23,7 @@ EXPORTS = [
     "pi05_save_weights", "pi05_load_weights", "pi05_prefill", "pi05_set_prefix_cache", "pi05_get_prefix_cache",
     "pi05_denoise", "pi05_infer", "pi05_stream", "pi05_sync", "pi05_prefix_len", "pi05_graph_launches",
     "pi05_synth_images", "pi05_synth_tokens", "pi05_synth_noise", "pi05_synth_prefix_cache", "pi05_create_batch",
-    "pi05_infer_batch", "pi05_set_stage", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
+    "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
 ]
 
 
@@ -93,6 +93,8 @@ def _load():
     L.pi05_create_batch.restype = vp
     L.pi05_infer_batch.argtypes = [vp, i32, vp, vp, vp, vp]
     L.pi05_set_stage.argtypes = [vp, i32, i32, i32]
+    L.pi05_act_batch.argtypes = [vp, i32, vp, vp, vp, vp, i32, i32, vp]
+    L.pi05_reset_slot.argtypes = [vp, i32]
     L.pi05_op_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp]
     L.pi05_op_attention.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32]
     L.pi05_op_siglip_attention.argtypes = [vp, i32, vp, vp]
@@ -333,6 +335,24 @@ class Engine:
 
     def set_stage(self, slot, stage, mode=1):
         self._check(lib.pi05_set_stage(self._h, slot, stage, mode))
+
+    def act_batch(self, slots, images, tokens, noise, replan=16, act_dim=23):
+        """Receding-horizon step of the environment slots `slots`: the next action row (first act_dim
+        entries) of each slot's chunk, re-planning (one batched infer) the slots whose chunk is empty or
+        has had `replan` rows executed.  images/tokens/noise: host arrays in the infer layout, one row
+        per listed slot.  Returns float32 [len(slots)][act_dim]."""
+        sl = np.ascontiguousarray(np.asarray(slots, dtype=np.int32))
+        n = sl.shape[0]
+        out = np.empty((n, act_dim), np.float32)
+        pi, ki = _ptr(images, np.uint8)
+        pt, kt = _ptr(tokens, np.int32)
+        pn, kn = _ptr(noise, np.float32)
+        po, ko = _ptr(out, np.float32, writable=True)
+        self._check(lib.pi05_act_batch(self._h, n, sl.ctypes.data_as(ctypes.c_void_p), pi, pt, pn, replan, act_dim, po))
+        return out
+
+    def reset_slot(self, slot):
+        self._check(lib.pi05_reset_slot(self._h, slot))
 
 
 def linear_static(x, w, out, bias=None, stream=None):

@@ -182,6 +182,16 @@ PI05_API int pi05_infer_batch(pi05_engine* e, int n, const uint8_t* images, cons
                      float* actions);
 /* PiBehavior stage channel; plain pi0.5 has no stage head, so this only validates its arguments. */
 PI05_API int pi05_set_stage(pi05_engine* e, int slot, int stage, int mode);
+/* Receding-horizon stepping (reference pi05_act_batch, π05_네이티브엔진.md:292-296, :33): environment slot
+ * slots[i] keeps the last 50x32 chunk it was given; each call writes, for every listed slot, the next
+ * row of that chunk (its first act_dim entries) to out[i][act_dim], and first runs one batched
+ * pi05_infer for the listed slots that have no chunk or have executed `replan` rows of it (their
+ * images, tokens and noise are row i of the pi05_infer-layout host inputs; rows of other slots are not
+ * read).  Host buffers; images are the 224x224 RGB camera frames pi05_infer takes. */
+PI05_API int pi05_act_batch(pi05_engine* e, int n, const int* slots, const uint8_t* images, const int32_t* tokens,
+                            const float* noise, int replan, int act_dim, float* out);
+/* Forget a slot's chunk (reference reset(eng, slot)): its next pi05_act_batch step re-plans. */
+PI05_API int pi05_reset_slot(pi05_engine* e, int slot);
 
 #ifdef __cplusplus
 }

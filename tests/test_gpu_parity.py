@@ -323,3 +323,35 @@ def test_fused_norm_denoise_matches_separate_norm(pn, monkeypatch, layers, steps
     a, b = out["1"], out["0"]
     assert np.isfinite(a).all()
     assert np.abs(a - b).max() <= 1e-2 and cos(a, b) >= 0.9999, (np.abs(a - b).max(), cos(a, b))
+
+
+def test_act_batch_receding_horizon(pn):
+    """pi05_act_batch: a slot executes rows 0..replan-1 of the chunk pi05_infer gives for its inputs,
+    then re-plans from the inputs of that call; pi05_reset_slot forces a re-plan; slots re-plan
+    independently within one call."""
+    cfg = pn.Config.make(siglip_layers=1, gemma_layers=2, num_steps=2)
+    eng = pn.Engine(cfg, max_batch=2)
+    eng.init_random_weights(8)
+    H = cfg.horizon
+
+    def inputs(seed, samples):
+        return (np.stack([pn.synth_images(seed, i) for i in samples]), np.stack([pn.synth_tokens(seed, i) for i in samples]),
+                np.stack([pn.synth_noise(seed, i) for i in samples]))
+
+    replan, act_dim = 4, 23
+    im, tk, nz = inputs(1, [0, 1])
+    ref = eng.infer(im, tk, nz)
+    for step in range(replan):
+        a = eng.act_batch([0, 1], im, tk, nz, replan=replan, act_dim=act_dim)
+        np.testing.assert_array_equal(a, ref[:, step, :act_dim])
+    im2, tk2, nz2 = inputs(2, [0, 1])
+    ref2 = eng.infer(im2, tk2, nz2)
+    a = eng.act_batch([1, 0], im2[::-1], tk2[::-1], nz2[::-1], replan=replan, act_dim=act_dim)  # both re-plan
+    np.testing.assert_array_equal(a, ref2[::-1, 0, :act_dim])
+    eng.reset_slot(1)
+    im3, tk3, nz3 = inputs(3, [0, 1])
+    ref3 = eng.infer(im3[1:], tk3[1:], nz3[1:])
+    a = eng.act_batch([0, 1], im3, tk3, nz3, replan=replan, act_dim=act_dim)  # slot 0 continues, slot 1 re-plans
+    np.testing.assert_array_equal(a[0], ref2[0, 1, :act_dim])
+    np.testing.assert_array_equal(a[1], ref3[0, 0, :act_dim])
+    assert H >= replan
