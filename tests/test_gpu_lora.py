@@ -1,6 +1,6 @@
 """LoRA train step on the GPU against fp32 torch autograd of the same loss (oracle/lora_ref.py).
 
-Tolerance: LoRA gradients within 3e-2 relative L2, per adapter tensor.
+Tolerance (the parity contract of this engine): LoRA gradients within 3e-2 relative L2, per adapter tensor.
 Reduced depth (1 SigLIP layer, 2 joint Gemma/expert layers), all widths full, 2 samples.
 """
 import numpy as np

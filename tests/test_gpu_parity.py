@@ -1,7 +1,7 @@
 """GPU parity: the sm_100a engine through the C ABI against the CPU oracle on the same seeded weights,
 inputs and noise.
 
-Tolerances: action chunks max-abs <= 2e-2 and cosine >= 0.999.  Intermediate
+Tolerances (the parity contract of this engine): action chunks max-abs <= 2e-2 and cosine >= 0.999.  Intermediate
 points (KV cache, image tokens) use rel-L2 <= 2e-2, i.e. bf16 rounding noise of reordered sums.
 """
 import numpy as np
