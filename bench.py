@@ -500,9 +500,10 @@ def run_lora(args, world, rank, local):
 
     hbm, tf_burst, tf_sus, peak_src = peaks()
     nb = args.lora_batch
-    eng = pn.Engine(pn.Config.make(), device=local, max_batch=args.micro_batch)
+    mb = min(args.micro_batch, nb)  # no larger than the per-GPU batch
+    eng = pn.Engine(pn.Config.make(), device=local, max_batch=mb)
     eng.init_random_weights(args.seed)
-    eng.lora_init(seed=args.seed + 1, micro_batch=args.micro_batch)
+    eng.lora_init(seed=args.seed + 1, micro_batch=mb)
     first, _ = dp.shard(nb * world, world, rank)
     imgs, toks, acts, noise, t = lora_inputs(pn, nb, first, args.seed)
     dev = [torch.from_numpy(a).cuda() for a in (imgs, toks, acts, noise, t)]
@@ -537,7 +538,7 @@ def run_lora(args, world, rank, local):
             "ms_per_step": total_ms / args.steps, "lora_steps_per_s": args.steps / (total_ms / 1e3),
             "scaling": "weak", "dtype": "bf16", "data": "synthetic", "vs_baseline": None, "loss": loss,
             "config": {"workload": f"LoRA step (rank 16, alpha 32, q/k/v/o/gate/up/down of Gemma-2B and the expert): "
-                                   f"{nb} samples per GPU, micro-batch {args.micro_batch}, flow-matching loss, "
+                                   f"{nb} samples per GPU, micro-batch {mb}, flow-matching loss, "
                                    f"AdamW lr 1e-4" + (", NCCL gradient allreduce" if world > 1 else ""),
                        "model": MODEL, "global_batch": samples, "per_gpu_batch": nb, "parallelism": f"dp{world}",
                        "l2": "no flush: every step streams GBs of weights and saved activations (> 126 MB L2)"},
@@ -582,7 +583,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="bs64", choices=["bs64", "bs1", "denoise", "sweep", "gemm", "lora"])
     ap.add_argument("--lora-batch", type=int, default=32, help="samples per GPU per LoRA step")
-    ap.add_argument("--micro-batch", type=int, default=8, help="samples per LoRA forward/backward pass")
+    ap.add_argument("--micro-batch", type=int, default=32,
+                    help="samples per LoRA forward/backward pass (measured on B200: one 32-sample pass 86.0 "
+                         "samples/s, four 8-sample passes 76.3)")
     ap.add_argument("--gemm", default="7744,32768,2048", help="M,N,K for --workload gemm")
     ap.add_argument("--epi", default="geglu", help="epilogue for --workload gemm")
     ap.add_argument("--batch", type=int, default=64)
