@@ -1,0 +1,146 @@
+// preprocess.cu — host-side camera-frame preprocessing: aspect-preserving resize into a zero-padded
+// frame (the reference's resize_with_pad, π05_네이티브엔진.md:296-297, which follows openpi's
+// image_tools.resize_with_pad over Pillow's bilinear resize).  Host code only; no GPU is involved.
+//
+// Geometry (openpi): ratio = max(w / out_w, h / out_h) in double precision; the resized image is
+// int(w / ratio) x int(h / ratio), pasted at (int((out_w - rw) / 2), int((out_h - rh) / 2)) into a
+// zero frame; a frame already of the output size is copied unchanged.
+//
+// Resampling (Pillow's 8-bit bilinear "reduce-aware" filter, restated): separable, one pass per axis
+// whose size changes (width first, then height).  Output sample i of an axis of n_in -> n_out samples
+// has centre c = (i + 0.5) * s, s = n_in / n_out; the triangle filter is widened by f = max(s, 1)
+// (support f), taps x in [int(c - f + 0.5) clamped at 0, int(c + f + 0.5) clamped at n_in), weights
+// tri((x - c + 0.5) / f) normalised to sum 1, then rounded to fixed point with 22 fraction bits
+// (round half away from zero).  A pass accumulates the 8-bit samples times the integer weights from
+// 2^21 (rounding), shifts by 22 and clamps to [0, 255].
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "../../include/pi05.h"
+
+namespace {
+
+constexpr int RS_BITS = 22;
+
+struct AxisTaps {
+  int taps = 0;                  // weights per output sample
+  std::vector<int> first, count;  // first input sample and number of taps per output sample
+  std::vector<int32_t> w;         // [n_out][taps]
+};
+
+AxisTaps axis_taps(int n_in, int n_out) {
+  AxisTaps t;
+  const double s = (double)n_in / (double)n_out;
+  const double f = s < 1.0 ? 1.0 : s;
+  t.taps = (int)std::ceil(f) * 2 + 1;
+  t.first.resize(n_out);
+  t.count.resize(n_out);
+  t.w.assign((size_t)n_out * t.taps, 0);
+  std::vector<double> k(t.taps);
+  for (int i = 0; i < n_out; ++i) {
+    const double c = (i + 0.5) * s;
+    int lo = (int)(c - f + 0.5);
+    if (lo < 0) lo = 0;
+    int hi = (int)(c + f + 0.5);
+    if (hi > n_in) hi = n_in;
+    const int cnt = hi - lo;
+    double sum = 0.0;
+    for (int x = 0; x < cnt; ++x) {
+      const double d = std::fabs((x + lo - c + 0.5) / f);
+      k[x] = d < 1.0 ? 1.0 - d : 0.0;
+      sum += k[x];
+    }
+    for (int x = 0; x < cnt; ++x) {
+      const double v = sum != 0.0 ? k[x] / sum : k[x];
+      const double q = v * (double)(1 << RS_BITS);
+      t.w[(size_t)i * t.taps + x] = (int32_t)(q < 0.0 ? q - 0.5 : q + 0.5);
+    }
+    t.first[i] = lo;
+    t.count[i] = cnt;
+  }
+  return t;
+}
+
+inline uint8_t rs_clip(int32_t acc) {
+  if (acc <= 0) return 0;
+  const int32_t v = acc >> RS_BITS;
+  return v > 255 ? 255 : (uint8_t)v;
+}
+
+// width pass: in [h][w_in][3] -> out [h][w_out][3]
+void resample_width(const uint8_t* in, int h, int w_in, uint8_t* out, int w_out) {
+  const AxisTaps t = axis_taps(w_in, w_out);
+  for (int y = 0; y < h; ++y) {
+    const uint8_t* row = in + (size_t)y * w_in * 3;
+    uint8_t* orow = out + (size_t)y * w_out * 3;
+    for (int i = 0; i < w_out; ++i) {
+      const int32_t* wi = &t.w[(size_t)i * t.taps];
+      for (int ch = 0; ch < 3; ++ch) {
+        int32_t acc = 1 << (RS_BITS - 1);
+        for (int x = 0; x < t.count[i]; ++x) acc += (int32_t)row[(size_t)(t.first[i] + x) * 3 + ch] * wi[x];
+        orow[(size_t)i * 3 + ch] = rs_clip(acc);
+      }
+    }
+  }
+}
+
+// height pass: in [h_in][w][3] -> out [h_out][w][3]
+void resample_height(const uint8_t* in, int h_in, int w, uint8_t* out, int h_out) {
+  const AxisTaps t = axis_taps(h_in, h_out);
+  for (int i = 0; i < h_out; ++i) {
+    const int32_t* wi = &t.w[(size_t)i * t.taps];
+    uint8_t* orow = out + (size_t)i * w * 3;
+    for (int e = 0; e < w * 3; ++e) {
+      int32_t acc = 1 << (RS_BITS - 1);
+      for (int y = 0; y < t.count[i]; ++y) acc += (int32_t)in[(size_t)(t.first[i] + y) * w * 3 + e] * wi[y];
+      orow[e] = rs_clip(acc);
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int pi05_resize_with_pad(const uint8_t* src, int h, int w, int channels, long stride, uint8_t* dst, int out_h,
+                         int out_w) {
+  if (!src || !dst || h < 1 || w < 1 || out_h < 1 || out_w < 1 || (channels != 3 && channels != 4) ||
+      stride < (long)w * channels)
+    return PI05_ERR_ARG;
+  // RGB rows, contiguous (alpha dropped)
+  std::vector<uint8_t> rgb((size_t)h * w * 3);
+  for (int y = 0; y < h; ++y)
+    for (int x = 0; x < w; ++x)
+      memcpy(&rgb[((size_t)y * w + x) * 3], src + (size_t)y * stride + (size_t)x * channels, 3);
+  if (h == out_h && w == out_w) {
+    memcpy(dst, rgb.data(), rgb.size());
+    return PI05_OK;
+  }
+  const double ratio = std::fmax((double)w / (double)out_w, (double)h / (double)out_h);
+  const int rh = (int)((double)h / ratio), rw = (int)((double)w / ratio);
+  if (rh < 1 || rw < 1 || rh > out_h || rw > out_w) return PI05_ERR_ARG;
+  std::vector<uint8_t> a = rgb, b;
+  int ch = h, cw = w;
+  if (rw != cw) {
+    b.resize((size_t)ch * rw * 3);
+    resample_width(a.data(), ch, cw, b.data(), rw);
+    a.swap(b);
+    cw = rw;
+  }
+  if (rh != ch) {
+    b.resize((size_t)rh * cw * 3);
+    resample_height(a.data(), ch, cw, b.data(), rh);
+    a.swap(b);
+    ch = rh;
+  }
+  const int pad_h = std::max(0, (int)((out_h - rh) / 2.0)), pad_w = std::max(0, (int)((out_w - rw) / 2.0));
+  memset(dst, 0, (size_t)out_h * out_w * 3);
+  for (int y = 0; y < rh; ++y)
+    memcpy(dst + ((size_t)(y + pad_h) * out_w + pad_w) * 3, &a[(size_t)y * rw * 3], (size_t)rw * 3);
+  return PI05_OK;
+}
+
+}  // extern "C"

@@ -23,7 +23,7 @@ EXPORTS = [
     "pi05_save_weights", "pi05_load_weights", "pi05_prefill", "pi05_set_prefix_cache", "pi05_get_prefix_cache",
     "pi05_denoise", "pi05_infer", "pi05_stream", "pi05_sync", "pi05_prefix_len", "pi05_graph_launches",
     "pi05_synth_images", "pi05_synth_tokens", "pi05_synth_noise", "pi05_synth_prefix_cache", "pi05_create_batch",
-    "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
+    "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_resize_with_pad", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
 ]
 
 
@@ -95,6 +95,7 @@ def _load():
     L.pi05_set_stage.argtypes = [vp, i32, i32, i32]
     L.pi05_act_batch.argtypes = [vp, i32, vp, vp, vp, vp, i32, i32, vp]
     L.pi05_reset_slot.argtypes = [vp, i32]
+    L.pi05_resize_with_pad.argtypes = [vp, i32, i32, i32, ctypes.c_long, vp, i32, i32]
     L.pi05_op_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp]
     L.pi05_op_attention.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32]
     L.pi05_op_siglip_attention.argtypes = [vp, i32, vp, vp]
@@ -353,6 +354,22 @@ class Engine:
 
     def reset_slot(self, slot):
         self._check(lib.pi05_reset_slot(self._h, slot))
+
+
+def resize_with_pad(image, out_h=224, out_w=224):
+    """Camera frame (uint8 [h][w][3 or 4], any row stride) -> the zero-padded, aspect-preserving
+    bilinear resize of pi05_resize_with_pad, uint8 [out_h][out_w][3].  Host only."""
+    img = np.asarray(image)
+    if img.dtype != np.uint8 or img.ndim != 3 or img.shape[2] not in (3, 4) or img.strides[1] != img.shape[2] \
+            or img.strides[2] != 1:
+        img = np.ascontiguousarray(img, dtype=np.uint8)
+    h, w, c = img.shape
+    out = np.empty((out_h, out_w, 3), np.uint8)
+    rc = lib.pi05_resize_with_pad(img.ctypes.data_as(ctypes.c_void_p), h, w, c, img.strides[0],
+                                  out.ctypes.data_as(ctypes.c_void_p), out_h, out_w)
+    if rc != 0:
+        raise Pi05Error(rc, f"pi05_resize_with_pad: unsupported frame {h}x{w}x{c} -> {out_h}x{out_w}")
+    return out
 
 
 def linear_static(x, w, out, bias=None, stream=None):

@@ -192,6 +192,13 @@ PI05_API int pi05_act_batch(pi05_engine* e, int n, const int* slots, const uint8
                             const float* noise, int replan, int act_dim, float* out);
 /* Forget a slot's chunk (reference reset(eng, slot)): its next pi05_act_batch step re-plans. */
 PI05_API int pi05_reset_slot(pi05_engine* e, int slot);
+/* Camera-frame preprocessing on the host (reference resize_with_pad, π05_네이티브엔진.md:296-297, after
+ * openpi image_tools.resize_with_pad with Pillow's bilinear filter): the h x w frame (`channels` 3 = RGB
+ * or 4 = RGBA, alpha dropped; rows `stride` bytes apart) is resized keeping its aspect ratio and pasted,
+ * centred, into a zero out_h x out_w RGB frame (dst, out_h*out_w*3 bytes); a frame of the output size
+ * is copied.  Host memory; needs no engine or GPU. */
+PI05_API int pi05_resize_with_pad(const uint8_t* src, int h, int w, int channels, long stride, uint8_t* dst, int out_h,
+                                  int out_w);
 
 #ifdef __cplusplus
 }
