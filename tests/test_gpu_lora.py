@@ -105,3 +105,34 @@ def test_lora_state_checkpoint_resume(lora_case, tmp_path):
     eng.lora_load_state(path)
     eng.lora_step(imgs, toks, acts, noise, t)
     assert np.array_equal(eng.lora_get_params(), p2)
+
+
+def test_lora_gradients_tcgen05_backward_match_mma_sync(lora_case, pn, monkeypatch):
+    """The tcgen05 attention backward (dQ; dK / dV with query-split fp32 partials, which this 2-sample
+    case exercises) against the mma.sync kernels it replaced, on the same weights, adapters and batch.
+    Both round dS to bf16 for the tensor-core product, at points that differ in the last bits, so
+    per adapter they may differ by about as much as each differs from the fp32 autograd reference
+    (independent errors: ~1.4x); the whole gradient stays within the LoRA tolerance."""
+    cfg = pn.Config.make(siglip_layers=1, gemma_layers=2, num_steps=10)
+    imgs, toks, acts, noise, t = lora_case["batch"]
+    monkeypatch.setenv("PI05_ATTN_TC", "0")
+    eng = pn.Engine(cfg, max_batch=2)
+    eng.init_random_weights(4)
+    eng.lora_init(seed=5, micro_batch=2)
+    eng.lora_set_params(lora_case["p0"])
+    eng.lora_zero_grads()
+    loss = eng.lora_accumulate(imgs, toks, acts, noise, t)
+    g_mma = eng.lora_get_grads()
+    g_tc = lora_case["g_gpu"]
+    assert abs(loss - lora_case["loss_gpu"]) <= 1e-3 * abs(loss)
+    g_ref = lora_case["g_ref"]
+    bad = []
+    for n, sl in lora_case["slices"].items():
+        if np.linalg.norm(g_ref[sl]) < 1e-12:
+            continue
+        d = rel_l2(g_tc[sl], g_mma[sl].astype(np.float64))
+        e = max(rel_l2(g_tc[sl], g_ref[sl]), rel_l2(g_mma[sl], g_ref[sl]))
+        if d > 1.5 * e + 2e-3:
+            bad.append((n, d, e))
+    assert not bad, bad
+    assert rel_l2(g_tc, g_mma.astype(np.float64)) <= GRAD_REL_L2
