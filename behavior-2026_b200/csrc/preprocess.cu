@@ -143,4 +143,52 @@ int pi05_resize_with_pad(const uint8_t* src, int h, int w, int channels, long st
   return PI05_OK;
 }
 
+// openpi Normalize / Unnormalize in float32, per dimension j of x[n][dim], in place:
+//   mode 0 (z-score, a = mean, b = std):   y = (x - a) / (b + 1e-6)        inverse x = y * (b + 1e-6) + a
+//   mode 1 (quantile, a = q01, b = q99):   y = (x - a) / (b - a + 1e-6) * 2 - 1
+//                                          inverse x = (y + 1) / 2 * (b - a + 1e-6) + a
+int pi05_normalize(float* x, int n, int dim, const float* a, const float* b, int mode, int inverse) {
+  if (!x || !a || !b || n < 0 || dim < 1 || (mode != 0 && mode != 1)) return PI05_ERR_ARG;
+  const float eps = 1e-6f;
+  for (long i = 0; i < (long)n * dim; ++i) {
+    const int j = (int)(i % dim);
+    const float v = x[i];
+    if (mode == 0)
+      x[i] = inverse ? v * (b[j] + eps) + a[j] : (v - a[j]) / (b[j] + eps);
+    else
+      x[i] = inverse ? (v + 1.0f) / 2.0f * (b[j] - a[j] + eps) + a[j] : (v - a[j]) / (b[j] - a[j] + eps) * 2.0f - 1.0f;
+  }
+  return PI05_OK;
+}
+
+// State discretisation of the pi0.5 prompt (openpi): bin = (number of edges <= x) - 1 over the `bins`
+// edges -1 + 2k / bins, k = 0 .. bins-1 (numpy digitize of linspace(-1, 1, bins + 1)[:-1], minus one):
+// -1 below -1, bins - 1 at or above 1 - 2 / bins.  The edges are exact in binary for power-of-two bins.
+int pi05_discretize_state(const float* x, int n, int dim, int bins, int32_t* out) {
+  if (!x || !out || n < 0 || dim < 1 || bins < 1) return PI05_ERR_ARG;
+  for (long i = 0; i < (long)n * dim; ++i) {
+    const double v = x[i];
+    int lo = 0, hi = bins;  // count of edges <= v, by bisection over the increasing edges
+    while (lo < hi) {
+      const int mid = (lo + hi) / 2;
+      if (-1.0 + 2.0 * mid / bins <= v)
+        lo = mid + 1;
+      else
+        hi = mid;
+    }
+    out[i] = lo - 1;
+  }
+  return PI05_OK;
+}
+
+// Delta to absolute actions (openpi AbsoluteActions): actions[t][j] += state[j] for the dimensions j
+// with mask[j] != 0, t < horizon, in place.
+int pi05_absolute_actions(float* actions, int horizon, int dim, const float* state, const uint8_t* mask) {
+  if (!actions || !state || !mask || horizon < 0 || dim < 1) return PI05_ERR_ARG;
+  for (int t = 0; t < horizon; ++t)
+    for (int j = 0; j < dim; ++j)
+      if (mask[j]) actions[(size_t)t * dim + j] += state[j];
+  return PI05_OK;
+}
+
 }  // extern "C"

@@ -23,7 +23,7 @@ EXPORTS = [
     "pi05_save_weights", "pi05_load_weights", "pi05_prefill", "pi05_set_prefix_cache", "pi05_get_prefix_cache",
     "pi05_denoise", "pi05_infer", "pi05_stream", "pi05_sync", "pi05_prefix_len", "pi05_graph_launches",
     "pi05_synth_images", "pi05_synth_tokens", "pi05_synth_noise", "pi05_synth_prefix_cache", "pi05_create_batch",
-    "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_resize_with_pad", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
+    "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_resize_with_pad", "pi05_normalize", "pi05_discretize_state", "pi05_absolute_actions", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
 ]
 
 
@@ -96,6 +96,9 @@ def _load():
     L.pi05_act_batch.argtypes = [vp, i32, vp, vp, vp, vp, i32, i32, vp]
     L.pi05_reset_slot.argtypes = [vp, i32]
     L.pi05_resize_with_pad.argtypes = [vp, i32, i32, i32, ctypes.c_long, vp, i32, i32]
+    L.pi05_normalize.argtypes = [vp, i32, i32, vp, vp, i32, i32]
+    L.pi05_discretize_state.argtypes = [vp, i32, i32, i32, vp]
+    L.pi05_absolute_actions.argtypes = [vp, i32, i32, vp, vp]
     L.pi05_op_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp]
     L.pi05_op_attention.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32]
     L.pi05_op_siglip_attention.argtypes = [vp, i32, vp, vp]
@@ -370,6 +373,46 @@ def resize_with_pad(image, out_h=224, out_w=224):
     if rc != 0:
         raise Pi05Error(rc, f"pi05_resize_with_pad: unsupported frame {h}x{w}x{c} -> {out_h}x{out_w}")
     return out
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def normalize(x, a, b, mode="quantile", inverse=False):
+    """pi05_normalize on a copy of x [..., dim]: mode "zscore" (a, b = mean, std) or "quantile"
+    (a, b = q01, q99); inverse=True un-normalises."""
+    y = _f32(x).copy()
+    dim = y.shape[-1]
+    av, bv = _f32(a), _f32(b)
+    rc = lib.pi05_normalize(y.ctypes.data_as(ctypes.c_void_p), y.size // dim, dim, av.ctypes.data_as(ctypes.c_void_p),
+                            bv.ctypes.data_as(ctypes.c_void_p), {"zscore": 0, "quantile": 1}[mode], int(inverse))
+    if rc != 0:
+        raise Pi05Error(rc, "pi05_normalize")
+    return y
+
+
+def discretize_state(x, bins=256):
+    """pi05_discretize_state: int32 bins of a normalised state [..., dim]."""
+    xv = _f32(x)
+    out = np.empty(xv.shape, np.int32)
+    dim = xv.shape[-1]
+    rc = lib.pi05_discretize_state(xv.ctypes.data_as(ctypes.c_void_p), xv.size // dim, dim, bins,
+                                   out.ctypes.data_as(ctypes.c_void_p))
+    if rc != 0:
+        raise Pi05Error(rc, "pi05_discretize_state")
+    return out
+
+
+def absolute_actions(actions, state, mask):
+    """pi05_absolute_actions on a copy of actions [horizon][dim]: += state where mask."""
+    y = _f32(actions).copy()
+    st, mk = _f32(state), np.ascontiguousarray(mask, dtype=np.uint8)
+    rc = lib.pi05_absolute_actions(y.ctypes.data_as(ctypes.c_void_p), y.shape[0], y.shape[1],
+                                   st.ctypes.data_as(ctypes.c_void_p), mk.ctypes.data_as(ctypes.c_void_p))
+    if rc != 0:
+        raise Pi05Error(rc, "pi05_absolute_actions")
+    return y
 
 
 def linear_static(x, w, out, bias=None, stream=None):

@@ -199,6 +199,15 @@ PI05_API int pi05_reset_slot(pi05_engine* e, int slot);
  * is copied.  Host memory; needs no engine or GPU. */
 PI05_API int pi05_resize_with_pad(const uint8_t* src, int h, int w, int channels, long stride, uint8_t* dst, int out_h,
                                   int out_w);
+/* State / action transforms of the reference wrapper (π05_네이티브엔진.md:32-35, :83-84, after openpi's
+ * Normalize, Unnormalize, AbsoluteActions and the pi0.5 state discretisation), float32, host memory:
+ *   pi05_normalize: x[n][dim] in place; mode 0 z-score with (a, b) = (mean, std), mode 1 quantile with
+ *     (a, b) = (q01, q99) mapping to [-1, 1]; inverse != 0 un-normalises;
+ *   pi05_discretize_state: out[n][dim] = bin of x among `bins` equal bins of [-1, 1) (-1 below -1);
+ *   pi05_absolute_actions: actions[horizon][dim] += state where mask != 0 (delta actions). */
+PI05_API int pi05_normalize(float* x, int n, int dim, const float* a, const float* b, int mode, int inverse);
+PI05_API int pi05_discretize_state(const float* x, int n, int dim, int bins, int32_t* out);
+PI05_API int pi05_absolute_actions(float* actions, int horizon, int dim, const float* state, const uint8_t* mask);
 
 #ifdef __cplusplus
 }

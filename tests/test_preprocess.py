@@ -48,3 +48,56 @@ def test_resize_with_pad_strided_rows_and_smooth_content(pn):
 def test_resize_with_pad_rejects_bad_frames(pn):
     with pytest.raises(pn.Pi05Error):
         pn.resize_with_pad(np.zeros((1, 4000, 3), np.uint8))  # resized height would be 0
+
+
+# ---------------------------------------------------------------- state / action transforms
+# numpy restatements of openpi's Normalize / Unnormalize (float32), the pi0.5 state discretisation
+# (digitize over linspace(-1, 1, bins + 1)[:-1], minus one) and AbsoluteActions
+def ref_normalize(x, a, b, mode, inverse):
+    x, a, b = (np.asarray(v, np.float32) for v in (x, a, b))
+    eps = np.float32(1e-6)
+    if mode == "zscore":
+        return x * (b + eps) + a if inverse else (x - a) / (b + eps)
+    return (x + np.float32(1.0)) / np.float32(2.0) * (b - a + eps) + a if inverse else \
+        (x - a) / (b - a + eps) * np.float32(2.0) - np.float32(1.0)
+
+
+@pytest.mark.parametrize("mode", ["zscore", "quantile"])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_normalize_matches_numpy(pn, mode, inverse):
+    rng = np.random.default_rng(11)
+    x = rng.normal(0, 3, (5, 23)).astype(np.float32)
+    if mode == "zscore":
+        a, b = rng.normal(0, 1, 23).astype(np.float32), rng.uniform(0.1, 2, 23).astype(np.float32)
+    else:
+        a = rng.uniform(-3, 0, 23).astype(np.float32)
+        b = (a + rng.uniform(0.5, 4, 23)).astype(np.float32)
+    np.testing.assert_array_equal(pn.normalize(x, a, b, mode, inverse), ref_normalize(x, a, b, mode, inverse))
+
+
+def test_normalize_round_trip(pn):
+    rng = np.random.default_rng(12)
+    x = rng.uniform(-2, 2, (50, 32)).astype(np.float32)
+    q01, q99 = np.full(32, -2.5, np.float32), np.full(32, 2.5, np.float32)
+    y = pn.normalize(pn.normalize(x, q01, q99, "quantile"), q01, q99, "quantile", inverse=True)
+    np.testing.assert_allclose(y, x, rtol=0, atol=2e-6)
+
+
+def test_discretize_state_matches_numpy(pn):
+    rng = np.random.default_rng(13)
+    edges = np.linspace(-1, 1, 256 + 1)[:-1]
+    x = np.concatenate([rng.uniform(-1.2, 1.2, (4, 23)).astype(np.float32).ravel(),
+                        edges.astype(np.float32), np.float32([-1.0, 1.0, -1.0000001, 0.9921875, 0.99218744])])
+    x = x.reshape(-1, 1)  # every value, edges and the values just beside them included
+    ref = (np.digitize(x, bins=edges) - 1).astype(np.int32)
+    np.testing.assert_array_equal(pn.discretize_state(x, 256), ref)
+
+
+def test_absolute_actions(pn):
+    rng = np.random.default_rng(14)
+    acts = rng.normal(size=(50, 23)).astype(np.float32)
+    state = rng.normal(size=23).astype(np.float32)
+    mask = (np.arange(23) % 3 != 2).astype(np.uint8)
+    ref = acts.copy()
+    ref[:, mask.astype(bool)] += state[mask.astype(bool)]
+    np.testing.assert_array_equal(pn.absolute_actions(acts, state, mask), ref)
