@@ -65,7 +65,9 @@ def lib():
         L.p5o_gen_normal.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_double,
                                      ctypes.c_int, f32]
         L.p5o_gen_param.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_double, f32]
-        for f in (L.p5o_gen_images, L.p5o_gen_tokens, L.p5o_gen_normal, L.p5o_gen_param):
+        L.p5o_gen_param_at.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_double, f32]
+        for f in (L.p5o_gen_images, L.p5o_gen_tokens, L.p5o_gen_normal, L.p5o_gen_param, L.p5o_gen_param_at):
             f.restype = None
         _lib = L
     return _lib
@@ -115,6 +117,13 @@ def gen_normal(seed, kind, sub, shape, std=1.0, round_bf16=False):
 def gen_param(seed, kind, sub, shape, std=0.02):
     out = np.empty(shape, np.float32)
     lib().p5o_gen_param(seed, kind, sub, out.size, std, _p(out, ctypes.c_float))
+    return out
+
+
+def gen_param_at(seed, kind, sub, first, n, std=0.02):
+    """elements [first, first + n) of a parameter stream"""
+    out = np.empty((n,), np.float32)
+    lib().p5o_gen_param_at(seed, kind, sub, first, n, std, _p(out, ctypes.c_float))
     return out
 
 

@@ -467,6 +467,11 @@ void p5o_gen_normal(uint64_t seed, int kind, int sub, int64_t n, double stdv, in
 void p5o_gen_param(uint64_t seed, int kind, int sub, int64_t n, double stdv, float* out) {
   gen_param(out, seed, kind, sub, (size_t)n, stdv, p5_kind_has_unit_base(kind) ? 1.0f : 0.0f);
 }
+void p5o_gen_param_at(uint64_t seed, int kind, int sub, int64_t first, int64_t n, double stdv, float* out) {
+  const uint64_t key = p5_key(seed, kind, sub);
+  const float sc = p5_scale_for_std(stdv), base = p5_kind_has_unit_base(kind) ? 1.0f : 0.0f;
+  for (int64_t i = 0; i < n; ++i) out[i] = p5_bf2f(p5_param_bf(key, (uint64_t)(first + i), sc, base));
+}
 
 int p5o_siglip(const p5o_config* c, uint64_t seed, const uint8_t* images, float* img_tokens, int flags,
                p5o_probe_fn probe, void* ctx) {

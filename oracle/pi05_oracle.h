@@ -39,6 +39,8 @@ void p5o_gen_images(uint64_t seed, int sample, int n_cam, uint8_t* out);
 void p5o_gen_tokens(uint64_t seed, int sample, int n, int32_t* out);
 void p5o_gen_normal(uint64_t seed, int kind, int sub, int64_t n, double stdv, int round_bf16, float* out);
 void p5o_gen_param(uint64_t seed, int kind, int sub, int64_t n, double stdv, float* out);
+/* elements [first, first + n) of a parameter stream (rows of the token-embedding table) */
+void p5o_gen_param_at(uint64_t seed, int kind, int sub, int64_t first, int64_t n, double stdv, float* out);
 
 /* images: [n_cameras][224][224][3] uint8; out: [n_cameras*256][2048] */
 int p5o_siglip(const p5o_config* c, uint64_t seed, const uint8_t* images, float* img_tokens, int flags,

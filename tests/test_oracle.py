@@ -1,5 +1,6 @@
 """CPU checks of the oracle: the conventions the reference engine's record pins, the committed golden
-fixtures, and a cross-check of the C++ oracle against the independent torch restatement."""
+fixtures, and cross-checks of the C++ oracle against the independent torch restatements (vision tower:
+oracle/siglip_ref.py; joint Gemma / expert network: oracle/lora_ref.py)."""
 import json
 import os
 
@@ -66,6 +67,7 @@ def test_cpp_oracle_matches_torch_restatement(oracle):
     import torch
 
     import lora_ref
+    import siglip_ref
 
     cfg = oracle.Config.make(siglip_layers=1, gemma_layers=2, num_steps=10, n_cameras=1, n_text=16)
     img, tok, noise = oracle.gen_images(2, 0, 1), oracle.gen_tokens(2, 0, 16), oracle.gen_noise(2, 0)
@@ -80,6 +82,45 @@ def test_cpp_oracle_matches_torch_restatement(oracle):
             with torch.no_grad():
                 ref.params[name].zero_()
     emb = oracle.prefix_embed(cfg, 9, img, tok)[None]
+    # the torch chain's own prefix (SigLIP restatement + Gemma embedder) gives the same embedding
+    emb_t = siglip_ref.prefix_embedding(9, 1, img, tok)[None]
+    assert np.abs(emb_t - emb).max() < 2e-2 * max(1.0, np.abs(emb).max())
+    emb = emb_t
     with torch.no_grad():
         v_t = ref.velocity(emb, torch.from_numpy(noise[None]), np.array([1.0], np.float32))[0].numpy()
     assert np.abs(v_t - v_cpp).max() < 2e-2 and np.corrcoef(v_t.ravel(), v_cpp.ravel())[0, 1] > 0.9999
+
+
+def test_cpp_oracle_siglip_matches_torch_restatement(oracle):
+    """The vision tower (stem conv + learned posemb, pre-LN blocks, final LayerNorm, projector) of the C++
+    oracle against the torch restatement written from flax's SigLIP modules, two layers, three cameras.
+    Pure fp32 on both sides: max-abs <= 2e-2 (measured ~5e-4: fp32 summation order only, so a misplaced
+    norm, a different GELU or posemb would show).  With bf16 activations the two round at slightly
+    different points (the torch side also rounds the image, the conv output and the logits, as flax's
+    bf16 modules do): every named point within rel-L2 2e-2."""
+    import siglip_ref
+
+    cfg = oracle.Config.make(siglip_layers=2, gemma_layers=1)
+    img = oracle.gen_images(3, 0)
+    ref32 = oracle.siglip(cfg, 7, img, flags=oracle.FP32_ACTIVATIONS)
+    mine32 = siglip_ref.SiglipRef(2, 7, bf16=False)(img)
+    assert np.abs(mine32 - ref32).max() <= 2e-2
+    pr = oracle.Probe(keep=["img."])
+    ref = oracle.siglip(cfg, 7, img, probe=pr)
+    pts = {}
+    mine = siglip_ref.SiglipRef(2, 7)(img, points=pts)
+    pts["img.tokens"] = mine.ravel()
+    pr.points["img.tokens"] = ref.ravel()
+    for name in ("img.stem", "img.l0.out", "img.l1.out", "img.encoded", "img.tokens"):
+        a, b = pts[name].astype(np.float64), pr.points[name].astype(np.float64)
+        assert np.linalg.norm(a - b) / np.linalg.norm(b) <= 2e-2, name
+
+
+def test_text_embedding_matches_oracle(oracle):
+    """Gemma embedder rows x bf16(sqrt(2048)) of the torch restatement against the C++ oracle's txt.emb."""
+    import siglip_ref
+
+    cfg = oracle.Config.make(siglip_layers=0, gemma_layers=1, n_cameras=1, n_text=24)
+    img, tok = oracle.gen_images(4, 0, 1), oracle.gen_tokens(4, 0, 24)
+    emb = oracle.prefix_embed(cfg, 2, img, tok)[256:]
+    np.testing.assert_array_equal(siglip_ref.text_embedding(2, tok), emb)
