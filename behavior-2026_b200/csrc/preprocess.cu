@@ -164,10 +164,15 @@ int pi05_normalize(float* x, int n, int dim, const float* a, const float* b, int
 // State discretisation of the pi0.5 prompt (openpi): bin = (number of edges <= x) - 1 over the `bins`
 // edges -1 + 2k / bins, k = 0 .. bins-1 (numpy digitize of linspace(-1, 1, bins + 1)[:-1], minus one):
 // -1 below -1, bins - 1 at or above 1 - 2 / bins.  The edges are exact in binary for power-of-two bins.
+// NaN lands in bin bins - 1, as numpy's digitize sorts NaN after every edge.
 int pi05_discretize_state(const float* x, int n, int dim, int bins, int32_t* out) {
   if (!x || !out || n < 0 || dim < 1 || bins < 1) return PI05_ERR_ARG;
   for (long i = 0; i < (long)n * dim; ++i) {
     const double v = x[i];
+    if (std::isnan(v)) {
+      out[i] = bins - 1;
+      continue;
+    }
     int lo = 0, hi = bins;  // count of edges <= v, by bisection over the increasing edges
     while (lo < hi) {
       const int mid = (lo + hi) / 2;

@@ -87,8 +87,9 @@ def test_discretize_state_matches_numpy(pn):
     rng = np.random.default_rng(13)
     edges = np.linspace(-1, 1, 256 + 1)[:-1]
     x = np.concatenate([rng.uniform(-1.2, 1.2, (4, 23)).astype(np.float32).ravel(),
-                        edges.astype(np.float32), np.float32([-1.0, 1.0, -1.0000001, 0.9921875, 0.99218744])])
-    x = x.reshape(-1, 1)  # every value, edges and the values just beside them included
+                        edges.astype(np.float32), np.float32([-1.0, 1.0, -1.0000001, 0.9921875, 0.99218744]),
+                        np.float32([np.nan, -np.inf, np.inf])])
+    x = x.reshape(-1, 1)  # every value, edges, the values just beside them, NaN and infinities included
     ref = (np.digitize(x, bins=edges) - 1).astype(np.int32)
     np.testing.assert_array_equal(pn.discretize_state(x, 256), ref)
 
