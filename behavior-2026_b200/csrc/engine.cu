@@ -8,6 +8,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -23,6 +24,7 @@
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
+#include "resize.cuh"
 
 using namespace p5;
 
@@ -116,10 +118,30 @@ struct pi05_engine {
   // few-token denoise: adaRMSNorm folded into the q/k/v and gate/up cluster GEMMs, fed by per-token
   // sum-of-squares partials from the producers of x (PI05_FUSE_NORM=0: separate rmsnorm launches)
   bool fuse_norm = true;
-  // receding-horizon stepping (pi05_act_batch): per slot the last chunk and the next row to execute
+  // receding-horizon stepping (pi05_act_batch): per slot the last post-processed chunk [horizon][act_dim],
+  // the next row to execute and the plans made (offset of the slot's noise stream)
+  int act_dim = P5_ACT_D, act_replan = 16;
+  std::vector<float> act_mean, act_std;
+  std::vector<uint8_t> act_delta;
+  uint64_t act_seed = 0;
   std::vector<std::vector<float>> act_chunk;
   std::vector<int> act_next;
+  std::vector<long> act_plans;
+  // device staging of pi05_act_batch's camera frames: host frames, resize tap tables, frame jobs
+  uint8_t* frame_stage = nullptr;
+  size_t frame_stage_bytes = 0;
+  int32_t* rs_tab = nullptr;
+  size_t rs_tab_bytes = 0;
+  p5rs::FrameJob* rs_jobs = nullptr;
+  size_t rs_jobs_bytes = 0;
   float* nrm_ss = nullptr;  // 2 buffers of [P5_EXP_W / 16 parts][64 tokens]
+  // verify run (pi05_verify): named intermediate points of sample 0 are copied to the host and passed
+  // to probe_fn after the kernels that produce them; null outside a verify run (and during capture)
+  pi05_probe_fn probe_fn = nullptr;
+  void* probe_ctx = nullptr;
+  // single-sample passes at batch position s0 (batch-invariant mode): the bodies offset the per-sample
+  // inputs, KV cache and flow state by s0 and share the scratch activations of position 0
+  int s0 = 0;
 };
 
 namespace {
@@ -752,6 +774,29 @@ bool attention(pi05_engine* e, const AttnArgs& a0, int batch, int hd) {
 
 int rows_grid(long rows_warps) { return (int)((rows_warps * 32 + 255) / 256); }
 
+// Verify run: wait for the stream, copy a [rows][cols] bf16 (ld-strided) or fp32 block of sample 0 to
+// the host as fp32 and hand it to the probe callback.
+bool emit_bf16(pi05_engine* e, const std::string& name, const bf16* dev, long rows, int cols, int ld) {
+  if (!e->probe_fn) return true;
+  std::vector<uint16_t> h((size_t)rows * cols);
+  CK(cudaMemcpy2DAsync(h.data(), (size_t)cols * 2, dev, (size_t)ld * 2, (size_t)cols * 2, rows,
+                       cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  std::vector<float> f(h.size());
+  for (size_t i = 0; i < h.size(); ++i) f[i] = p5_bf2f(h[i]);
+  e->probe_fn(name.c_str(), f.data(), (int64_t)f.size(), e->probe_ctx);
+  return true;
+}
+
+bool emit_f32(pi05_engine* e, const std::string& name, const float* dev, long n) {
+  if (!e->probe_fn) return true;
+  std::vector<float> f((size_t)n);
+  CK(cudaMemcpyAsync(f.data(), dev, (size_t)n * 4, cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  e->probe_fn(name.c_str(), f.data(), (int64_t)n, e->probe_ctx);
+  return true;
+}
+
 // ------------------------------------------------------------------ forward passes
 bool run_siglip(pi05_engine* e, int n) {
   const int T = n * e->cfg.n_cameras * P5_SIG_TOK, D = P5_SIG_W;
@@ -759,7 +804,7 @@ bool run_siglip(pi05_engine* e, int n) {
   {
     const long tot = (long)T * P5_SIG_KPAD;
     if (!launch(e, patchify_kernel, dim3((unsigned)std::min<long>((tot + 255) / 256, 65535)), dim3(256), 0, false,
-                A.images, A.patches, n * e->cfg.n_cameras))
+                A.images + (size_t)e->s0 * e->cfg.n_cameras * P5_IMG * P5_IMG * 3, A.patches, n * e->cfg.n_cameras))
       return false;
   }
   {
@@ -772,6 +817,7 @@ bool run_siglip(pi05_engine* e, int n) {
     L.add_ld = D;
     L.add_mod = 256;
     if (!linear(e, L)) return false;
+    if (!emit_bf16(e, "img.stem", A.sx, T, D, D)) return false;
   }
   for (int l = 0; l < e->cfg.siglip_layers; ++l) {
     const SigLayer& s = e->sig[l];
@@ -825,10 +871,12 @@ bool run_siglip(pi05_engine* e, int n) {
     m2.res = A.sx;
     m2.ld_res = D;
     if (!linear(e, m2)) return false;
+    if (!emit_bf16(e, "img.l" + std::to_string(l) + ".out", A.sx, T, D, D)) return false;
   }
   if (!launch(e, layernorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.sx, A.sy, e->sig_post_s, e->sig_post_b,
               T, D))
     return false;
+  if (!emit_bf16(e, "img.encoded", A.sy, T, D, D)) return false;
   // projector 1152 -> 2048 straight into the image rows of each sample's prefix
   const int img_tok = e->cfg.n_cameras * P5_SIG_TOK;
   for (int b = 0; b < n; ++b) {
@@ -838,7 +886,7 @@ bool run_siglip(pi05_engine* e, int n) {
     h.bias = e->sig_head_b;
     if (!linear(e, h)) return false;
   }
-  return true;
+  return emit_bf16(e, "img.tokens", A.px, img_tok, P5_GEM_W, P5_GEM_W);
 }
 
 bool run_gemma(pi05_engine* e, int n) {
@@ -850,8 +898,10 @@ bool run_gemma(pi05_engine* e, int n) {
     if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.px, A.ph, g.rms1, (const bf16*)nullptr,
                 T, D, 1, 0, D))
       return false;
-    bf16* kc = A.kcache + l * cache_layer;
-    bf16* vc = A.vcache + l * cache_layer;
+    const std::string pl = "pre.l" + std::to_string(l);
+    if (!emit_bf16(e, pl + ".norm1", A.ph, P, D, D)) return false;
+    bf16* kc = A.kcache + l * cache_layer + (size_t)e->s0 * P * P5_HD;
+    bf16* vc = A.vcache + l * cache_layer + (size_t)e->s0 * P * P5_HD;
     // q/k/v projection with RoPE (and the K/V cache write) in the epilogue
     Lin q{A.ph, D, T, e->gem_wqkv_il + (size_t)l * P5_QKV * D, D, P5_QKV, D};
     q.epi = EPI_ROPE;
@@ -866,6 +916,7 @@ bool run_gemma(pi05_engine* e, int n) {
     q.rope_k = kc;
     q.rope_v = vc;
     if (!linear(e, q)) return false;
+    if (!emit_bf16(e, pl + ".k", kc, P, P5_HD, P5_HD) || !emit_bf16(e, pl + ".v", vc, P, P5_HD, P5_HD)) return false;
     if (l == e->cfg.gemma_layers - 1) break;  // later outputs of the last layer feed nothing
     AttnArgs at = {};
     at.q = A.pqkv;
@@ -896,6 +947,7 @@ bool run_gemma(pi05_engine* e, int n) {
     if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.px, A.ph, g.rms2, (const bf16*)nullptr,
                 T, D, 1, 0, D))
       return false;
+    if (!emit_bf16(e, pl + ".norm2", A.ph, P, D, D)) return false;
     Lin gu{A.ph, D, T, g.wgu, D, 2 * P5_GEM_MLP, D};
     gu.epi = EPI_GEGLU;
     gu.out = A.pact;
@@ -908,6 +960,7 @@ bool run_gemma(pi05_engine* e, int n) {
     dn.res = A.px;
     dn.ld_res = D;
     if (!linear(e, dn)) return false;
+    if (!emit_bf16(e, pl + ".out", A.px, P, D, D)) return false;
   }
   return true;
 }
@@ -915,8 +968,12 @@ bool run_gemma(pi05_engine* e, int n) {
 bool run_prefill_body(pi05_engine* e, int n) {
   if (!run_siglip(e, n)) return false;
   if (e->cfg.n_text > 0 &&
-      !launch(e, embed_text_kernel, dim3(e->cfg.n_text, n), dim3(256), 0, true, (const int32_t*)e->A.tokens,
+      !launch(e, embed_text_kernel, dim3(e->cfg.n_text, n), dim3(256), 0, true,
+              (const int32_t*)e->A.tokens + (size_t)e->s0 * e->cfg.n_text,
               (const bf16*)e->embed, e->A.px, e->cfg.n_text, e->P, e->cfg.n_cameras * P5_SIG_TOK))
+    return false;
+  if (e->cfg.n_text > 0 && !emit_bf16(e, "txt.emb", e->A.px + (size_t)e->cfg.n_cameras * P5_SIG_TOK * P5_GEM_W,
+                                      e->cfg.n_text, P5_GEM_W, P5_GEM_W))
     return false;
   return run_gemma(e, n);
 }
@@ -1062,9 +1119,11 @@ bool run_denoise_mega(pi05_engine* e) {
 }
 
 bool run_denoise_body(pi05_engine* e, int n) {
-  if (mega_applies(e, n)) return run_denoise_mega(e);
+  if (mega_applies(e, n) && !e->probe_fn && e->s0 == 0) return run_denoise_mega(e);
   const int H = e->cfg.horizon, T = n * H, D = P5_EXP_W, P = e->P;
   Acts& A = e->A;
+  float* xt = A.xt + (size_t)e->s0 * H * P5_ACT_D;
+  const size_t kv_s0 = (size_t)e->s0 * P * P5_HD;
   const size_t cache_layer = (size_t)e->max_batch * P * P5_HD;
   const int MW = e->NM * 3 * D;  // modulation row width
   const float dtb = p5_dt_bf16(e->cfg.num_steps);
@@ -1086,9 +1145,11 @@ bool run_denoise_body(pi05_engine* e, int n) {
   };
   for (int s = 0; s < e->cfg.num_steps; ++s) {
     const bf16* mrow = e->mods + (size_t)s * MW;
-    if (!launch(e, action_in_kernel, dim3((T * D + 255) / 256), dim3(256), 0, true, (const float*)A.xt,
+    if (!launch(e, action_in_kernel, dim3((T * D + 255) / 256), dim3(256), 0, true, (const float*)xt,
                 (const bf16*)e->ain_w, (const bf16*)e->ain_b, A.ex, T, D, fnorm ? ss_mlp : (float*)nullptr, SSLD))
       return false;
+    const std::string sp = "suf.s" + std::to_string(s);
+    if (!emit_bf16(e, sp + ".in", A.ex, H, D, D)) return false;
     for (int l = 0; l < e->cfg.expert_layers; ++l) {
       const ExpLayer& x = e->ex[l];
       const bf16* m1 = mrow + (size_t)(2 * l) * 3 * D;
@@ -1127,8 +1188,8 @@ bool run_denoise_body(pi05_engine* e, int n) {
       at.out = A.eo;
       at.ldo = P5_QDIM;
       at.o_bstride = (long)H * P5_QDIM;
-      at.k1 = A.kcache + l * cache_layer;
-      at.v1 = A.vcache + l * cache_layer;
+      at.k1 = A.kcache + l * cache_layer + kv_s0;
+      at.v1 = A.vcache + l * cache_layer + kv_s0;
       at.ld1 = P5_HD;
       at.len1 = P;
       at.b1stride = (long)P * P5_HD;
@@ -1179,21 +1240,28 @@ bool run_denoise_body(pi05_engine* e, int n) {
         dn.ss_ld = SSLD;
       }
       if (!linear(e, dn)) return false;
+      if (!emit_bf16(e, sp + ".l" + std::to_string(l) + ".out", A.ex, H, D, D)) return false;
     }
     const bf16* mf = mrow + (size_t)(e->NM - 1) * 3 * D;
     if (!launch(e, rmsnorm_kernel, dim3(rows_grid(T)), dim3(256), 0, true, A.ex, A.eh, mf, mf + D, T, D, 1, 0, D))
       return false;
+    if (!emit_bf16(e, sp + ".final", A.eh, H, D, D)) return false;
+    // the verify run also keeps the velocity v (A.actions is otherwise unused scratch of this size)
     if (!launch(e, action_out_euler_kernel, dim3(rows_grid((long)T * P5_ACT_D)), dim3(256), 0, true,
-                (const bf16*)A.eh, (const bf16*)e->aout_w, (const bf16*)e->aout_b, A.xt, (float*)nullptr, T, D, dtb))
+                (const bf16*)A.eh, (const bf16*)e->aout_w, (const bf16*)e->aout_b, xt,
+                e->probe_fn ? A.actions : (float*)nullptr, T, D, dtb))
+      return false;
+    if (!emit_f32(e, sp + ".v", A.actions, (long)H * P5_ACT_D) || !emit_f32(e, sp + ".x", xt, (long)H * P5_ACT_D))
       return false;
   }
   return true;
 }
 
-// Capture `body` once per batch size and replay it.
+// Capture `body` once per batch size n (and single-sample position s0) and replay it.
 bool run_graph(pi05_engine* e, std::map<int, cudaGraphExec_t>& cache, std::map<int, long>& counts, int n,
                bool (*body)(pi05_engine*, int)) {
-  auto it = cache.find(n);
+  const int key = n + (e->s0 << 16);
+  auto it = cache.find(key);
   if (it == cache.end()) {
     cudaGraph_t g = nullptr;
     const long before = e->launches;
@@ -1209,8 +1277,8 @@ bool run_graph(pi05_engine* e, std::map<int, cudaGraphExec_t>& cache, std::map<i
     ce = cudaGraphInstantiate(&ex, g, 0);
     cudaGraphDestroy(g);
     if (ce != cudaSuccess) return set_err(e, std::string("graph instantiate: ") + cudaGetErrorString(ce));
-    counts[n] = e->launches - before;
-    it = cache.emplace(n, ex).first;
+    counts[key] = e->launches - before;
+    it = cache.emplace(key, ex).first;
   }
   CK(cudaGraphLaunch(it->second, e->stream));
   return true;
@@ -1242,6 +1310,52 @@ bool check_status(pi05_engine* e) {
 
 int fail_code(pi05_engine* e) {
   return e->err.rfind("device-side", 0) == 0 ? PI05_ERR_DEVICE : PI05_ERR_CUDA;
+}
+
+// Prefill of batch positions [0, n) whose images and tokens are already in A.images / A.tokens.  In
+// batch-invariant mode every position runs the single-sample graph (at its own offsets), so a sample's
+// result does not depend on the batch it came in.
+bool prefill_resident(pi05_engine* e, int n) {
+  if (!qkv_interleave_prepare(e)) return false;
+  if (!e->cfg.batch_invariant) return run_graph(e, e->prefill_graphs, e->prefill_launches, n, run_prefill_body);
+  for (int b = 0; b < n; ++b) {
+    e->s0 = b;
+    const bool ok = run_graph(e, e->prefill_graphs, e->prefill_launches, 1, run_prefill_body);
+    e->s0 = 0;
+    if (!ok) return false;
+  }
+  return true;
+}
+
+// Denoise of batch positions [0, n) from the noise already in A.xt (the chunk replaces it there).
+bool denoise_resident(pi05_engine* e, int n) {
+  const int nb = e->cfg.batch_invariant ? 1 : n;
+  if (mega_applies(e, nb) && !mega_prepare(e)) return false;
+  if (fused_rope_applies(e, nb) && !qkv_interleave_prepare(e)) return false;
+  if (!e->cfg.batch_invariant) return run_graph(e, e->denoise_graphs, e->denoise_launches, n, run_denoise_body);
+  for (int b = 0; b < n; ++b) {
+    e->s0 = b;
+    const bool ok = run_graph(e, e->denoise_graphs, e->denoise_launches, 1, run_denoise_body);
+    e->s0 = 0;
+    if (!ok) return false;
+  }
+  return true;
+}
+
+// Device buffer that grows to `need` bytes (contents are not kept).
+bool grow(pi05_engine* e, void** p, size_t* cap, size_t need) {
+  if (need <= *cap) return true;
+  if (*p) {
+    CK(cudaStreamSynchronize(e->stream));
+    CK(cudaFree(*p));
+    e->allocs.erase(std::find(e->allocs.begin(), e->allocs.end(), *p));
+    *p = nullptr;
+    *cap = 0;
+  }
+  const size_t bytes = need + need / 4;
+  if (!dalloc(e, p, bytes)) return false;
+  *cap = bytes;
+  return true;
 }
 
 // time conditioning -> modulation table for every step (depends only on the fixed schedule)
@@ -1474,6 +1588,7 @@ extern "C" {
 
 void pi05_default_config(pi05_config* c) {
   if (!c) return;
+  c->batch_invariant = 0;
   c->siglip_layers = 27;
   c->gemma_layers = 18;
   c->expert_layers = 18;
@@ -1492,7 +1607,8 @@ pi05_engine* pi05_create(const pi05_config* c, int device, int max_batch, char* 
   pi05_default_config(&cfg);
   if (c) cfg = *c;
   if (cfg.siglip_layers < 0 || cfg.gemma_layers < 1 || cfg.expert_layers != cfg.gemma_layers || cfg.num_steps < 1 ||
-      cfg.n_cameras < 1 || cfg.n_text < 0 || cfg.horizon < 1 || cfg.horizon > 128 || max_batch < 1)
+      cfg.n_cameras < 1 || cfg.n_text < 0 || cfg.horizon < 1 || cfg.horizon > 128 || max_batch < 1 ||
+      (cfg.batch_invariant != 0 && cfg.batch_invariant != 1) || max_batch > 32767)
     return fail("pi05_create: invalid configuration");
   pi05_engine* e = new pi05_engine();
   e->cfg = cfg;
@@ -1514,6 +1630,7 @@ void pi05_destroy(pi05_engine* e) {
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (auto& kv : e->denoise_graphs) cudaGraphExecDestroy(kv.second);
   for (auto& kv : e->prefill_graphs) cudaGraphExecDestroy(kv.second);
+  if (e->tr) dp_release(e->tr->dp);
   delete e->tr;
   for (void* p : e->allocs) cudaFree(p);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -1668,8 +1785,7 @@ int pi05_prefill(pi05_engine* e, int n, const uint8_t* images, const int32_t* to
   const size_t ib = (size_t)n * e->cfg.n_cameras * P5_IMG * P5_IMG * 3;
   if (!copy_in(e, e->A.images, images, ib)) return PI05_ERR_CUDA;
   if (e->cfg.n_text > 0 && !copy_in(e, e->A.tokens, tokens, (size_t)n * e->cfg.n_text * 4)) return PI05_ERR_CUDA;
-  if (!qkv_interleave_prepare(e)) return fail_code(e);
-  if (!run_graph(e, e->prefill_graphs, e->prefill_launches, n, run_prefill_body)) return fail_code(e);
+  if (!prefill_resident(e, n)) return fail_code(e);
   e->prefix_n = n;
   return PI05_OK;
 }
@@ -1732,9 +1848,7 @@ int pi05_denoise(pi05_engine* e, int n, const float* noise, float* actions) {
   cudaSetDevice(e->device);
   const size_t bytes = (size_t)n * e->cfg.horizon * P5_ACT_D * 4;
   if (!copy_in(e, e->A.xt, noise, bytes)) return PI05_ERR_CUDA;
-  if (mega_applies(e, n) && !mega_prepare(e)) return fail_code(e);
-  if (fused_rope_applies(e, n) && !qkv_interleave_prepare(e)) return fail_code(e);
-  if (!run_graph(e, e->denoise_graphs, e->denoise_launches, n, run_denoise_body)) return fail_code(e);
+  if (!denoise_resident(e, n)) return fail_code(e);
   if (cudaMemcpyAsync(actions, e->A.xt, bytes, cudaMemcpyDefault, e->stream) != cudaSuccess) return PI05_ERR_CUDA;
   if (!is_device_ptr(actions)) return pi05_sync(e);
   return PI05_OK;
@@ -1745,6 +1859,36 @@ int pi05_infer(pi05_engine* e, int n, const uint8_t* images, const int32_t* toke
   int rc = pi05_prefill(e, n, images, tokens);
   if (rc != PI05_OK) return rc;
   return pi05_denoise(e, n, noise, actions);
+}
+
+int pi05_verify(pi05_engine* e, const uint8_t* images, const int32_t* tokens, const float* noise, float* actions,
+                pi05_probe_fn fn, void* ctx) {
+  if (!e) return PI05_ERR_ARG;
+  if (!images || (e->cfg.n_text > 0 && !tokens) || !noise) {
+    e->err = "pi05_verify: bad arguments";
+    return PI05_ERR_ARG;
+  }
+  if (!e->weights_ready) {
+    e->err = "pi05_verify: weights not loaded";
+    return PI05_ERR_STATE;
+  }
+  cudaSetDevice(e->device);
+  const size_t ib = (size_t)e->cfg.n_cameras * P5_IMG * P5_IMG * 3, ab = (size_t)e->cfg.horizon * P5_ACT_D * 4;
+  if (!copy_in(e, e->A.images, images, ib)) return PI05_ERR_CUDA;
+  if (e->cfg.n_text > 0 && !copy_in(e, e->A.tokens, tokens, (size_t)e->cfg.n_text * 4)) return PI05_ERR_CUDA;
+  if (!copy_in(e, e->A.xt, noise, ab)) return PI05_ERR_CUDA;
+  if (!qkv_interleave_prepare(e)) return fail_code(e);
+  e->probe_fn = fn;
+  e->probe_ctx = ctx;
+  bool ok = run_prefill_body(e, 1);
+  if (ok) e->prefix_n = 1;
+  ok = ok && run_denoise_body(e, 1);
+  e->probe_fn = nullptr;
+  e->probe_ctx = nullptr;
+  if (!ok) return fail_code(e);
+  if (actions && cudaMemcpyAsync(actions, e->A.xt, ab, cudaMemcpyDefault, e->stream) != cudaSuccess)
+    return PI05_ERR_CUDA;
+  return pi05_sync(e);
 }
 
 // kernels per call, as captured (for launch accounting in benchmarks)
@@ -1772,9 +1916,19 @@ void pi05_synth_noise(uint64_t seed, int sample, int horizon, float* out) {
 
 int pi05_op_linear(pi05_engine* e, int T, int F, int K, const void* x, const void* w, const void* bias,
                    const void* res, const void* gate, int epi, void* out) {
-  if (!e || T < 1 || F < 1 || K < 8 || K % 8 || epi < EPI_STORE || epi > EPI_F32 || !x || !w || !out ||
-      ((epi == EPI_RESID || epi == EPI_GATED) && !res) || (epi == EPI_GATED && !gate) || (epi == EPI_GEGLU && F % 32))
+  if (!e) return PI05_ERR_ARG;
+  if (T < 1 || F < 1 || K < 8 || K % 8 || epi < EPI_STORE || epi > EPI_F32 || !x || !w || !out ||
+      ((epi == EPI_RESID || epi == EPI_GATED) && !res) || (epi == EPI_GATED && !gate) || (epi == EPI_GEGLU && F % 32)) {
+    set_err(e, "pi05_op_linear: bad shape or missing operand (K % 8 == 0, GeGLU F % 32 == 0, res/gate for epi 2/3)");
     return PI05_ERR_ARG;
+  }
+  // the normal-orientation epilogue moves 8 bf16 (or 4 fp32) values per access: rows of out, res and the
+  // bias/gate vectors must start on 16-byte boundaries
+  const uintptr_t al = (uintptr_t)x | (uintptr_t)w | (uintptr_t)out | (uintptr_t)bias | (uintptr_t)res | (uintptr_t)gate;
+  if (F % 8 || (al & 15)) {
+    set_err(e, "pi05_op_linear: F must be a multiple of 8 and x, w, out, bias, res, gate 16-byte aligned");
+    return PI05_ERR_ARG;
+  }
   cudaSetDevice(e->device);
   Lin L{(const bf16*)x, K, T, (const bf16*)w, K, F, K};
   L.epi = epi;
@@ -1966,58 +2120,223 @@ int pi05_set_stage(pi05_engine* e, int slot, int stage, int mode) {
   return PI05_OK;
 }
 
-// Receding-horizon stepping over environment slots (reference pi05_act_batch, π05_네이티브엔진.md:292-296
-// and :33: the chunk is re-planned after a fixed number of executed steps).  Host-side bookkeeping
-// over pi05_infer: one batched inference for the listed slots that need a new chunk.
-int pi05_act_batch(pi05_engine* e, int n, const int* slots, const uint8_t* images, const int32_t* tokens,
-                   const float* noise, int replan, int act_dim, float* out) {
-  if (!e || n < 1 || n > e->max_batch || !slots || !images || !tokens || !noise || !out) return PI05_ERR_ARG;
-  const int H = e->cfg.horizon;
-  if (replan < 1 || replan > H || act_dim < 1 || act_dim > P5_ACT_D) return PI05_ERR_ARG;
-  if (is_device_ptr(images) || is_device_ptr(tokens) || is_device_ptr(noise) || is_device_ptr(out)) {
-    set_err(e, "pi05_act_batch: inputs and output are host buffers");
+// Receding-horizon stepping over environment slots (reference pi05_act_batch, π05_네이티브엔진.md:292-297
+// and :33: camera frames as the evaluator passes them, the chunk re-planned after a fixed number of
+// executed steps, actions returned as the wrapper returns them).
+int pi05_set_act_config(pi05_engine* e, const pi05_act_config* c) {
+  if (!e || !c) return PI05_ERR_ARG;
+  if (c->act_dim < 1 || c->act_dim > P5_ACT_D || c->replan < 1 || c->replan > e->cfg.horizon ||
+      (!c->mean) != (!c->std)) {
+    set_err(e, "pi05_set_act_config: needs 1 <= act_dim <= 32, 1 <= replan <= horizon, mean and std both or neither");
     return PI05_ERR_ARG;
   }
+  e->act_dim = c->act_dim;
+  e->act_replan = c->replan;
+  e->act_mean.clear();
+  e->act_std.clear();
+  e->act_delta.clear();
+  if (c->mean) {
+    e->act_mean.assign(c->mean, c->mean + c->act_dim);
+    e->act_std.assign(c->std, c->std + c->act_dim);
+  }
+  if (c->delta_mask) e->act_delta.assign(c->delta_mask, c->delta_mask + c->act_dim);
+  e->act_seed = c->noise_seed;
+  e->act_chunk.assign(e->max_batch, std::vector<float>());
+  e->act_next.assign(e->max_batch, 0);
+  e->act_plans.assign(e->max_batch, 0);
+  return PI05_OK;
+}
+
+namespace {
+
+// Resize the camera frames of the m re-planning slots into batch positions [0, m) of A.images.
+bool stage_frames(pi05_engine* e, const std::vector<const pi05_frame*>& fr) {
+  const int ncam = e->cfg.n_cameras, m = (int)fr.size() / ncam;
+  std::vector<p5rs::FrameJob> jobs(fr.size());
+  std::vector<int32_t> tab;
+  size_t host_bytes = 0;
+  std::vector<char> on_dev(fr.size(), 0);
+  for (size_t j = 0; j < fr.size(); ++j) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, fr[j]->data) != cudaSuccess) {
+      cudaGetLastError();
+      at.type = cudaMemoryTypeUnregistered;
+    }
+    on_dev[j] = at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+    if (on_dev[j] && at.device != e->device) return set_err(e, "pi05_act_batch: a frame is on another device");
+    if (!on_dev[j]) host_bytes += (size_t)fr[j]->height * fr[j]->width * fr[j]->channels;
+  }
+  void* stage = e->frame_stage;
+  if (!grow(e, &stage, &e->frame_stage_bytes, std::max<size_t>(host_bytes, 1))) return false;
+  e->frame_stage = (uint8_t*)stage;
+  size_t off = 0;
+  for (size_t j = 0; j < fr.size(); ++j) {
+    const pi05_frame& f = *fr[j];
+    p5rs::Geometry g;
+    if (!p5rs::geometry(f.height, f.width, P5_IMG, P5_IMG, &g)) return set_err(e, "pi05_act_batch: frame too small to resize");
+    p5rs::FrameJob& J = jobs[j];
+    J.h = f.height;
+    J.w = f.width;
+    J.ch = f.channels;
+    J.rh = g.rh;
+    J.rw = g.rw;
+    J.pad_h = g.pad_h;
+    J.pad_w = g.pad_w;
+    J.dst = e->A.images + j * (size_t)P5_IMG * P5_IMG * 3;  // position j / ncam, camera j % ncam
+    if (on_dev[j]) {
+      J.src = (const uint8_t*)f.data;
+      J.stride = (long)f.stride;
+    } else {
+      const size_t pitch = (size_t)f.width * f.channels;
+      CK(cudaMemcpy2DAsync(e->frame_stage + off, pitch, f.data, (size_t)f.stride, pitch, f.height,
+                           cudaMemcpyHostToDevice, e->stream));
+      J.src = e->frame_stage + off;
+      J.stride = (long)pitch;
+      off += pitch * f.height;
+    }
+    auto add = [&](int n_in, int n_out, int* taps) -> long {
+      if (n_in == n_out) return -1;
+      const p5rs::AxisTaps t = p5rs::axis_taps(n_in, n_out);
+      const long at = (long)tab.size();
+      tab.insert(tab.end(), t.first.begin(), t.first.end());
+      tab.insert(tab.end(), t.count.begin(), t.count.end());
+      tab.insert(tab.end(), t.w.begin(), t.w.end());
+      *taps = t.taps;
+      return at;
+    };
+    J.tw = J.th = 0;
+    J.tab_w = add(f.width, g.rw, &J.tw);
+    J.tab_h = add(f.height, g.rh, &J.th);
+  }
+  void* tp = e->rs_tab;
+  void* jp = e->rs_jobs;
+  if (!grow(e, &tp, &e->rs_tab_bytes, std::max<size_t>(tab.size() * 4, 4)) ||
+      !grow(e, &jp, &e->rs_jobs_bytes, jobs.size() * sizeof(p5rs::FrameJob)))
+    return false;
+  e->rs_tab = (int32_t*)tp;
+  e->rs_jobs = (p5rs::FrameJob*)jp;
+  if (!tab.empty()) CK(cudaMemcpyAsync(e->rs_tab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, e->stream));
+  CK(cudaMemcpyAsync(e->rs_jobs, jobs.data(), jobs.size() * sizeof(p5rs::FrameJob), cudaMemcpyHostToDevice,
+                     e->stream));
+  const int px = P5_IMG * P5_IMG;
+  resize_with_pad_kernel<<<dim3((px + 255) / 256, (unsigned)jobs.size()), 256, 0, e->stream>>>(e->rs_jobs, e->rs_tab,
+                                                                                               P5_IMG, P5_IMG);
+  CK(cudaGetLastError());
+  (void)m;
+  return true;
+}
+
+}  // namespace
+
+int pi05_act_batch(pi05_engine* e, int n, const int* slots, const pi05_frame* frames, const int32_t* tokens,
+                   const float* state, const float* noise, float* out) {
+  if (!e) return PI05_ERR_ARG;
+  if (n < 1 || n > e->max_batch || !slots || !frames || (e->cfg.n_text > 0 && !tokens) || !out) {
+    set_err(e, "pi05_act_batch: bad arguments");
+    return PI05_ERR_ARG;
+  }
+  if (!e->weights_ready) {
+    set_err(e, "pi05_act_batch: weights not loaded");
+    return PI05_ERR_STATE;
+  }
+  cudaSetDevice(e->device);
   if ((int)e->act_chunk.size() != e->max_batch) {
     e->act_chunk.assign(e->max_batch, std::vector<float>());
     e->act_next.assign(e->max_batch, 0);
+    e->act_plans.assign(e->max_batch, 0);
   }
+  const int H = e->cfg.horizon, ncam = e->cfg.n_cameras, ad = e->act_dim;
   std::vector<int> need;  // positions in the call whose slot re-plans
   for (int i = 0; i < n; ++i) {
     const int sl = slots[i];
-    if (sl < 0 || sl >= e->max_batch) return PI05_ERR_ARG;
+    if (sl < 0 || sl >= e->max_batch) {
+      set_err(e, "pi05_act_batch: slot out of range");
+      return PI05_ERR_ARG;
+    }
     for (int j = 0; j < i; ++j)
-      if (slots[j] == sl) return PI05_ERR_ARG;  // a slot steps at most once per call
-    if (e->act_chunk[sl].empty() || e->act_next[sl] >= replan) need.push_back(i);
+      if (slots[j] == sl) {
+        set_err(e, "pi05_act_batch: a slot steps at most once per call");
+        return PI05_ERR_ARG;
+      }
+    if (e->act_chunk[sl].empty() || e->act_next[sl] >= e->act_replan) need.push_back(i);
+  }
+  // state rows (host copy; the dims of the delta mask are added to the re-planned chunks)
+  std::vector<float> st;
+  if (state && !e->act_delta.empty()) {
+    st.resize((size_t)n * ad);
+    if (cudaMemcpy(st.data(), state, st.size() * 4, cudaMemcpyDefault) != cudaSuccess) return PI05_ERR_CUDA;
   }
   if (!need.empty()) {
-    const size_t img = (size_t)e->cfg.n_cameras * P5_IMG * P5_IMG * 3, tok = (size_t)e->cfg.n_text,
-                 nz = (size_t)H * P5_ACT_D;
     const int m = (int)need.size();
-    std::vector<uint8_t> bi(img * m);
-    std::vector<int32_t> bt(tok * m);
-    std::vector<float> bn(nz * m), ba(nz * m);
+    std::vector<const pi05_frame*> fr;
+    for (int k = 0; k < m; ++k)
+      for (int c = 0; c < ncam; ++c) {
+        const pi05_frame* f = &frames[(size_t)need[k] * ncam + c];
+        if (!f->data || f->height < 1 || f->width < 1 || (f->channels != 3 && f->channels != 4) ||
+            f->stride < (int64_t)f->width * f->channels) {
+          set_err(e, "pi05_act_batch: bad camera frame (data, height, width, channels 3/4, stride >= width*channels)");
+          return PI05_ERR_ARG;
+        }
+        fr.push_back(f);
+      }
+    if (!stage_frames(e, fr)) return fail_code(e);
+    const size_t nz = (size_t)H * P5_ACT_D;
     for (int k = 0; k < m; ++k) {
-      const int i = need[k];
-      memcpy(bi.data() + img * k, images + img * i, img);
-      memcpy(bt.data() + tok * k, tokens + tok * i, tok * sizeof(int32_t));
-      memcpy(bn.data() + nz * k, noise + nz * i, nz * sizeof(float));
+      const int i = need[k], sl = slots[i];
+      if (e->cfg.n_text > 0 &&
+          !copy_in(e, e->A.tokens + (size_t)k * e->cfg.n_text, tokens + (size_t)i * e->cfg.n_text, e->cfg.n_text * 4))
+        return PI05_ERR_CUDA;
+      if (noise) {
+        if (!copy_in(e, e->A.xt + k * nz, noise + i * nz, nz * 4)) return PI05_ERR_CUDA;
+      } else {
+        // the slot's own stream: plan p of slot s draws elements [p * nz, (p + 1) * nz) of the generator
+        // stream (act seed, noise, s); the first plan equals pi05_synth_noise(seed, s)
+        std::vector<float> z(nz);
+        const uint64_t key = p5_key(e->act_seed, K_IN_NOISE, (uint32_t)sl);
+        const float sc = p5_scale_for_std(1.0);
+        for (size_t q = 0; q < nz; ++q) z[q] = p5_normal(key, (uint64_t)(e->act_plans[sl] * nz + q), sc);
+        if (cudaMemcpy(e->A.xt + k * nz, z.data(), nz * 4, cudaMemcpyHostToDevice) != cudaSuccess) return PI05_ERR_CUDA;
+      }
     }
-    const int rc = pi05_infer(e, m, bi.data(), bt.data(), bn.data(), ba.data());
+    if (!prefill_resident(e, m)) return fail_code(e);
+    e->prefix_n = m;
+    if (!denoise_resident(e, m)) return fail_code(e);
+    std::vector<float> ch((size_t)m * nz);
+    if (cudaMemcpyAsync(ch.data(), e->A.xt, ch.size() * 4, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
+      return PI05_ERR_CUDA;
+    const int rc = pi05_sync(e);
     if (rc != PI05_OK) return rc;
+    // post-process each new chunk as the wrapper does: un-normalise (openpi Unnormalize, z-score), then
+    // add the state to the delta dims (AbsoluteActions), keep the first act_dim dims
+    const float eps = 1e-6f;
     for (int k = 0; k < m; ++k) {
-      const int sl = slots[need[k]];
-      e->act_chunk[sl].assign(ba.begin() + nz * k, ba.begin() + nz * (k + 1));
+      const int i = need[k], sl = slots[i];
+      std::vector<float>& c = e->act_chunk[sl];
+      c.assign((size_t)H * ad, 0.f);
+      for (int r = 0; r < H; ++r)
+        for (int j = 0; j < ad; ++j) {
+          float a = ch[(size_t)k * nz + (size_t)r * P5_ACT_D + j];
+          if (!e->act_mean.empty()) a = a * (e->act_std[j] + eps) + e->act_mean[j];
+          if (!st.empty() && e->act_delta[j]) a += st[(size_t)i * ad + j];
+          c[(size_t)r * ad + j] = a;
+        }
       e->act_next[sl] = 0;
+      ++e->act_plans[sl];
     }
   }
+  std::vector<float> rows((size_t)n * ad);
   for (int i = 0; i < n; ++i) {
     const int sl = slots[i];
-    memcpy(out + (size_t)i * act_dim, e->act_chunk[sl].data() + (size_t)e->act_next[sl] * P5_ACT_D,
-           act_dim * sizeof(float));
+    memcpy(rows.data() + (size_t)i * ad, e->act_chunk[sl].data() + (size_t)e->act_next[sl] * ad, ad * sizeof(float));
     ++e->act_next[sl];
   }
+  if (cudaMemcpy(out, rows.data(), rows.size() * 4, cudaMemcpyDefault) != cudaSuccess) return PI05_ERR_CUDA;
   return PI05_OK;
+}
+
+int pi05_act(pi05_engine* e, int slot, const pi05_frame* frames, const int32_t* tokens, const float* state,
+             const float* noise, float* out) {
+  return pi05_act_batch(e, 1, &slot, frames, tokens, state, noise, out);
 }
 
 int pi05_reset_slot(pi05_engine* e, int slot) {

@@ -1,18 +1,7 @@
-// preprocess.cu — host-side camera-frame preprocessing: aspect-preserving resize into a zero-padded
-// frame (the reference's resize_with_pad, π05_네이티브엔진.md:296-297, which follows openpi's
-// image_tools.resize_with_pad over Pillow's bilinear resize).  Host code only; no GPU is involved.
-//
-// Geometry (openpi): ratio = max(w / out_w, h / out_h) in double precision; the resized image is
-// int(w / ratio) x int(h / ratio), pasted at (int((out_w - rw) / 2), int((out_h - rh) / 2)) into a
-// zero frame; a frame already of the output size is copied unchanged.
-//
-// Resampling (Pillow's 8-bit bilinear "reduce-aware" filter, restated): separable, one pass per axis
-// whose size changes (width first, then height).  Output sample i of an axis of n_in -> n_out samples
-// has centre c = (i + 0.5) * s, s = n_in / n_out; the triangle filter is widened by f = max(s, 1)
-// (support f), taps x in [int(c - f + 0.5) clamped at 0, int(c + f + 0.5) clamped at n_in), weights
-// tri((x - c + 0.5) / f) normalised to sum 1, then rounded to fixed point with 22 fraction bits
-// (round half away from zero).  A pass accumulates the 8-bit samples times the integer weights from
-// 2^21 (rounding), shifts by 22 and clamps to [0, 255].
+// preprocess.cu — host-side camera-frame preprocessing (the reference's resize_with_pad,
+// π05_네이티브엔진.md:296-297, after openpi's image_tools.resize_with_pad over Pillow's bilinear resize;
+// geometry and filter in resize.cuh, shared with the device kernel of pi05_act_batch) and the state /
+// action transforms of the reference wrapper.  Host code only; no GPU is involved.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -20,55 +9,15 @@
 #include <vector>
 
 #include "../../include/pi05.h"
+#define P5RS_HOST_ONLY  // the device kernel is compiled with the engine
+#include "resize.cuh"
 
 namespace {
 
-constexpr int RS_BITS = 22;
-
-struct AxisTaps {
-  int taps = 0;                  // weights per output sample
-  std::vector<int> first, count;  // first input sample and number of taps per output sample
-  std::vector<int32_t> w;         // [n_out][taps]
-};
-
-AxisTaps axis_taps(int n_in, int n_out) {
-  AxisTaps t;
-  const double s = (double)n_in / (double)n_out;
-  const double f = s < 1.0 ? 1.0 : s;
-  t.taps = (int)std::ceil(f) * 2 + 1;
-  t.first.resize(n_out);
-  t.count.resize(n_out);
-  t.w.assign((size_t)n_out * t.taps, 0);
-  std::vector<double> k(t.taps);
-  for (int i = 0; i < n_out; ++i) {
-    const double c = (i + 0.5) * s;
-    int lo = (int)(c - f + 0.5);
-    if (lo < 0) lo = 0;
-    int hi = (int)(c + f + 0.5);
-    if (hi > n_in) hi = n_in;
-    const int cnt = hi - lo;
-    double sum = 0.0;
-    for (int x = 0; x < cnt; ++x) {
-      const double d = std::fabs((x + lo - c + 0.5) / f);
-      k[x] = d < 1.0 ? 1.0 - d : 0.0;
-      sum += k[x];
-    }
-    for (int x = 0; x < cnt; ++x) {
-      const double v = sum != 0.0 ? k[x] / sum : k[x];
-      const double q = v * (double)(1 << RS_BITS);
-      t.w[(size_t)i * t.taps + x] = (int32_t)(q < 0.0 ? q - 0.5 : q + 0.5);
-    }
-    t.first[i] = lo;
-    t.count[i] = cnt;
-  }
-  return t;
-}
-
-inline uint8_t rs_clip(int32_t acc) {
-  if (acc <= 0) return 0;
-  const int32_t v = acc >> RS_BITS;
-  return v > 255 ? 255 : (uint8_t)v;
-}
+using p5rs::AxisTaps;
+using p5rs::axis_taps;
+using p5rs::RS_BITS;
+inline uint8_t rs_clip(int32_t acc) { return p5rs::clip8(acc); }
 
 // width pass: in [h][w_in][3] -> out [h][w_out][3]
 void resample_width(const uint8_t* in, int h, int w_in, uint8_t* out, int w_out) {
@@ -119,9 +68,9 @@ int pi05_resize_with_pad(const uint8_t* src, int h, int w, int channels, long st
     memcpy(dst, rgb.data(), rgb.size());
     return PI05_OK;
   }
-  const double ratio = std::fmax((double)w / (double)out_w, (double)h / (double)out_h);
-  const int rh = (int)((double)h / ratio), rw = (int)((double)w / ratio);
-  if (rh < 1 || rw < 1 || rh > out_h || rw > out_w) return PI05_ERR_ARG;
+  p5rs::Geometry geo;
+  if (!p5rs::geometry(h, w, out_h, out_w, &geo)) return PI05_ERR_ARG;
+  const int rh = geo.rh, rw = geo.rw;
   std::vector<uint8_t> a = rgb, b;
   int ch = h, cw = w;
   if (rw != cw) {
@@ -136,7 +85,7 @@ int pi05_resize_with_pad(const uint8_t* src, int h, int w, int channels, long st
     a.swap(b);
     ch = rh;
   }
-  const int pad_h = std::max(0, (int)((out_h - rh) / 2.0)), pad_w = std::max(0, (int)((out_w - rw) / 2.0));
+  const int pad_h = geo.pad_h, pad_w = geo.pad_w;
   memset(dst, 0, (size_t)out_h * out_w * 3);
   for (int y = 0; y < rh; ++y)
     memcpy(dst + ((size_t)(y + pad_h) * out_w + pad_w) * 3, &a[(size_t)y * rw * 3], (size_t)rw * 3);

@@ -16,6 +16,10 @@
 //     overlap on the GPU (different streams, no ordering between them) race on it.
 //   * The tickets are cleared at the start of every call; the partial tiles need no clearing
 //     because each is fully written before it is read.
+//   * The kernel's waits are bounded.  A wait that gives up records a code in a status word at the
+//     front of the array and the output of that call is incomplete; later calls skip their work
+//     until pi05_linear_static_status reads the word (after waiting for the stream), clears it and
+//     returns PI05_ERR_DEVICE.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -29,7 +33,8 @@
 using namespace p5;
 
 #define P5_STATIC_SCRATCH_BYTES (16u << 20)
-#define P5_STATIC_TICKET_BYTES (16u << 10)  // 4096 tickets at the front of the array
+#define P5_STATIC_STATUS_BYTES 256u         // status word of the bounded waits, at the front of the array
+#define P5_STATIC_TICKET_BYTES (16u << 10)  // then 4096 tickets, then the partial tiles
 #define P5_STATIC_MAX_T 64
 #define P5_STATIC_MAX_F 65536
 #define P5_STATIC_MAX_K 65536
@@ -100,8 +105,9 @@ extern "C" PI05_API int pi05_linear_static(int T, int F, int K, const void* x, c
   if (T < 1 || T > P5_STATIC_MAX_T || F < 1 || F > P5_STATIC_MAX_F || K < 8 || K > P5_STATIC_MAX_K || K % 8)
     return fail(err, err_len, PI05_ERR_ARG,
                 "pi05_linear_static: needs 1 <= T <= 64, 1 <= F <= 65536, 8 <= K <= 65536, K % 8 == 0");
-  if (!x || !w || !out || ((uintptr_t)x & 15) || ((uintptr_t)w & 15))
-    return fail(err, err_len, PI05_ERR_ARG, "pi05_linear_static: x, w, out must be device pointers, x/w 16-byte aligned");
+  if (!x || !w || !out || ((uintptr_t)x & 15) || ((uintptr_t)w & 15) || ((uintptr_t)out & 15) || ((uintptr_t)bias & 1))
+    return fail(err, err_len, PI05_ERR_ARG,
+                "pi05_linear_static: x, w, out must be 16-byte aligned device pointers, bias 2-byte aligned or NULL");
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return fail(err, err_len, PI05_ERR_CUDA, "pi05_linear_static: no current device");
@@ -121,7 +127,8 @@ extern "C" PI05_API int pi05_linear_static(int T, int F, int K, const void* x, c
   ga.group_m = 1;
   const int kt = (K + 63) / 64;
   const size_t tile_bytes = (size_t)128 * 64 * 4;
-  const int max_partials = (int)((P5_STATIC_SCRATCH_BYTES - P5_STATIC_TICKET_BYTES) / tile_bytes);
+  const int max_partials =
+      (int)((P5_STATIC_SCRATCH_BYTES - P5_STATIC_STATUS_BYTES - P5_STATIC_TICKET_BYTES) / tile_bytes);
   int splits = 1;
   if (ga.tiles_m < s.num_sms && kt >= 4) splits = std::max(1, std::min(s.num_sms / ga.tiles_m, kt / 2));
   while (splits > 1 && (splits * ga.tiles_m > max_partials || ga.tiles_m > (int)(P5_STATIC_TICKET_BYTES / 4)))
@@ -136,19 +143,42 @@ extern "C" PI05_API int pi05_linear_static(int T, int F, int K, const void* x, c
   ga.out_scale = 1.0f;
   ga.add_mod = 1;
   ga.gate_div = 1;
-  ga.counters = reinterpret_cast<int*>(s.scratch);
-  ga.ws = reinterpret_cast<float*>(s.scratch + P5_STATIC_TICKET_BYTES);
-  ga.status = nullptr;
+  ga.status = reinterpret_cast<int*>(s.scratch);
+  ga.counters = reinterpret_cast<int*>(s.scratch + P5_STATIC_STATUS_BYTES);
+  ga.ws = reinterpret_cast<float*>(s.scratch + P5_STATIC_STATUS_BYTES + P5_STATIC_TICKET_BYTES);
   ga.pdl = 0;
 
   CUtensorMap ta, tb;
   if (!tmap(&ta, w, F, K, 128) || !tmap(&tb, x, T, K, 64))
     return fail(err, err_len, PI05_ERR_ARG, "pi05_linear_static: tensor map rejected the operands");
-  if (cudaMemsetAsync(s.scratch, 0, P5_STATIC_TICKET_BYTES, st) != cudaSuccess)
+  if (cudaMemsetAsync(s.scratch + P5_STATIC_STATUS_BYTES, 0, P5_STATIC_TICKET_BYTES, st) != cudaSuccess)
     return fail(err, err_len, PI05_ERR_CUDA, "pi05_linear_static: clearing the tickets failed");
   const int units = ga.tiles_m * ga.splits;
   gemm_tc_kernel<64, EPI_STORE><<<dim3(std::min(units, s.num_sms)), 256, GemmCfg<64>::SMEM, st>>>(ta, tb, ga);
   const cudaError_t ce = cudaGetLastError();
   if (ce != cudaSuccess) return fail(err, err_len, PI05_ERR_CUDA, cudaGetErrorString(ce));
   return PI05_OK;
+}
+
+// Waits for `stream`, then reads and clears the status word that the kernel's bounded waits write.
+extern "C" PI05_API int pi05_linear_static_status(void* stream, char* err, size_t err_len) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(err, err_len, PI05_ERR_CUDA, "pi05_linear_static_status: no current device");
+  const int rc = setup(dev, err, err_len);
+  if (rc != PI05_OK) return rc;
+  const DeviceState& s = g_dev[dev];
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t ce = cudaStreamSynchronize(st);
+  if (ce != cudaSuccess) return fail(err, err_len, PI05_ERR_CUDA, cudaGetErrorString(ce));
+  int word = 0;
+  ce = cudaMemcpy(&word, s.scratch, sizeof(int), cudaMemcpyDeviceToHost);
+  if (ce != cudaSuccess) return fail(err, err_len, PI05_ERR_CUDA, cudaGetErrorString(ce));
+  if (word == 0) return PI05_OK;
+  if (cudaMemset(s.scratch, 0, sizeof(int)) != cudaSuccess)
+    return fail(err, err_len, PI05_ERR_CUDA, "pi05_linear_static_status: clearing the status word failed");
+  char msg[128];
+  snprintf(msg, sizeof msg, "pi05_linear_static: a device-side wait gave up (status %d); that call's output is incomplete",
+           word);
+  return fail(err, err_len, PI05_ERR_DEVICE, msg);
 }

@@ -16,6 +16,7 @@
 #include "attention_bwd.cuh"
 #include "attention_bwd_tc.cuh"
 #include "train_kernels.cuh"
+#include "dp_nccl.cuh"
 
 namespace {
 
@@ -42,6 +43,12 @@ struct Trainer {
   pi05_lora_config cfg;
   int mb = 8;
   int n_total = 0;  // samples in the current optimizer step (loss normalisation)
+  int n_seen = 0;   // samples accumulated since the last zero_grads: the buffer holds their mean
+  // data parallelism (pi05_lora_attach_nccl): `overlap` averages each layer's gradients over the ranks as
+  // soon as the backward pass of the current (last) micro-batch has finished that layer; `reduced` says
+  // the buffer already holds the average of the ranks
+  struct DpComm* dp = nullptr;
+  bool overlap = false, reduced = false;
   long n_params = 0;
   float *p = nullptr, *g = nullptr, *m = nullptr, *v = nullptr;
   float* sumsq = nullptr;
@@ -704,16 +711,34 @@ bool micro_step(pi05_engine* e, int nb, const float* h_t) {
                      prefix ? T->gx_p : T->gx_s, R, D);
     };
     if (!qkv_bwd(false) || !qkv_bwd(true)) return false;
+    if (T->overlap) {  // layer l's adapter gradients (both stacks) are final: average them over the ranks
+      CK(cudaEventRecord(T->dp->layer_done[l], e->stream));
+      for (const TrainLayer* tl : {&tp, &ts}) {
+        const long a = tl->qkv.offA[0], b = tl->dn.offB[0] + 16L * tl->dn.Fa[0];
+        if (!dp_average(e, T->dp, T->g + a, (size_t)(b - a), T->dp->layer_done[l])) return false;
+      }
+    }
   }
+  if (T->overlap && !dp_average(e, T->dp, T->d_loss, 1, nullptr)) return false;
   return true;
 }
 
 bool lora_accumulate(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* actions,
-                     const float* noise, const float* t) {
+                     const float* noise, const float* t, bool exchange = false) {
   Trainer* T = e->tr;
   const int H = e->cfg.horizon;
   const size_t ib = (size_t)e->cfg.n_cameras * P5_IMG * P5_IMG * 3;
-  T->n_total = n;
+  // the gradient buffer and the loss hold the mean over every sample accumulated since the last zero:
+  // re-weight what is there by c / (c + n), and let this call's samples add with weight 1 / (c + n)
+  const int c = T->n_seen;
+  if (c > 0) {
+    const float w = (float)c / (float)(c + n);
+    scale_f32_kernel<<<148 * 4, 256, 0, e->stream>>>(T->g, T->n_params, w);
+    scale_f32_kernel<<<1, 32, 0, e->stream>>>(T->d_loss, 1, w);
+    CK(cudaGetLastError());
+  }
+  T->n_total = c + n;
+  T->n_seen = c + n;
   for (int b0 = 0; b0 < n; b0 += T->mb) {
     const int nb = std::min(T->mb, n - b0);
     CK(cudaMemcpyAsync(e->A.images, images + b0 * ib, nb * ib, cudaMemcpyDefault, e->stream));
@@ -726,9 +751,25 @@ bool lora_accumulate(pi05_engine* e, int n, const uint8_t* images, const int32_t
     std::vector<float> th(nb);
     CK(cudaMemcpy(th.data(), t + b0, nb * 4, cudaMemcpyDefault));
     CK(cudaMemcpyAsync(T->d_t, th.data(), nb * 4, cudaMemcpyHostToDevice, e->stream));
-    if (!micro_step(e, nb, th.data())) return false;
+    // with `exchange`, the last micro-batch averages each finished layer over the ranks during its backward
+    T->overlap = exchange && T->dp && b0 + nb >= n;
+    const bool ok = micro_step(e, nb, th.data());
+    T->overlap = false;
+    if (!ok) return false;
   }
+  T->reduced = exchange && T->dp;
   return true;
+}
+
+// Gradients and loss averaged over the ranks (when attached) before the optimizer reads them.
+bool lora_exchange(pi05_engine* e) {
+  Trainer* T = e->tr;
+  if (!T->dp) return true;
+  if (!T->reduced && (!dp_average(e, T->dp, T->g, (size_t)T->n_params, nullptr) ||
+                      !dp_average(e, T->dp, T->d_loss, 1, nullptr)))
+    return false;
+  T->reduced = false;
+  return dp_join(e, T->dp);
 }
 
 bool lora_opt(pi05_engine* e) {
@@ -787,6 +828,7 @@ int pi05_lora_zero_grads(pi05_engine* e) {
   if (cudaMemsetAsync(e->tr->g, 0, e->tr->n_params * 4, e->stream) != cudaSuccess ||
       cudaMemsetAsync(e->tr->d_loss, 0, 4, e->stream) != cudaSuccess)
     return PI05_ERR_CUDA;
+  e->tr->n_seen = 0;
   return PI05_OK;
 }
 
@@ -806,7 +848,7 @@ int pi05_lora_accumulate(pi05_engine* e, int n, const uint8_t* images, const int
 int pi05_lora_opt_step(pi05_engine* e) {
   if (!e || !e->tr) return PI05_ERR_STATE;
   cudaSetDevice(e->device);
-  if (!lora_opt(e)) return fail_code(e);
+  if (!lora_exchange(e) || !lora_opt(e)) return fail_code(e);
   return PI05_OK;
 }
 
@@ -814,8 +856,10 @@ int pi05_lora_step(pi05_engine* e, int n, const uint8_t* images, const int32_t* 
                    const float* noise, const float* t, float* loss) {
   int rc = pi05_lora_zero_grads(e);
   if (rc != PI05_OK) return rc;
-  rc = pi05_lora_accumulate(e, n, images, tokens, actions, noise, t, nullptr);
-  if (rc != PI05_OK) return rc;
+  if (n < 1 || !images || !actions || !noise || !t || (e->cfg.n_text > 0 && !tokens)) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  // one accumulate pass whose backward averages each finished layer over the ranks (data parallelism)
+  if (!lora_accumulate(e, n, images, tokens, actions, noise, t, true)) return fail_code(e);
   rc = pi05_lora_opt_step(e);
   if (rc != PI05_OK) return rc;
   if (loss) {
@@ -914,5 +958,67 @@ int pi05_lora_load_state(pi05_engine* e, const char* path) {
   if (!scatter_all(e, T)) return fail_code(e);
   return pi05_sync(e);
 }
+
+
+int pi05_nccl_unique_id(void* id) {
+  if (!id) return PI05_ERR_ARG;
+  NcclApi& A = nccl_api();
+  if (!A.ok) return PI05_ERR_STATE;
+  ncclUniqueId u;
+  if (A.get_unique_id(&u) != ncclSuccess) return PI05_ERR_CUDA;
+  memcpy(id, &u, sizeof(u));
+  return PI05_OK;
+}
+
+int pi05_lora_attach_nccl(pi05_engine* e, const void* id, int rank, int world) {
+  if (!e) return PI05_ERR_ARG;
+  if (!e->tr) {
+    e->err = "pi05_lora_attach_nccl: call pi05_lora_init first";
+    return PI05_ERR_STATE;
+  }
+  if (!id || world < 1 || rank < 0 || rank >= world) {
+    e->err = "pi05_lora_attach_nccl: needs 0 <= rank < world and the 128-byte unique id";
+    return PI05_ERR_ARG;
+  }
+  if (e->tr->dp) {
+    e->err = "pi05_lora_attach_nccl: already attached";
+    return PI05_ERR_STATE;
+  }
+  NcclApi& A = nccl_api();
+  if (!A.ok) {
+    e->err = "pi05_lora_attach_nccl: " + A.why;
+    return PI05_ERR_STATE;
+  }
+  cudaSetDevice(e->device);
+  DpComm* d = new DpComm();
+  d->rank = rank;
+  d->world = world;
+  auto fail = [&](int code) {
+    if (d->comm) A.comm_abort(d->comm);
+    d->comm = nullptr;
+    dp_release(d);
+    return code;
+  };
+  if (cudaStreamCreateWithFlags(&d->cs, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&d->reduced, cudaEventDisableTiming) != cudaSuccess)
+    return fail(PI05_ERR_CUDA);
+  d->layer_done.assign(e->cfg.gemma_layers, nullptr);
+  for (cudaEvent_t& ev : d->layer_done)
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return fail(PI05_ERR_CUDA);
+  ncclUniqueId u;
+  memcpy(&u, id, sizeof(u));
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;  // init and collectives return at once; every wait on them is bounded (nccl_settle)
+  const ncclResult_t r = A.init_rank_config(&d->comm, world, u, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    e->err = std::string("ncclCommInitRankConfig: ") + A.error_string(r);
+    return fail(PI05_ERR_CUDA);
+  }
+  if (!nccl_settle(e, d->comm, "ncclCommInitRankConfig")) return fail(PI05_ERR_CUDA);
+  e->tr->dp = d;
+  return PI05_OK;
+}
+
+int pi05_lora_world(pi05_engine* e) { return (e && e->tr && e->tr->dp) ? e->tr->dp->world : 1; }
 
 }  // extern "C"

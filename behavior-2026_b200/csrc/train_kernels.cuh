@@ -330,6 +330,11 @@ __global__ void lora_frozen_copy_kernel(const bf16* W, int F, int K, bf16* Wf, i
   }
 }
 
+// x[i] *= s: re-weights a running mean when more samples join it
+__global__ void scale_f32_kernel(float* x, long n, float s) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) x[i] *= s;
+}
+
 // ---------------------------------------------------------------- optimizer
 // sum of squares of the gradient, deterministic two-level reduction
 __global__ void sumsq_partial_kernel(const float* g, long n, float* partial) {

@@ -1,12 +1,34 @@
-"""Data parallelism for the pi0.5 engine: batch sharding and the LoRA gradient allreduce.
+"""Data parallelism for the pi0.5 engine: batch sharding and the LoRA gradient exchange.
 
 The reference engine was single-GPU (docs/archive/windows/π05_네이티브엔진.md:464).  Here:
   * inference shards independent environments across ranks with no collective (`shard`);
-  * the LoRA step allreduces the flat fp32 adapter-gradient buffer (26.5 M floats at full depth)
-    between pi05_lora_accumulate and pi05_lora_opt_step, averaging over ranks (`allreduce_mean_`).
-One process per GPU; torch.distributed supplies the communicator (NCCL on GPUs, gloo on CPU).
+  * the LoRA step averages the flat fp32 adapter-gradient buffer (26.5 M floats at full depth) over
+    the ranks.  `attach_nccl` gives the engine its own NCCL communicator (pi05_lora_attach_nccl): the
+    engine then averages each layer's gradients during the backward pass, on its own stream, inside
+    pi05_lora_step.  torch.distributed only carries the 128-byte NCCL id from rank 0 to the others.
+    `lora_allreduce` is the host-ordered alternative through torch.distributed (any backend).
+One process per GPU.
 """
 import torch
+
+
+def exchange_unique_id(uid, rank):
+    """rank 0's 128-byte id to every rank over the default process group (any backend)"""
+    import torch.distributed as dist
+
+    box = [uid if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    return box[0]
+
+
+def attach_nccl(engine, rank, world):
+    """make `engine` (after lora_init) a member of a `world`-rank NCCL communicator; no-op for one rank"""
+    if world == 1:
+        return
+    import pi05native as pn
+
+    uid = exchange_unique_id(pn.nccl_unique_id() if rank == 0 else None, rank)
+    engine.lora_attach_nccl(uid, rank, world)
 
 
 def shard(n_global, world, rank):

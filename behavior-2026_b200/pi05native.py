@@ -24,6 +24,8 @@ EXPORTS = [
     "pi05_denoise", "pi05_infer", "pi05_stream", "pi05_sync", "pi05_prefix_len", "pi05_graph_launches",
     "pi05_synth_images", "pi05_synth_tokens", "pi05_synth_noise", "pi05_synth_prefix_cache", "pi05_create_batch",
     "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_resize_with_pad", "pi05_normalize", "pi05_discretize_state", "pi05_absolute_actions", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
+    "pi05_linear_static_status", "pi05_verify", "pi05_set_act_config", "pi05_act",
+    "pi05_nccl_unique_id", "pi05_lora_attach_nccl", "pi05_lora_world",
 ]
 
 
@@ -35,11 +37,13 @@ class Pi05Error(RuntimeError):
 
 class Config(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in
-                ("siglip_layers", "gemma_layers", "expert_layers", "num_steps", "n_cameras", "n_text", "horizon")]
+                ("siglip_layers", "gemma_layers", "expert_layers", "num_steps", "n_cameras", "n_text", "horizon",
+                 "batch_invariant")]
 
     @classmethod
-    def make(cls, siglip_layers=27, gemma_layers=18, num_steps=10, n_cameras=3, n_text=200, horizon=50):
-        return cls(siglip_layers, gemma_layers, gemma_layers, num_steps, n_cameras, n_text, horizon)
+    def make(cls, siglip_layers=27, gemma_layers=18, num_steps=10, n_cameras=3, n_text=200, horizon=50,
+             batch_invariant=0):
+        return cls(siglip_layers, gemma_layers, gemma_layers, num_steps, n_cameras, n_text, horizon, batch_invariant)
 
     @property
     def prefix_len(self):
@@ -49,10 +53,24 @@ class Config(ctypes.Structure):
         return {n: getattr(self, n) for n, _ in self._fields_}
 
 
+class Frame(ctypes.Structure):
+    """pi05_frame: one camera frame (RGB or RGBA, any size and row stride, host or device memory)"""
+    _fields_ = [("data", ctypes.c_void_p), ("height", ctypes.c_int32), ("width", ctypes.c_int32),
+                ("channels", ctypes.c_int32), ("stride", ctypes.c_int64)]
+
+
+class ActConfig(ctypes.Structure):
+    _fields_ = [("act_dim", ctypes.c_int32), ("replan", ctypes.c_int32), ("mean", ctypes.c_void_p),
+                ("std", ctypes.c_void_p), ("delta_mask", ctypes.c_void_p), ("noise_seed", ctypes.c_uint64)]
+
+
 class LoraConfig(ctypes.Structure):
     _fields_ = [("rank", ctypes.c_int32), ("alpha", ctypes.c_float), ("lr", ctypes.c_float), ("beta1", ctypes.c_float),
                 ("beta2", ctypes.c_float), ("eps", ctypes.c_float), ("weight_decay", ctypes.c_float),
                 ("clip_norm", ctypes.c_float), ("micro_batch", ctypes.c_int32)]
+
+
+PROBE = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float), ctypes.c_int64, ctypes.c_void_p)
 
 
 def _load():
@@ -93,7 +111,7 @@ def _load():
     L.pi05_create_batch.restype = vp
     L.pi05_infer_batch.argtypes = [vp, i32, vp, vp, vp, vp]
     L.pi05_set_stage.argtypes = [vp, i32, i32, i32]
-    L.pi05_act_batch.argtypes = [vp, i32, vp, vp, vp, vp, i32, i32, vp]
+    L.pi05_act_batch.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp]
     L.pi05_reset_slot.argtypes = [vp, i32]
     L.pi05_resize_with_pad.argtypes = [vp, i32, i32, i32, ctypes.c_long, vp, i32, i32]
     L.pi05_normalize.argtypes = [vp, i32, i32, vp, vp, i32, i32]
@@ -103,6 +121,7 @@ def _load():
     L.pi05_op_attention.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32]
     L.pi05_op_siglip_attention.argtypes = [vp, i32, vp, vp]
     L.pi05_linear_static.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_char_p, ctypes.c_size_t]
+    L.pi05_linear_static_status.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t]
     L.pi05_lora_default_config.argtypes = [P(LoraConfig)]
     L.pi05_lora_default_config.restype = None
     L.pi05_lora_init.argtypes = [vp, P(LoraConfig), u64]
@@ -119,6 +138,12 @@ def _load():
     L.pi05_lora_grad_buffer.restype = vp
     L.pi05_op_bench_linear.argtypes = [vp, i32, i32, i32, i32, i32, P(ctypes.c_float)]
     L.pi05_lora_reset_optimizer.argtypes = [vp]
+    L.pi05_verify.argtypes = [vp, vp, vp, vp, vp, PROBE, vp]
+    L.pi05_set_act_config.argtypes = [vp, P(ActConfig)]
+    L.pi05_nccl_unique_id.argtypes = [vp]
+    L.pi05_lora_attach_nccl.argtypes = [vp, vp, i32, i32]
+    L.pi05_lora_world.argtypes = [vp]
+    L.pi05_act.argtypes = [vp, i32, vp, vp, vp, vp, vp]
     L.pi05_lora_save_state.argtypes = [vp, ctypes.c_char_p]
     L.pi05_lora_load_state.argtypes = [vp, ctypes.c_char_p]
     return L
@@ -240,6 +265,25 @@ class Engine:
         self._check(lib.pi05_infer(self._h, n, pi, pt, pn, po))
         return out
 
+    def verify(self, images, tokens, noise, keep=None):
+        """Verify run of one observation (pi05_verify): returns (actions [horizon][32], {point name: fp32
+        array}) with the points whose names start with one of `keep` (all when None): img.*, txt.emb,
+        pre.l<N>.{norm1,k,v,norm2,out}, suf.s<S>.{in,l<N>.out,final,v,x}."""
+        points = {}
+
+        def on(name, data, n, _ctx):
+            name = name.decode()
+            if keep is None or any(name.startswith(k) for k in keep):
+                points[name] = np.ctypeslib.as_array(data, shape=(n,)).copy()
+
+        cb = PROBE(on)
+        out = np.empty((self.config.horizon, 32), np.float32)
+        pi, ki = _ptr(images, np.uint8)
+        pt, kt = _ptr(tokens, np.int32)
+        pn, kn = _ptr(noise, np.float32)
+        self._check(lib.pi05_verify(self._h, pi, pt, pn, out.ctypes.data, cb, None))
+        return out, points
+
     # -- hot operators on device tensors (asynchronous on the engine stream)
     EPI = {"store": 0, "gelu": 1, "resid": 2, "gated": 3, "geglu": 4, "f32": 5}
 
@@ -324,6 +368,15 @@ class Engine:
     def lora_grad_ptr(self):
         return lib.pi05_lora_grad_buffer(self._h)
 
+    def lora_attach_nccl(self, unique_id, rank, world):
+        """pi05_lora_attach_nccl: join the `world`-rank communicator of the 128-byte NCCL id"""
+        buf = ctypes.create_string_buffer(bytes(unique_id), 128)
+        self._check(lib.pi05_lora_attach_nccl(self._h, buf, rank, world))
+
+    @property
+    def lora_world(self):
+        return lib.pi05_lora_world(self._h)
+
     def lora_reset_optimizer(self):
         self._check(lib.pi05_lora_reset_optimizer(self._h))
 
@@ -340,23 +393,75 @@ class Engine:
     def set_stage(self, slot, stage, mode=1):
         self._check(lib.pi05_set_stage(self._h, slot, stage, mode))
 
-    def act_batch(self, slots, images, tokens, noise, replan=16, act_dim=23):
-        """Receding-horizon step of the environment slots `slots`: the next action row (first act_dim
-        entries) of each slot's chunk, re-planning (one batched infer) the slots whose chunk is empty or
-        has had `replan` rows executed.  images/tokens/noise: host arrays in the infer layout, one row
-        per listed slot.  Returns float32 [len(slots)][act_dim]."""
+    def set_act_config(self, act_dim=32, replan=16, mean=None, std=None, delta_mask=None, noise_seed=0):
+        """pi05_set_act_config: output transform (z-score un-normalise, delta -> absolute actions on the
+        dims of delta_mask, first act_dim dims) and re-plan period of act_batch / act."""
+        keep = [None if v is None else np.ascontiguousarray(v, dt) for v, dt in
+                ((mean, np.float32), (std, np.float32), (delta_mask, np.uint8))]
+        c = ActConfig(act_dim, replan, *[None if k is None else k.ctypes.data for k in keep], noise_seed)
+        self._check(lib.pi05_set_act_config(self._h, ctypes.byref(c)))
+        self.act_dim = act_dim
+
+    @staticmethod
+    def _frames(frames):
+        """[n][n_cameras] frames (uint8 [h][w][3 or 4] numpy arrays or CUDA tensors, any row stride) ->
+        (pi05_frame array, keep-alive list)"""
+        flat, keep = [], []
+        for row in frames:
+            for f in row:
+                if hasattr(f, "data_ptr"):  # torch tensor (host or CUDA), rows may be strided
+                    h, w, c = f.shape
+                    assert f.dtype.itemsize == 1 and f.stride(2) == 1 and f.stride(1) == c
+                    flat.append(Frame(f.data_ptr(), h, w, c, f.stride(0)))
+                else:
+                    a = np.asarray(f)
+                    if a.dtype != np.uint8 or a.strides[2] != 1 or a.strides[1] != a.shape[2]:
+                        a = np.ascontiguousarray(a, np.uint8)
+                    h, w, c = a.shape
+                    flat.append(Frame(a.ctypes.data, h, w, c, a.strides[0]))
+                keep.append(f if hasattr(f, "data_ptr") else a)
+        arr = (Frame * len(flat))(*flat)
+        return arr, keep
+
+    def act_batch(self, slots, frames, tokens, state=None, noise=None, out=None):
+        """pi05_act_batch: one receding-horizon step of the environment slots `slots`.  frames[i][c] is camera
+        c of slot slots[i] at any size (RGB or RGBA, host or CUDA); tokens int32 [n][n_text]; state f32
+        [n][act_dim] or None; noise f32 [n][horizon][32] or None (the slots' generator streams).  Returns
+        f32 [n][act_dim] (or fills `out`, host or CUDA)."""
         sl = np.ascontiguousarray(np.asarray(slots, dtype=np.int32))
         n = sl.shape[0]
-        out = np.empty((n, act_dim), np.float32)
-        pi, ki = _ptr(images, np.uint8)
+        fa, fk = self._frames(frames)
+        if out is None:
+            out = np.empty((n, getattr(self, "act_dim", 32)), np.float32)
         pt, kt = _ptr(tokens, np.int32)
-        pn, kn = _ptr(noise, np.float32)
+        ps, ks = _ptr(state, np.float32) if state is not None else (None, None)
+        pz, kz = _ptr(noise, np.float32) if noise is not None else (None, None)
         po, ko = _ptr(out, np.float32, writable=True)
-        self._check(lib.pi05_act_batch(self._h, n, sl.ctypes.data_as(ctypes.c_void_p), pi, pt, pn, replan, act_dim, po))
+        self._check(lib.pi05_act_batch(self._h, n, sl.ctypes.data_as(ctypes.c_void_p), fa, pt, ps, pz, po))
+        return out
+
+    def act(self, slot, frames, tokens, state=None, noise=None):
+        """pi05_act: act_batch for one slot; frames [n_cameras], tokens [n_text], state [act_dim],
+        noise [horizon][32] or None.  Returns f32 [act_dim]."""
+        fa, fk = self._frames([frames])
+        out = np.empty((getattr(self, "act_dim", 32),), np.float32)
+        pt, kt = _ptr(tokens, np.int32)
+        ps, ks = _ptr(state, np.float32) if state is not None else (None, None)
+        pz, kz = _ptr(noise, np.float32) if noise is not None else (None, None)
+        self._check(lib.pi05_act(self._h, slot, fa, pt, ps, pz, out.ctypes.data))
         return out
 
     def reset_slot(self, slot):
         self._check(lib.pi05_reset_slot(self._h, slot))
+
+
+def nccl_unique_id():
+    """pi05_nccl_unique_id: a new 128-byte NCCL id (rank 0 creates it and shares it with the others)"""
+    buf = ctypes.create_string_buffer(128)
+    rc = lib.pi05_nccl_unique_id(buf)
+    if rc != OK:
+        raise Pi05Error(rc, "pi05_nccl_unique_id: NCCL unavailable")
+    return buf.raw
 
 
 def resize_with_pad(image, out_h=224, out_w=224):
@@ -427,6 +532,15 @@ def linear_static(x, w, out, bias=None, stream=None):
     err = ctypes.create_string_buffer(512)
     p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
     rc = lib.pi05_linear_static(T, F, K, p(x), p(w), p(bias), p(out), ctypes.c_void_p(stream or 0), err, len(err))
+    if rc != OK:
+        raise Pi05Error(rc, err.value.decode())
+
+
+def linear_static_status(stream=None):
+    """pi05_linear_static_status: waits for `stream`; raises Pi05Error(ERR_DEVICE) if a
+    pi05_linear_static call on the current device had a device-side wait give up."""
+    err = ctypes.create_string_buffer(512)
+    rc = lib.pi05_linear_static_status(ctypes.c_void_p(stream or 0), err, len(err))
     if rc != OK:
         raise Pi05Error(rc, err.value.decode())
 

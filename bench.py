@@ -504,17 +504,16 @@ def run_lora(args, world, rank, local):
     eng = pn.Engine(pn.Config.make(), device=local, max_batch=mb)
     eng.init_random_weights(args.seed)
     eng.lora_init(seed=args.seed + 1, micro_batch=mb)
+    dp.attach_nccl(eng, rank, world)  # the engine's own communicator: per-layer averages during backward
     first, _ = dp.shard(nb * world, world, rank)
     imgs, toks, acts, noise, t = lora_inputs(pn, nb, first, args.seed)
     dev = [torch.from_numpy(a).cuda() for a in (imgs, toks, acts, noise, t)]
     host = [torch.from_numpy(a).pin_memory() for a in (imgs, toks, acts, noise, t)]
 
     def step(bufs):
-        eng.lora_zero_grads()
-        loss = eng.lora_accumulate(*bufs)
-        dp.lora_allreduce(eng, world)
-        eng.lora_opt_step()
-        return loss
+        # zero + forward/backward (each finished layer's gradients averaged over the ranks on the engine's
+        # communication stream) + clip/AdamW; the loss is read back to the host
+        return eng.lora_step(*bufs)
 
     for _ in range(args.warmup):
         step(dev)
@@ -539,7 +538,8 @@ def run_lora(args, world, rank, local):
             "scaling": "weak", "dtype": "bf16", "data": "synthetic", "vs_baseline": None, "loss": loss,
             "config": {"workload": f"LoRA step (rank 16, alpha 32, q/k/v/o/gate/up/down of Gemma-2B and the expert): "
                                    f"{nb} samples per GPU, micro-batch {mb}, flow-matching loss, "
-                                   f"AdamW lr 1e-4" + (", NCCL gradient allreduce" if world > 1 else ""),
+                                   f"AdamW lr 1e-4" + (", NCCL gradient average per layer, overlapped with the "
+                                                       f"backward pass" if world > 1 else ""),
                        "model": MODEL, "global_batch": samples, "per_gpu_batch": nb, "parallelism": f"dp{world}",
                        "l2": "no flush: every step streams GBs of weights and saved activations (> 126 MB L2)"},
             "e2e": {"value": samples * args.steps / (total_e2e / 1e3), "unit": "samples/s",

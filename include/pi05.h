@@ -14,7 +14,7 @@
  * (pi05_stream) and pi05_sync waits for it.  Calls on one engine are not re-entrant.
  *
  * Shapes (n = batch of independent observations, n <= max_batch):
- *   images   uint8 [n][n_cameras][224][224][3]  (RGB, 224x224 already; resize is out of scope)
+ *   images   uint8 [n][n_cameras][224][224][3]  (RGB 224x224; pi05_act_batch takes camera frames of any size)
  *   tokens   int32 [n][n_text]                  (ids < 257152)
  *   noise    fp32  [n][horizon][32]             (flow-matching start x_1)
  *   actions  fp32  [n][horizon][32]             (x_0 after num_steps Euler steps)
@@ -52,6 +52,12 @@ typedef struct {
   int32_t n_cameras;       /* 3 */
   int32_t n_text;          /* 200 prompt tokens */
   int32_t horizon;         /* 50 actions per chunk */
+  /* 1: every sample of a batch is computed exactly as a batch of one (at its own offsets, one
+   * single-sample CUDA graph per batch position), so results are bit-identical for any batch size and
+   * position, as the reference's batch path was (π05_네이티브엔진.md:299-302), at about the bs1 throughput.
+   * 0 (default): batches run as one GEMM/attention problem each, for throughput; per-sample results
+   * then differ from the batch-of-one results in the last bits (different tilings and sum orders). */
+  int32_t batch_invariant;
 } pi05_config;
 
 PI05_API void pi05_default_config(pi05_config* c);
@@ -81,6 +87,21 @@ PI05_API int pi05_denoise(pi05_engine* e, int n, const float* noise, float* acti
 /* prefill + denoise (replaces pi05_infer_batch, π05_네이티브엔진.md:292). */
 PI05_API int pi05_infer(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* noise,
                float* actions);
+
+/* Verify run (replaces the reference's layer-by-layer verifier tools/verify.cpp, π05_네이티브엔진.md:53-63,
+ * whose point names it keeps): one observation (batch 1) through the same kernels as pi05_infer,
+ * launched one by one instead of from the CUDA graph, with each named intermediate point copied to
+ * the host as fp32 and passed to `fn` in network order:
+ *   img.stem, img.l<N>.out, img.encoded, img.tokens        [256*n_cameras][1152 or 2048]
+ *   txt.emb                                                [n_text][2048]
+ *   pre.l<N>.norm1, .k, .v, .norm2, .out                   [P][2048] or [P][256] (the last layer: norm1, k, v)
+ *   suf.s<S>.in, .l<N>.out, .final                         [horizon][1024]
+ *   suf.s<S>.v, .x                                         [horizon][32] (velocity, flow state after step S)
+ * `data` is valid during the callback only.  `actions` (optional) receives the chunk, the same values
+ * pi05_infer returns for this observation.  Inputs may be host or device pointers. */
+typedef void (*pi05_probe_fn)(const char* name, const float* data, int64_t n, void* ctx);
+PI05_API int pi05_verify(pi05_engine* e, const uint8_t* images, const int32_t* tokens, const float* noise,
+                         float* actions, pi05_probe_fn fn, void* ctx);
 
 /* Stream and synchronisation. */
 PI05_API void* pi05_stream(pi05_engine* e);  /* cudaStream_t of the engine */
@@ -120,7 +141,9 @@ PI05_API void pi05_lora_default_config(pi05_lora_config* c);
 PI05_API int pi05_lora_init(pi05_engine* e, const pi05_lora_config* c, uint64_t seed);
 PI05_API long pi05_lora_num_params(pi05_engine* e);
 PI05_API int pi05_lora_zero_grads(pi05_engine* e);
-/* forward + backward over n samples, gradients added to the flat buffer (LoraTrainer::accumulate);
+/* forward + backward over n samples into the flat gradient buffer (LoraTrainer::accumulate), which holds
+ * the mean gradient over every sample accumulated since the last pi05_lora_zero_grads (calls of 8 + 8
+ * samples give what one call of 16 gives, up to fp32 rounding);
  * images u8 [n][cams][224][224][3], tokens i32 [n][n_text], actions/noise f32 [n][horizon][32], t f32 [n];
  * *loss (optional) = mean squared velocity error over the samples accumulated since the last zero. */
 PI05_API int pi05_lora_accumulate(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens,
@@ -131,6 +154,19 @@ PI05_API int pi05_lora_opt_step(pi05_engine* e);
 /* zero_grads + accumulate + opt_step */
 PI05_API int pi05_lora_step(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* actions,
                             const float* noise, const float* t, float* loss);
+/* Data parallelism over NCCL (the LoRA step's exchange: the adapter gradients, and the loss, averaged over
+ * the ranks before the identical clip + AdamW on every rank; the reference trained on one GPU,
+ * π05_네이티브엔진.md:464).  Rank 0 writes the 128-byte ncclUniqueId with pi05_nccl_unique_id and shares it
+ * with the other ranks by any host channel; each rank then attaches its engine (one GPU per rank) after
+ * pi05_lora_init.  Once attached, pi05_lora_step averages each layer's gradients on a communication
+ * stream as soon as its backward pass has finished that layer (no host synchronisation), and
+ * pi05_lora_opt_step averages the whole buffer first when the gradients came from pi05_lora_accumulate
+ * calls.  Every rank takes the same calls in the same order.  NCCL is loaded at run time (libnccl.so.2,
+ * the process's own copy when a framework has loaded one); waits on the communicator are bounded by
+ * PI05_NCCL_TIMEOUT_S seconds (default 120).  pi05_lora_world: ranks of the attached communicator (1). */
+PI05_API int pi05_nccl_unique_id(void* id);
+PI05_API int pi05_lora_attach_nccl(pi05_engine* e, const void* id, int rank, int world);
+PI05_API int pi05_lora_world(pi05_engine* e);
 PI05_API int pi05_lora_get_params(pi05_engine* e, float* out);
 PI05_API int pi05_lora_set_params(pi05_engine* e, const float* in);
 PI05_API int pi05_lora_get_grads(pi05_engine* e, float* out);
@@ -169,12 +205,18 @@ PI05_API int pi05_op_bench_linear(pi05_engine* e, int T, int F, int K, int epi, 
  * must not allocate after start-up).  Its split-K scratch is one file-scope device array of
  * 16 MiB that every GPU loading this library holds until exit.  Limits: 1 <= T <= 64,
  * 1 <= F <= 65536, 8 <= K <= 65536, K % 8 == 0; other sizes return PI05_ERR_ARG with a message in err.
+ * x, w and out are 16-byte aligned device pointers, bias a device pointer or NULL.
  * The first call on a device sets that device up (looks up the array's address) and should come
  * before any stream capture.  All calls share the array: calls that overlap on the GPU race.
- * Asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream); x, w, bias, out are device
- * pointers.  No counterpart in the reference's ABI. */
+ * Asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream).  The kernel's waits are
+ * bounded; one that gives up leaves that call's output incomplete and makes later calls skip their
+ * work until pi05_linear_static_status reports it.  No counterpart in the reference's ABI. */
 PI05_API int pi05_linear_static(int T, int F, int K, const void* x, const void* w, const void* bias, void* out,
                                 void* stream, char* err, size_t err_len);
+/* Waits for `stream`, then reports (PI05_ERR_DEVICE, message in err) and clears a bounded-wait
+ * give-up recorded by pi05_linear_static calls on the current device; PI05_OK when there was none.
+ * No counterpart in the reference's ABI. */
+PI05_API int pi05_linear_static_status(void* stream, char* err, size_t err_len);
 
 /* Reference batch-API names (π05_네이티브엔진.md:288-303). */
 PI05_API pi05_engine* pi05_create_batch(const char* weights_path, int device, int max_batch);
@@ -182,14 +224,44 @@ PI05_API int pi05_infer_batch(pi05_engine* e, int n, const uint8_t* images, cons
                      float* actions);
 /* PiBehavior stage channel; plain pi0.5 has no stage head, so this only validates its arguments. */
 PI05_API int pi05_set_stage(pi05_engine* e, int slot, int stage, int mode);
-/* Receding-horizon stepping (reference pi05_act_batch, π05_네이티브엔진.md:292-296, :33): environment slot
- * slots[i] keeps the last 50x32 chunk it was given; each call writes, for every listed slot, the next
- * row of that chunk (its first act_dim entries) to out[i][act_dim], and first runs one batched
- * pi05_infer for the listed slots that have no chunk or have executed `replan` rows of it (their
- * images, tokens and noise are row i of the pi05_infer-layout host inputs; rows of other slots are not
- * read).  Host buffers; images are the 224x224 RGB camera frames pi05_infer takes. */
-PI05_API int pi05_act_batch(pi05_engine* e, int n, const int* slots, const uint8_t* images, const int32_t* tokens,
-                            const float* noise, int replan, int act_dim, float* out);
+/* Receding-horizon stepping (reference pi05_act_batch / pi05_act, π05_네이티브엔진.md:292-297, :33, :303).
+ * A camera frame as the evaluator passes it: RGB or RGBA (alpha ignored) at any resolution, rows `stride`
+ * bytes apart, in host memory or device memory of the engine's device.  Frames that are not 224x224 are
+ * resized with padding on the GPU (resize_with_pad: the pi05_resize_with_pad arithmetic, bit for bit). */
+typedef struct {
+  const void* data;
+  int32_t height, width;
+  int32_t channels; /* 3 = RGB, 4 = RGBA */
+  int64_t stride;   /* bytes from one row to the next, >= width * channels */
+} pi05_frame;
+/* Output transform and re-plan period of pi05_act_batch (the wrapper's, π05_네이티브엔진.md:32-35, :293-295):
+ * each new chunk is un-normalised a = a * (std + 1e-6) + mean (openpi Unnormalize, z-score; mean/std NULL:
+ * none), the state is added to the dims that delta_mask marks (openpi AbsoluteActions; NULL: none), and
+ * the first act_dim dims are kept.  A slot re-plans when it has no chunk or has executed `replan` rows.
+ * Noise, when the caller passes none, comes from the slot's own generator stream: re-plan p of slot s
+ * draws elements [p, p+1) * horizon*32 of the stream (noise_seed, noise, s), so its first re-plan uses
+ * pi05_synth_noise(noise_seed, s).  Setting the configuration forgets every slot's chunk.
+ * Defaults: act_dim 32, replan 16, no transforms, noise_seed 0. */
+typedef struct {
+  int32_t act_dim;
+  int32_t replan;
+  const float* mean;          /* [act_dim] or NULL */
+  const float* std;           /* [act_dim] or NULL */
+  const uint8_t* delta_mask;  /* [act_dim] or NULL */
+  uint64_t noise_seed;
+} pi05_act_config;
+PI05_API int pi05_set_act_config(pi05_engine* e, const pi05_act_config* c);
+/* One environment step of the n slots slots[i] (each at most once per call): writes the slot's next
+ * action row to out[i][act_dim] (f32, host or device), after one batched inference for the listed slots
+ * that re-plan.  frames [n][n_cameras] (frames[i * n_cameras + c]); tokens int32 [n][n_text]; state f32
+ * [n][act_dim] (read for the delta dims; may be NULL without a delta mask); noise f32 [n][horizon][32]
+ * or NULL (the slots' generator streams).  Host or device pointers.  With batch_invariant = 1 the result
+ * is bit-identical to stepping each slot alone with pi05_act. */
+PI05_API int pi05_act_batch(pi05_engine* e, int n, const int* slots, const pi05_frame* frames, const int32_t* tokens,
+                            const float* state, const float* noise, float* out);
+/* pi05_act_batch for one slot (the reference's single-slot pi05_act). */
+PI05_API int pi05_act(pi05_engine* e, int slot, const pi05_frame* frames, const int32_t* tokens, const float* state,
+                      const float* noise, float* out);
 /* Forget a slot's chunk (reference reset(eng, slot)): its next pi05_act_batch step re-plans. */
 PI05_API int pi05_reset_slot(pi05_engine* e, int slot);
 /* Camera-frame preprocessing on the host (reference resize_with_pad, π05_네이티브엔진.md:296-297, after

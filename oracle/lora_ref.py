@@ -26,7 +26,7 @@ QD, HD = 2048, 256
 
 def R(x):
     """round to bf16, gradient passes straight through"""
-    return x + (x.to(torch.bfloat16).float() - x).detach()
+    return x + (x.to(torch.bfloat16).to(x.dtype) - x).detach()
 
 
 def rope_table(npos):
@@ -57,12 +57,15 @@ def lora_layout(L, gem_w=2048, exp_w=1024, gem_mlp=16384, exp_mlp=4096):
 
 
 class LoraRef:
-    def __init__(self, cfg, seed, flat_params):
+    def __init__(self, cfg, seed, flat_params, dtype=torch.float32):
+        """dtype float64 gives a second computation of the same bf16-rounded network whose distance from
+        the float32 one measures the floating-point floor of these comparisons"""
         torch.set_num_threads(max(1, torch.get_num_threads()))
         self.cfg = cfg
         self.seed = seed
+        self.dtype = dtype
         self.L = cfg.gemma_layers
-        P = lambda kind, sub, shape: torch.from_numpy(O.gen_param(seed, kind, sub, shape))
+        P = lambda kind, sub, shape: torch.from_numpy(O.gen_param(seed, kind, sub, shape)).to(dtype)
         self.g, self.e = [], []
         for l in range(self.L):
             self.g.append(dict(rms1=P(GEM_RMS1, l, (2048,)), rms2=P(GEM_RMS2, l, (2048,)), q=P(GEM_WQ, l, (QD, 2048)),
@@ -91,7 +94,7 @@ class LoraRef:
         flat = np.asarray(flat_params, np.float32)
         for name, shape in self.layout:
             n = shape[0] * shape[1]
-            self.params[name] = torch.tensor(flat[off:off + n].reshape(shape), requires_grad=True)
+            self.params[name] = torch.tensor(flat[off:off + n].reshape(shape), dtype=dtype, requires_grad=True)
             off += n
         assert off == flat.size, (off, flat.size)
 
@@ -132,7 +135,7 @@ class LoraRef:
         return q, k, v
 
     def mods(self, t):
-        emb = torch.from_numpy(np.stack([time_embedding(tb) for tb in t]))
+        emb = torch.from_numpy(np.stack([time_embedding(tb) for tb in t])).to(self.dtype)
         c1 = emb @ self.tin_w.t() + self.tin_b
         c1 = c1 * torch.sigmoid(c1)
         c2 = c1 @ self.tout_w.t() + self.tout_b
@@ -142,22 +145,24 @@ class LoraRef:
 
     # ---- the loss
     def loss(self, prefix_emb, actions, noise, t):
-        a = torch.from_numpy(np.asarray(actions, np.float32))
-        eps = torch.from_numpy(np.asarray(noise, np.float32))
-        tt = torch.from_numpy(np.asarray(t, np.float32))[:, None, None]
+        a = torch.from_numpy(np.asarray(actions, np.float32)).to(self.dtype)
+        eps = torch.from_numpy(np.asarray(noise, np.float32)).to(self.dtype)
+        tt = torch.from_numpy(np.asarray(t, np.float32)).to(self.dtype)[:, None, None]
         xt = tt * eps + (1 - tt) * a
         u = eps - a
         v = self.velocity(prefix_emb, xt, t)
         return ((v - u) ** 2).mean()
 
-    def velocity(self, prefix_emb, xt, t):
-        """v = net(x_t, t, prefix) for a batch: prefix_emb [nb][P][2048], xt [nb][H][32] (tensor), t [nb]"""
+    def velocity(self, prefix_emb, xt, t, points=None):
+        """v = net(x_t, t, prefix) for a batch: prefix_emb [nb][P][2048], xt [nb][H][32] (tensor), t [nb].
+        `points` (a dict) receives the prefix K/V cache of sample 0 per layer, pre.l<N>.k / .v."""
         nb, P, _ = prefix_emb.shape
         H = xt.shape[1]
-        xp = torch.from_numpy(np.ascontiguousarray(prefix_emb, np.float32))
-        xs = R(xt @ self.ain_w.t() + self.ain_b)
+        xp = torch.from_numpy(np.ascontiguousarray(prefix_emb, np.float32)).to(self.dtype)
+        xs = R(xt.to(self.dtype) @ self.ain_w.t() + self.ain_b)
         md = self.mods(t)
         cos, sin = rope_table(P + H)
+        cos, sin = cos.to(self.dtype), sin.to(self.dtype)
         cp, sp = cos[:P], sin[:P]
         cs, ss = cos[P:P + H], sin[P:P + H]
         for l in range(self.L):
@@ -166,6 +171,9 @@ class LoraRef:
             m1, m2 = md[:, 2 * l], md[:, 2 * l + 1]
             h1 = self.rms(xp, g["rms1"])
             qp, kp, vp = self.qkv(h1, g, "gem", l, cp, sp)
+            if points is not None:
+                points[f"pre.l{l}.k"] = kp[0].detach().double().numpy().ravel()
+                points[f"pre.l{l}.v"] = vp[0].detach().double().numpy().ravel()
             h1s = self.rms(xs, m1[:, None, :1024], m1[:, None, 1024:2048])
             qs, ks, vs = self.qkv(h1s, e, "exp", l, cs, ss)
             os_ = self.attend(qs, torch.cat([kp, ks], 1), torch.cat([vp, vs], 1))
@@ -192,7 +200,7 @@ class LoraRef:
         out = []
         for n, shape in self.layout:
             g = self.params[n].grad
-            out.append(np.zeros(shape[0] * shape[1], np.float32) if g is None else g.numpy().ravel())
+            out.append(np.zeros(shape[0] * shape[1], np.float32) if g is None else g.double().numpy().ravel())
         return np.concatenate(out)
 
     def named_slices(self):

@@ -1,5 +1,6 @@
-"""Host-side multi-rank logic on CPU with gloo ranks (world size 2): batch sharding and the gradient
-average that the LoRA step applies between accumulate and the optimizer step."""
+"""Host-side multi-rank logic on CPU with gloo ranks (world size 2): batch sharding, the gradient
+average that the LoRA step applies between accumulate and the optimizer step, and the hand-over of the
+NCCL id with which every rank attaches its engine's own communicator."""
 import os
 import socket
 
@@ -28,7 +29,10 @@ def _worker(rank, world, port, q):
         # each rank's "gradient" = its rank-specific contribution; the average is known in closed form
         g = torch.arange(10, dtype=torch.float32) * (rank + 1)
         dp.allreduce_mean_(g, world)
-        q.put((rank, first, count, g.tolist()))
+        # the NCCL id of the engine's communicator travels from rank 0 over the process group
+        import pi05native as pn
+        uid = dp.exchange_unique_id(pn.nccl_unique_id() if rank == 0 else None, rank)
+        q.put((rank, first, count, g.tolist(), uid))
     finally:
         dist.destroy_process_group()
 
@@ -44,8 +48,9 @@ def test_shard_and_gradient_average_over_two_gloo_ranks():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    (r0, f0, c0, g0), (r1, f1, c1, g1) = out
+    (r0, f0, c0, g0, u0), (r1, f1, c1, g1, u1) = out
     assert (f0, c0, f1, c1) == (0, 32, 32, 32)
+    assert isinstance(u0, bytes) and len(u0) == 128 and u0 == u1
     expect = [i * 1.5 for i in range(10)]  # mean of i*1 and i*2
     assert g0 == pytest.approx(expect) and g1 == pytest.approx(expect)
 

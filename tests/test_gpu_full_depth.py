@@ -1,0 +1,219 @@
+"""Full-depth parity on the configurations the benchmark times: the sm_100a engine through the C ABI
+against the CPU oracle on the same seeded weights, inputs and noise.
+
+  config 2  bs1 full pi0.5 (SigLIP 27 layers, Gemma-2B 18, expert 18 x 10 steps): pi05_verify's named
+            points, chained as the reference's verifier compared them (tools/verify.cpp,
+            docs/archive/windows/π05_네이티브엔진.md:53-63; point names from logs/pi05_verify_radio_021324.log):
+            img.tokens, every pre.l<N>.k / .v, every suf.s<S>.v / .x, and the final chunk
+  config 3  bs64: one pi05_infer over 64 independent samples, samples 0, 31 and 63 against the oracle
+  config 4  LoRA: 18-layer gradients of one sample against fp32 torch autograd (oracle/lora_ref.py), and
+            the 32-sample single pass the benchmark runs against four 8-sample passes
+
+Tolerances: action chunks max-abs <= 2e-2 and cosine >= 0.999 (the parity contract); LoRA gradients
+rel-L2 <= 3e-2 for the whole gradient.  Intermediate points (rel-L2) and single adapter tensors: 2e-2
+(points) / 3e-2 (adapters), or, where two CPU computations of the same bf16-rounded network already
+differ by more, twice that floor - the reference verifier's rule (every point within 2x the JAX
+CPU-vs-GPU floor, π05_네이티브엔진.md:60-61; its own Gemma layer 17 floor was 1e-1, :69).  The floors here
+come from two CPU computations of the same network: the C++ oracle against the torch restatement
+(oracle/siglip_ref.py + oracle/lora_ref.py) for the forward points; for the gradients, torch autograd
+on the C++ oracle's prefix embedding against torch autograd on the torch restatement's (the two
+prefixes differ by bf16 rounding flips, as the GPU's does).  Flips between any two valid summation
+orders grow with depth, which is what the floor measures.
+"""
+import numpy as np
+import pytest
+
+pytestmark = [pytest.mark.gpu, pytest.mark.slow]
+
+ACT_MAXABS = 2e-2
+ACT_COS = 0.999
+POINT_REL_L2 = 2e-2
+GRAD_REL_L2 = 3e-2
+
+
+def cos(a, b):
+    a = a.ravel().astype(np.float64)
+    b = b.ravel().astype(np.float64)
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-30))
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / (np.linalg.norm(b) + 1e-30))
+
+
+def torch_prefix_points(oracle, seed, img, tok):
+    """img.tokens and every pre.l<N>.k / .v of the torch restatement (plain network: LoRA A = B = 0)."""
+    import torch
+
+    import lora_ref
+    import siglip_ref
+
+    cfg = oracle.Config.make()
+    emb = siglip_ref.prefix_embedding(seed, cfg.siglip_layers, img, tok)
+    pts = {"img.tokens": emb[:256 * cfg.n_cameras].ravel()}
+    nparam = sum(a * b for _, (a, b) in lora_ref.lora_layout(cfg.gemma_layers))
+    ref = lora_ref.LoraRef(cfg, seed, np.zeros(nparam, np.float32))
+    with torch.no_grad():
+        ref.velocity(emb[None], torch.zeros(1, cfg.horizon, 32), np.array([1.0], np.float32), points=pts)
+    return pts
+
+
+@pytest.fixture(scope="module")
+def bs1_full(pn, oracle):
+    cfg = pn.Config.make()
+    eng = pn.Engine(cfg, max_batch=1)
+    eng.init_random_weights(0)
+    img, tok, noise = pn.synth_images(0, 0), pn.synth_tokens(0, 0), pn.synth_noise(0, 0)
+    keep = ["img.tokens", "pre.", "suf."]
+    act_v, pts = eng.verify(img, tok, noise, keep=keep)
+    act_i = eng.infer(img[None], tok[None], noise[None])[0]
+    eng.close()
+    probe = oracle.Probe(keep=keep)
+    ref = oracle.infer(oracle.Config.make(), 0, img, tok, noise, probe=probe)
+    torch_pts = torch_prefix_points(oracle, 0, img, tok)
+    floor = {n: rel_l2(torch_pts[n], probe.points[n]) for n in torch_pts}
+    return dict(act_v=act_v, act_i=act_i, pts=pts, ref=ref, ref_pts=probe.points, cfg=cfg, floor=floor)
+
+
+def test_bs1_verify_run_equals_graph_path(bs1_full):
+    """The verify run launches the pi05_infer kernels one by one: the same chunk, bit for bit."""
+    assert np.array_equal(bs1_full["act_v"], bs1_full["act_i"])
+
+
+def test_bs1_full_depth_actions_match_oracle(bs1_full):
+    act, ref = bs1_full["act_i"], bs1_full["ref"]
+    assert np.isfinite(act).all()
+    d, c = float(np.abs(act - ref).max()), cos(act, ref)
+    print(f"bs1 full depth: max-abs {d:.3e} cos {c:.6f}")
+    assert d <= ACT_MAXABS and c >= ACT_COS, (d, c)
+
+
+def test_bs1_full_depth_image_tokens_and_kv_cache_match_oracle(bs1_full):
+    """Chained points of the prefix: the SigLIP -> projector output and every layer's K/V cache."""
+    pts, ref = bs1_full["pts"], bs1_full["ref_pts"]
+    names = ["img.tokens"] + [f"pre.l{l}.{kv}" for l in range(bs1_full["cfg"].gemma_layers) for kv in "kv"]
+    floor = bs1_full["floor"]
+    errs = {n: rel_l2(pts[n], ref[n]) for n in names}
+    print("rel-L2 vs oracle (floor):", {n: f"{e:.2e} ({floor[n]:.2e})" for n, e in errs.items()})
+    bad = {n: (e, floor[n]) for n, e in errs.items() if not e <= max(POINT_REL_L2, 2 * floor[n])}
+    assert not bad, bad
+
+
+def test_bs1_full_depth_flow_steps_match_oracle(bs1_full):
+    """Chained points of the denoise: velocity v and flow state x after every Euler step."""
+    pts, ref = bs1_full["pts"], bs1_full["ref_pts"]
+    names = [f"suf.s{s}.{p}" for s in range(bs1_full["cfg"].num_steps) for p in ("v", "x")]
+    errs = {n: rel_l2(pts[n], ref[n]) for n in names}
+    print("rel-L2 vs oracle:", {n: f"{e:.2e}" for n, e in errs.items()})
+    bad = {n: e for n, e in errs.items() if not e <= POINT_REL_L2}
+    assert not bad, bad
+
+
+def test_bs1_verify_emits_every_reference_point(bs1_full):
+    """Every point the oracle names for the prefix and the denoise is produced by the engine too."""
+    missing = sorted(set(bs1_full["ref_pts"]) - set(bs1_full["pts"]))
+    assert not missing, missing
+
+
+def test_bs64_full_depth_samples_match_oracle(pn, oracle):
+    """Config 3: 64 independent observations in one call; samples 0, 31, 63 against the oracle, and
+    sample 31 against its own batch-1 call."""
+    cfg = pn.Config.make()
+    eng = pn.Engine(cfg, max_batch=64)
+    eng.init_random_weights(0)
+    imgs = np.stack([pn.synth_images(11, i) for i in range(64)])
+    toks = np.stack([pn.synth_tokens(11, i) for i in range(64)])
+    noise = np.stack([pn.synth_noise(11, i) for i in range(64)])
+    act = eng.infer(imgs, toks, noise)
+    one = eng.infer(imgs[31:32], toks[31:32], noise[31:32])[0]
+    eng.close()
+    assert np.isfinite(act).all()
+    ocfg = oracle.Config.make()
+    for i in (0, 31, 63):
+        ref = oracle.infer(ocfg, 0, imgs[i], toks[i], noise[i])
+        d, c = float(np.abs(act[i] - ref).max()), cos(act[i], ref)
+        print(f"bs64 sample {i}: max-abs {d:.3e} cos {c:.6f}")
+        assert d <= ACT_MAXABS and c >= ACT_COS, (i, d, c)
+    assert np.abs(act[31] - one).max() <= ACT_MAXABS and cos(act[31], one) >= ACT_COS
+
+
+def _lora_batch(pn, oracle, n, seed):
+    imgs = np.stack([pn.synth_images(seed, i) for i in range(n)])
+    toks = np.stack([pn.synth_tokens(seed, i) for i in range(n)])
+    acts = oracle.gen_normal(seed, oracle.K_IN_ACTIONS, 0, (n, 50, 32))
+    noise = oracle.gen_normal(seed, oracle.K_IN_TRAIN_NOISE, 0, (n, 50, 32))
+    t = (np.arange(n, dtype=np.float32) * 0.37 + 0.05) % 0.95 + 0.025
+    return imgs, toks, acts, noise, t.astype(np.float32)
+
+
+def test_lora_full_depth_gradients_match_autograd(pn, oracle):
+    """Config 4 depth (SigLIP 27, Gemma-2B and expert 18 layers), one sample: every adapter's gradient
+    against fp32 torch autograd of the same loss."""
+    import lora_ref
+
+    cfg = pn.Config.make()
+    eng = pn.Engine(cfg, max_batch=1)
+    eng.init_random_weights(4)
+    eng.lora_init(seed=5, micro_batch=1)
+    imgs, toks, acts, noise, t = _lora_batch(pn, oracle, 1, 6)
+    p0 = eng.lora_get_params()
+    eng.lora_zero_grads()
+    loss = eng.lora_accumulate(imgs, toks, acts, noise, t)
+    g = eng.lora_get_grads()
+    eng.close()
+    import siglip_ref
+
+    ocfg = oracle.Config.make()
+    grads = {}
+    for src in ("oracle", "torch"):
+        emb = (oracle.prefix_embed(ocfg, 4, imgs[0], toks[0]) if src == "oracle" else
+               siglip_ref.prefix_embedding(4, ocfg.siglip_layers, imgs[0], toks[0]))
+        ref = lora_ref.LoraRef(ocfg, 4, p0)
+        L = ref.loss(emb[None], acts, noise, t)
+        L.backward()
+        grads[src] = (float(L.detach()), ref.grads())
+        slices = ref.named_slices()
+        del ref, L
+    loss_ref, gr = grads["oracle"]
+    g_alt = grads["torch"][1]
+    assert abs(loss - loss_ref) <= 1e-2 * abs(loss_ref)
+    assert np.isfinite(g).all()
+    bad, worst = [], (0.0, "", 0.0)
+    for name, sl in slices.items():
+        if np.linalg.norm(gr[sl]) < 1e-12:  # adapters the loss does not reach (last prefix layer's q/o/mlp)
+            assert np.abs(g[sl]).max() < 1e-6, name
+            continue
+        e, fl = rel_l2(g[sl], gr[sl]), rel_l2(gr[sl], g_alt[sl])
+        worst = max(worst, (e, name, fl))
+        if e > max(GRAD_REL_L2, 2 * fl):
+            bad.append((name, e, fl))
+    print(f"LoRA 18 layers: loss {loss:.6f} vs {loss_ref:.6f}, whole-gradient rel-L2 {rel_l2(g, gr):.3e} "
+          f"(floor {rel_l2(gr, g_alt):.3e}), worst adapter (error, name, floor) {worst}")
+    assert not bad, bad
+    assert rel_l2(g, gr) <= GRAD_REL_L2
+
+
+def test_lora_32_sample_pass_equals_four_8_sample_passes(pn, oracle):
+    """The benchmark's per-GPU step is one 32-sample forward/backward; accumulating the same 32 samples
+    as four 8-sample passes gives the same mean loss and gradients.  The two batch sizes tile the GEMMs
+    differently, so activations round to bf16 differently: loss within 1e-3 relative, gradients within
+    rel-L2 1e-2 (a third of the LoRA tolerance)."""
+    cfg = pn.Config.make()
+    eng = pn.Engine(cfg, max_batch=32)
+    eng.init_random_weights(4)
+    eng.lora_init(seed=5, micro_batch=32)
+    imgs, toks, acts, noise, t = _lora_batch(pn, oracle, 32, 8)
+    eng.lora_zero_grads()
+    l32 = eng.lora_accumulate(imgs, toks, acts, noise, t)
+    g32 = eng.lora_get_grads()
+    eng.lora_zero_grads()
+    for i in range(0, 32, 8):
+        l8 = eng.lora_accumulate(imgs[i:i + 8], toks[i:i + 8], acts[i:i + 8], noise[i:i + 8], t[i:i + 8])
+    g8 = eng.lora_get_grads()
+    eng.close()
+    assert np.isfinite(g32).all()
+    print(f"LoRA 32 vs 4x8: loss {l32:.7f} / {l8:.7f}, gradient rel-L2 {rel_l2(g32, g8):.3e}")
+    assert abs(l32 - l8) <= 1e-3 * abs(l32), (l32, l8)
+    assert rel_l2(g32, g8) <= 1e-2, rel_l2(g32, g8)
