@@ -39,16 +39,36 @@ def stale():
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force=False, verbose=False):
-    if not force and not stale():
-        return LIB
-    cmd = [nvcc()] + NVCC_FLAGS + ["-o", LIB] + [os.path.join(CSRC, s) for s in SOURCES]
+SERVER = os.path.join(HERE, "pi05_server")
+SERVER_SRC = [os.path.join(HERE, "server", f) for f in ("pi05_server.cpp", "wire.h")]
+
+
+def build_server(verbose=False):
+    """the policy server binary (host C++ over libpi05.so, found next to it at run time)"""
+    if os.path.exists(SERVER) and all(os.path.getmtime(SERVER) >= os.path.getmtime(p)
+                                      for p in SERVER_SRC + [LIB, os.path.join(HERE, "..", "include", "pi05.h")]):
+        return SERVER
+    cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-o", SERVER, SERVER_SRC[0], "-L" + HERE, "-lpi05",
+           "-Wl,-rpath,$ORIGIN", "-lpthread"]
     if verbose:
         print(" ".join(cmd))
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
-        raise RuntimeError("nvcc failed building libpi05.so")
+        raise RuntimeError("g++ failed building pi05_server")
+    return SERVER
+
+
+def build(force=False, verbose=False):
+    if force or stale():
+        cmd = [nvcc()] + NVCC_FLAGS + ["-o", LIB] + [os.path.join(CSRC, s) for s in SOURCES]
+        if verbose:
+            print(" ".join(cmd))
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise RuntimeError("nvcc failed building libpi05.so")
+    build_server(verbose)
     return LIB
 
 

@@ -1709,66 +1709,235 @@ int pi05_save_weights(pi05_engine* e, const char* path) {
   return PI05_OK;
 }
 
-int pi05_load_weights(pi05_engine* e, const char* path) {
-  if (!e || !path) return PI05_ERR_ARG;
-  cudaSetDevice(e->device);
-  FILE* f = fopen(path, "rb");
-  if (!f) {
-    e->err = std::string("cannot open ") + path;
-    return PI05_ERR_ARG;
+}  // extern "C"
+
+namespace {
+
+// ------------------------------------------------------------------ weight files (.pi05w)
+// A text manifest -- "pi05w <version>", "cfg <key> <value>" lines (the model hyper-parameters),
+// "t <name> <bf16|f32> <offset> <bytes> <dims...>" lines, "end" -- padded to 256 bytes, then the raw
+// tensors at 256-byte aligned offsets from the end of the manifest (the reference's format,
+// π05_네이티브엔진.md:46-47).
+struct WEntry {
+  size_t off = 0, bytes = 0;
+  int f32 = 0;  // element type in the file: bf16 or f32 (f32 is rounded to bf16 on load, as the reference
+                // cast its f32 orbax weights, π05_네이티브엔진.md:32)
+  long n = 0;   // elements
+};
+
+struct WFile {
+  FILE* f = nullptr;
+  size_t hdr = 0;
+  std::map<std::string, long> cfg;
+  std::map<std::string, WEntry> ent;
+  ~WFile() {
+    if (f) fclose(f);
+  }
+};
+
+bool read_manifest(const char* path, WFile& W, std::string& err) {
+  W.f = fopen(path, "rb");
+  if (!W.f) {
+    err = std::string("cannot open ") + path;
+    return false;
   }
   std::vector<std::string> lines;
   std::string cur;
   size_t consumed = 0;
   int ch;
-  while ((ch = fgetc(f)) != EOF) {
+  while ((ch = fgetc(W.f)) != EOF) {
     ++consumed;
     if (ch == '\n') {
       if (cur == "end") break;
       lines.push_back(cur);
       cur.clear();
+      if (lines.size() > (1u << 20)) break;
     } else {
       cur.push_back((char)ch);
     }
   }
-  const size_t hdr = (consumed + 255) & ~(size_t)255;
-  if (lines.empty() || lines[0] != "pi05w 1") {
-    fclose(f);
-    e->err = "not a pi05w file";
+  W.hdr = (consumed + 255) & ~(size_t)255;
+  if (lines.empty() || lines[0].rfind("pi05w", 0) != 0) {
+    err = "not a pi05w file";
+    return false;
+  }
+  for (const std::string& L : lines) {
+    char name[256], dt[16];
+    long v = 0;
+    size_t off = 0, bytes = 0;
+    if (sscanf(L.c_str(), "cfg %255s %ld", name, &v) == 2) {
+      W.cfg[name] = v;
+    } else if (sscanf(L.c_str(), "t %255s %15s %zu %zu", name, dt, &off, &bytes) == 4) {
+      WEntry e;
+      e.off = off;
+      e.bytes = bytes;
+      e.f32 = strcmp(dt, "f32") == 0;
+      if (!e.f32 && strcmp(dt, "bf16") != 0) {
+        err = std::string("tensor ") + name + ": unsupported dtype " + dt;
+        return false;
+      }
+      e.n = (long)(bytes / (e.f32 ? 4 : 2));
+      W.ent[name] = e;
+    }
+  }
+  return true;
+}
+
+uint16_t f32_to_bf16_bits(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);  // NaN stays NaN
+  return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+
+// Rows [r0, r0 + nr) of a file tensor seen as [rows][src_cols], columns [0, cols), as bf16 bits into
+// dst (row pitch dst_ld elements, row step dst_step rows).
+bool read_block(WFile& W, const WEntry& e, long src_cols, long r0, long nr, long cols, uint16_t* dst, long dst_ld,
+                long dst_step, std::string& err) {
+  const size_t es = e.f32 ? 4 : 2;
+  std::vector<char> row((size_t)src_cols * es);
+  for (long r = 0; r < nr; ++r) {
+    const size_t at = W.hdr + e.off + ((size_t)(r0 + r) * src_cols) * es;
+    if (fseek(W.f, (long)at, SEEK_SET) != 0 || fread(row.data(), 1, row.size(), W.f) != row.size()) {
+      err = "short read";
+      return false;
+    }
+    uint16_t* d = dst + (size_t)r * dst_step * dst_ld;
+    if (e.f32) {
+      const float* sf = reinterpret_cast<const float*>(row.data());
+      for (long c = 0; c < cols; ++c) d[c] = f32_to_bf16_bits(sf[c]);
+    } else {
+      memcpy(d, row.data(), (size_t)cols * 2);
+    }
+  }
+  return true;
+}
+
+// Assemble the engine tensor `t` from the file: under its own name, or from the reference's layout --
+// separate q / k / v and gate / up tensors ([out][in] each; gate/up rows interleaved here), the SigLIP
+// MLP padded 4304 -> 4352 (the padding dropped), the patch embedding at 588 columns (padded here to
+// 640 with zeros), and one adaRMS modulation Dense per norm.
+bool gather_tensor(pi05_engine* e, WFile& W, const Tensor& t, std::vector<uint16_t>& out, std::string& err) {
+  const long R = t.rows, C = t.cols;
+  out.assign((size_t)R * C, 0);
+  auto has = [&](const std::string& n, long elems) {
+    auto it = W.ent.find(n);
+    return it != W.ent.end() && it->second.n == elems;
+  };
+  auto rows_of = [&](const std::string& n, long src_cols, long r0, long nr, long cols, long dst_row, long dst_step) {
+    return read_block(W, W.ent[n], src_cols, r0, nr, cols, out.data() + (size_t)dst_row * C, C, dst_step, err);
+  };
+  if (has(t.name, R * C)) return rows_of(t.name, C, 0, R, C, 0, 1);
+  const std::string& nm = t.name;
+  auto ends = [&](const char* suf) {
+    const size_t n = strlen(suf);
+    return nm.size() > n && nm.compare(nm.size() - n, n, suf) == 0;
+  };
+  const std::string stem = nm.substr(0, nm.rfind('.') == std::string::npos ? 0 : nm.rfind('.'));  // "gem.l3.qkv"
+  const std::string base = stem.substr(0, stem.rfind('.') + 1);                                    // "gem.l3."
+  if (ends(".qkv.w") || ends(".qkv.b")) {
+    const bool bias = ends(".b");
+    const long D = bias ? 1 : C;
+    const bool sig = nm.rfind("sig.", 0) == 0;
+    const long fq = sig ? P5_SIG_W : P5_QDIM, fk = sig ? P5_SIG_W : P5_HD;
+    const std::string q = base + (bias ? "q.b" : "q.w"), k = base + (bias ? "k.b" : "k.w"), v = base + (bias ? "v.b" : "v.w");
+    if (bias) {
+      if (has(q, fq) && has(k, fk) && has(v, fk))
+        return read_block(W, W.ent[q], fq, 0, 1, fq, out.data(), C, 1, err) &&
+               read_block(W, W.ent[k], fk, 0, 1, fk, out.data() + fq, C, 1, err) &&
+               read_block(W, W.ent[v], fk, 0, 1, fk, out.data() + fq + fk, C, 1, err);
+    } else if (has(q, fq * D) && has(k, fk * D) && has(v, fk * D)) {
+      return rows_of(q, D, 0, fq, D, 0, 1) && rows_of(k, D, 0, fk, D, fq, 1) && rows_of(v, D, 0, fk, D, fq + fk, 1);
+    }
+  } else if (ends(".gu.w")) {
+    const long F = R / 2;
+    const std::string g = base + "gate.w", u = base + "up.w";
+    if (has(g, F * C) && has(u, F * C)) return rows_of(g, C, 0, F, C, 0, 2) && rows_of(u, C, 0, F, C, 1, 2);
+  } else if (nm.rfind("sig.", 0) == 0 && (ends(".mlp1.w") || ends(".mlp1.b") || ends(".mlp2.w"))) {
+    const long PAD = 4352;  // the reference padded the SigLIP MLP width to a multiple of 128 with zeros
+    if (ends(".mlp1.w") && has(nm, PAD * C)) return rows_of(nm, C, 0, R, C, 0, 1);
+    if (ends(".mlp1.b") && has(nm, PAD)) return rows_of(nm, PAD, 0, 1, C, 0, 1);
+    if (ends(".mlp2.w") && has(nm, R * PAD)) return rows_of(nm, PAD, 0, R, C, 0, 1);
+  } else if (nm == "sig.stem.w" && has(nm, R * P5_SIG_K)) {
+    return rows_of(nm, P5_SIG_K, 0, R, P5_SIG_K, 0, 1);
+  } else if (nm == "exp.ada.w" || nm == "exp.ada.b") {
+    const bool bias = nm == "exp.ada.b";
+    const long per = 3L * P5_EXP_W;
+    for (int m = 0; m < e->NM; ++m) {
+      const std::string n = m == e->NM - 1 ? std::string("exp.final.ada") + (bias ? ".b" : ".w")
+                                           : "exp.l" + std::to_string(m / 2) + ".ada" + std::to_string(m % 2 + 1) +
+                                                 (bias ? ".b" : ".w");
+      if (bias ? !has(n, per) : !has(n, per * C)) {
+        err = "weight file lacks " + n;
+        return false;
+      }
+      if (!(bias ? read_block(W, W.ent[n], per, 0, 1, per, out.data() + m * per, C, 1, err)
+                 : rows_of(n, C, 0, per, C, m * per, 1)))
+        return false;
+    }
+    return true;
+  }
+  err = "weight file lacks tensor " + nm + " of the configured shape";
+  return false;
+}
+
+const char* kCfgKeys[] = {"siglip_layers", "gemma_layers", "expert_layers", "num_steps", "n_cameras", "n_text",
+                          "horizon"};
+int32_t* cfg_field(pi05_config* c, int i) {
+  int32_t* f[] = {&c->siglip_layers, &c->gemma_layers, &c->expert_layers, &c->num_steps, &c->n_cameras, &c->n_text,
+                  &c->horizon};
+  return f[i];
+}
+
+}  // namespace
+
+extern "C" {
+
+int pi05_load_weights(pi05_engine* e, const char* path) {
+  if (!e || !path) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  WFile W;
+  std::string err;
+  if (!read_manifest(path, W, err)) {
+    e->err = "pi05_load_weights: " + err;
     return PI05_ERR_ARG;
   }
-  std::map<std::string, std::pair<size_t, size_t>> ent;
-  for (const std::string& L : lines) {
-    char name[256];
-    size_t off, bytes;
-    if (sscanf(L.c_str(), "t %255s bf16 %zu %zu", name, &off, &bytes) == 3) ent[name] = {off, bytes};
+  for (int i = 0; i < 7; ++i) {
+    auto it = W.cfg.find(kCfgKeys[i]);
+    if (it != W.cfg.end() && it->second != *cfg_field(&e->cfg, i)) {
+      e->err = std::string("pi05_load_weights: the file's ") + kCfgKeys[i] + " " + std::to_string(it->second) +
+               " differs from the engine's " + std::to_string(*cfg_field(&e->cfg, i));
+      return PI05_ERR_ARG;
+    }
   }
-  std::vector<char> buf;
+  std::vector<uint16_t> buf;
   for (const Tensor& t : e->tensors) {
-    auto it = ent.find(t.name);
-    const size_t bytes = (size_t)t.rows * t.cols * 2;
-    if (it == ent.end() || it->second.second != bytes) {
-      fclose(f);
-      e->err = "weight file lacks tensor " + t.name + " of the configured shape";
+    if (!gather_tensor(e, W, t, buf, err)) {
+      e->err = "pi05_load_weights: " + err;
       return PI05_ERR_ARG;
     }
-    buf.resize(bytes);
-    if (fseek(f, (long)(hdr + it->second.first), SEEK_SET) != 0 || fread(buf.data(), 1, bytes, f) != bytes) {
-      fclose(f);
-      e->err = "short read for " + t.name;
-      return PI05_ERR_ARG;
-    }
-    if (cudaMemcpy(t.ptr, buf.data(), bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
-      fclose(f);
+    if (cudaMemcpy(t.ptr, buf.data(), buf.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
       e->err = "device write failed";
       return PI05_ERR_CUDA;
     }
   }
-  fclose(f);
   if (!build_mods(e)) return fail_code(e);
   e->weights_ready = true;
-  ++e->wgen;  // weight-derived copies (the persistent denoise's q/k/v row permutation) are stale
+  ++e->wgen;  // weight-derived copies (the interleaved q/k/v rows of the fused-RoPE projections) are stale
   e->prefix_n = 0;
+  return PI05_OK;
+}
+
+int pi05_read_weights_config(const char* path, pi05_config* c) {
+  if (!path || !c) return PI05_ERR_ARG;
+  WFile W;
+  std::string err;
+  if (!read_manifest(path, W, err)) return PI05_ERR_ARG;
+  pi05_default_config(c);
+  for (int i = 0; i < 7; ++i) {
+    auto it = W.cfg.find(kCfgKeys[i]);
+    if (it != W.cfg.end()) *cfg_field(c, i) = (int32_t)it->second;
+  }
   return PI05_OK;
 }
 
@@ -2100,7 +2269,9 @@ int pi05_op_siglip_attention(pi05_engine* e, int images, const void* qkv, void* 
 
 pi05_engine* pi05_create_batch(const char* weights_path, int device, int max_batch) {
   char err[512];
-  pi05_engine* e = pi05_create(nullptr, device, max_batch, err, sizeof(err));
+  pi05_config cfg;
+  if (weights_path ? pi05_read_weights_config(weights_path, &cfg) != PI05_OK : false) return nullptr;
+  pi05_engine* e = pi05_create(weights_path ? &cfg : nullptr, device, max_batch, err, sizeof(err));
   if (!e) return nullptr;
   const int rc = weights_path ? pi05_load_weights(e, weights_path) : pi05_init_random_weights(e, 0);
   if (rc != PI05_OK) {

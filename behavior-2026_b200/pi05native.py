@@ -26,6 +26,7 @@ EXPORTS = [
     "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_resize_with_pad", "pi05_normalize", "pi05_discretize_state", "pi05_absolute_actions", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
     "pi05_linear_static_status", "pi05_verify", "pi05_set_act_config", "pi05_act",
     "pi05_nccl_unique_id", "pi05_lora_attach_nccl", "pi05_lora_world",
+    "pi05_read_weights_config",
 ]
 
 
@@ -141,6 +142,7 @@ def _load():
     L.pi05_verify.argtypes = [vp, vp, vp, vp, vp, PROBE, vp]
     L.pi05_set_act_config.argtypes = [vp, P(ActConfig)]
     L.pi05_nccl_unique_id.argtypes = [vp]
+    L.pi05_read_weights_config.argtypes = [ctypes.c_char_p, cfg]
     L.pi05_lora_attach_nccl.argtypes = [vp, vp, i32, i32]
     L.pi05_lora_world.argtypes = [vp]
     L.pi05_act.argtypes = [vp, i32, vp, vp, vp, vp, vp]
@@ -252,6 +254,18 @@ class Engine:
         pn, kn = _ptr(noise, np.float32)
         po, ko = _ptr(out, np.float32, writable=True)
         self._check(lib.pi05_denoise(self._h, n, pn, po))
+        return out
+
+    def infer_batch(self, images, tokens, noise, out=None):
+        """pi05_infer_batch (the reference's name for infer)"""
+        n = images.shape[0]
+        if out is None:
+            out = np.empty((n, self.config.horizon, 32), np.float32)
+        pi, ki = _ptr(images, np.uint8)
+        pt, kt = _ptr(tokens, np.int32)
+        pn_, kn = _ptr(noise, np.float32)
+        po, ko = _ptr(out, np.float32, writable=True)
+        self._check(lib.pi05_infer_batch(self._h, n, pi, pt, pn_, po))
         return out
 
     def infer(self, images, tokens, noise, out=None):
@@ -453,6 +467,27 @@ class Engine:
 
     def reset_slot(self, slot):
         self._check(lib.pi05_reset_slot(self._h, slot))
+
+
+def read_weights_config(path):
+    """pi05_read_weights_config: the Config a weight file's cfg lines describe (no GPU)"""
+    c = Config()
+    rc = lib.pi05_read_weights_config(path.encode(), ctypes.byref(c))
+    if rc != OK:
+        raise Pi05Error(rc, f"pi05_read_weights_config: cannot read {path}")
+    return c
+
+
+def create_batch(weights_path, device=0, max_batch=1):
+    """pi05_create_batch (the reference's constructor): an Engine configured and loaded from the file"""
+    h = lib.pi05_create_batch(weights_path.encode() if weights_path else None, device, max_batch)
+    if not h:
+        raise Pi05Error(ERR_ARG, f"pi05_create_batch failed for {weights_path}")
+    eng = Engine.__new__(Engine)
+    eng.config = read_weights_config(weights_path) if weights_path else Config.make()
+    eng.max_batch = max_batch
+    eng._h = ctypes.c_void_p(h)
+    return eng
 
 
 def nccl_unique_id():

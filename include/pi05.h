@@ -68,12 +68,20 @@ PI05_API void pi05_destroy(pi05_engine* e);
 PI05_API const char* pi05_last_error(const pi05_engine* e);
 
 /* Weights.  pi05_init_random_weights fills every tensor from the seeded generator (linear weights
- * N(0, 0.02) in bf16; the synthetic workload of the benchmarks).  pi05_load_weights reads a weight
- * file written by pi05_save_weights (text manifest + 256-byte aligned raw bf16 tensors, the same
- * scheme as the reference's .pi05w, π05_네이티브엔진.md:46-49). */
+ * N(0, 0.02) in bf16; the synthetic workload of the benchmarks).  Weight files (.pi05w, the reference's
+ * scheme, π05_네이티브엔진.md:46-49): a text manifest of "cfg <key> <value>" lines (the pi05_config fields)
+ * and "t <name> <bf16|f32> <offset> <bytes> <dims...>" lines, then 256-byte aligned raw tensors, every
+ * linear [out][in].  pi05_save_weights writes the engine's layout (bf16, fused q|k|v, gate/up rows
+ * interleaved).  pi05_load_weights also takes the reference's layout, tensor by tensor (:48): separate
+ * q/k/v and gate/up tensors (interleaved on load; q/k rows are paired per head for the fused RoPE when
+ * the engine prepares them), the SigLIP MLP padded 4304 -> 4352 (padding dropped), the 588-column patch
+ * embedding, one adaRMS Dense per norm, f32 tensors rounded to bf16 (the reference cast its f32
+ * checkpoint the same way, :32); a file whose cfg differs from the engine's is refused.
+ * pi05_read_weights_config: the file's configuration (defaults for keys it lacks), no GPU needed. */
 PI05_API int pi05_init_random_weights(pi05_engine* e, uint64_t seed);
 PI05_API int pi05_save_weights(pi05_engine* e, const char* path);
 PI05_API int pi05_load_weights(pi05_engine* e, const char* path);
+PI05_API int pi05_read_weights_config(const char* path, pi05_config* c);
 
 /* Prefix: SigLIP over the camera images, text embedding, Gemma-2B prefill; fills the per-sample
  * bf16 KV cache.  (Reference: the per-board prefix CUDA graph, π05_네이티브엔진.md:298.) */
@@ -218,7 +226,8 @@ PI05_API int pi05_linear_static(int T, int F, int K, const void* x, const void* 
  * No counterpart in the reference's ABI. */
 PI05_API int pi05_linear_static_status(void* stream, char* err, size_t err_len);
 
-/* Reference batch-API names (π05_네이티브엔진.md:288-303). */
+/* Reference batch-API names (π05_네이티브엔진.md:288-303).  pi05_create_batch configures the engine from the
+ * weight file's cfg lines (NULL path: default configuration with pi05_init_random_weights(0)). */
 PI05_API pi05_engine* pi05_create_batch(const char* weights_path, int device, int max_batch);
 PI05_API int pi05_infer_batch(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens, const float* noise,
                      float* actions);
