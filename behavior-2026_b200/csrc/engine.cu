@@ -730,9 +730,11 @@ bool attention_tc(pi05_engine* e, const AttnArgs& a0, int batch) {
 
 bool attention(pi05_engine* e, const AttnArgs& a0, int batch, int hd) {
   if (hd == P5_HD && a0.G == 8 && a0.qdiv == 1.0f && e->attn_tc && a0.len1 > 0) return attention_tc(e, a0, batch);
-  if (hd == P5_SIG_HD && a0.G == 1 && e->attn_tc && a0.T == AttnSigCfg::ROWS * 2 && a0.len1 == AttnSigCfg::KEYS &&
-      a0.len2 == 0 && !a0.lse) {
-    // SigLIP: one CTA per (128 queries, head, image) on tcgen05
+  // SigLIP: one CTA per (128 queries, head, image) on tcgen05 up to 32 images; measured per call (CUDA events,
+  // 20 launches): 3 images 9.7 vs 14.5 us, 24 images 51.4 vs 55.5 us, 48 images 111.7 vs 101.3 us, 192 images
+  // 422.8 vs 378.2 us for the tcgen05 and the mma.sync kernel, so the larger batches take the mma.sync kernel
+  if (hd == P5_SIG_HD && a0.G == 1 && e->attn_tc && batch <= 32 && a0.T == AttnSigCfg::ROWS * 2 &&
+      a0.len1 == AttnSigCfg::KEYS && a0.len2 == 0 && !a0.lse) {
     AttnArgs a = a0;
     a.pdl = e->pdl ? 1 : 0;
     return launch(e, attn_sig_kernel, dim3(2, P5_SIG_HEADS, batch), dim3(384), (size_t)AttnSigCfg::SMEM, true, a,

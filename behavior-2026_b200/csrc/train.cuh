@@ -51,6 +51,7 @@ struct Trainer {
   bool overlap = false, reduced = false;
   long n_params = 0;
   float *p = nullptr, *g = nullptr, *m = nullptr, *v = nullptr;
+  float* ema = nullptr;  // EMA of p (cfg.ema_decay > 0)
   float* sumsq = nullptr;
   int step = 0;
   std::vector<TrainLayer> gl, el;
@@ -260,9 +261,11 @@ bool lora_create(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
   if (!talloc(e, (void**)&T->p, np * 4) || !talloc(e, (void**)&T->g, np * 4) || !talloc(e, (void**)&T->m, np * 4) ||
       !talloc(e, (void**)&T->v, np * 4) || !talloc(e, (void**)&T->sumsq, 1024 * 4))
     return false;
+  if (c->ema_decay > 0.f && !talloc(e, (void**)&T->ema, np * 4)) return false;
   lora_init_kernel<<<148 * 8, 256, 0, e->stream>>>(T->p, np, p5_key(seed, K_LORA_GEM_A, 0),
                                                     p5_scale_for_std(P5_LORA_STD));
   CK(cudaGetLastError());
+  if (T->ema) CK(cudaMemcpyAsync(T->ema, T->p, np * 4, cudaMemcpyDeviceToDevice, e->stream));  // EMA starts at p
   for (int l = 0; l < L; ++l) {
     const GemLayer& g = e->gem[l];
     const ExpLayer& x = e->ex[l];
@@ -772,14 +775,30 @@ bool lora_exchange(pi05_engine* e) {
   return dp_join(e, T->dp);
 }
 
+// openpi's warmup + cosine schedule (optax warmup_cosine_decay_schedule with init lr / (warmup + 1)), in
+// double precision and rounded once, as the host computes it before each update
+float lora_schedule_lr(const pi05_lora_config& c, int k) {
+  if (c.warmup_steps <= 0 && c.decay_steps <= 0) return c.lr;
+  const double peak = c.lr, end = c.decay_lr, w = c.warmup_steps;
+  if (k < c.warmup_steps) {
+    const double init = peak / (w + 1.0);
+    return (float)(init + (peak - init) * (double)k / w);
+  }
+  const double span = std::max(1.0, (double)c.decay_steps - w);
+  const double t = std::min((double)k - w, span);
+  return (float)(end + (peak - end) * 0.5 * (1.0 + std::cos(M_PI * t / span)));
+}
+
 bool lora_opt(pi05_engine* e) {
   Trainer* T = e->tr;
   const int nb = 256;
   sumsq_partial_kernel<<<nb, 256, 0, e->stream>>>(T->g, T->n_params, T->sumsq);
+  const float lr = lora_schedule_lr(T->cfg, T->step);  // update number T->step (0-based) of the schedule
   T->step += 1;
   adamw_kernel<<<148 * 8, 256, 0, e->stream>>>(T->p, T->g, T->m, T->v, T->n_params, T->sumsq, nb, T->cfg.clip_norm,
-                                               T->cfg.lr, T->cfg.beta1, T->cfg.beta2, T->cfg.eps, T->cfg.weight_decay,
+                                               lr, T->cfg.beta1, T->cfg.beta2, T->cfg.eps, T->cfg.weight_decay,
                                                T->step);
+  if (T->ema) ema_kernel<<<148 * 4, 256, 0, e->stream>>>(T->ema, T->p, T->n_params, T->cfg.ema_decay);
   CK(cudaGetLastError());
   return scatter_all(e, T);
 }
@@ -800,6 +819,20 @@ void pi05_lora_default_config(pi05_lora_config* c) {
   c->weight_decay = 1e-10f;
   c->clip_norm = 1.0f;
   c->micro_batch = 8;
+  c->warmup_steps = 0;
+  c->decay_steps = 0;
+  c->decay_lr = 0.f;
+  c->ema_decay = 0.f;
+}
+
+float pi05_lora_schedule_lr(const pi05_lora_config* c, int k) { return c ? lora_schedule_lr(*c, k) : 0.f; }
+
+int pi05_lora_get_ema(pi05_engine* e, float* out) {
+  if (!e || !e->tr || !e->tr->ema) return PI05_ERR_STATE;
+  if (!out) return PI05_ERR_ARG;
+  cudaSetDevice(e->device);
+  if (cudaMemcpy(out, e->tr->ema, e->tr->n_params * 4, cudaMemcpyDefault) != cudaSuccess) return PI05_ERR_CUDA;
+  return PI05_OK;
 }
 
 int pi05_lora_init(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
@@ -882,6 +915,10 @@ int pi05_lora_set_params(pi05_engine* e, const float* in) {
   cudaSetDevice(e->device);
   if (cudaMemcpyAsync(e->tr->p, in, e->tr->n_params * 4, cudaMemcpyDefault, e->stream) != cudaSuccess)
     return PI05_ERR_CUDA;
+  // new adapters: the EMA restarts from them
+  if (e->tr->ema && cudaMemcpyAsync(e->tr->ema, e->tr->p, e->tr->n_params * 4, cudaMemcpyDeviceToDevice,
+                                    e->stream) != cudaSuccess)
+    return PI05_ERR_CUDA;
   if (!scatter_all(e, e->tr)) return fail_code(e);
   return pi05_sync(e);
 }
@@ -898,7 +935,8 @@ int pi05_lora_reset_optimizer(pi05_engine* e) {
   return pi05_sync(e);
 }
 
-// Train state file: "pi05lora 1\nparams N\nstep S\n" padded to 256 bytes, then p, m, v (fp32, N each).
+// Train state file: "pi05lora 1\nparams N\nstep S\nema E\n" padded to 256 bytes, then p, m, v (fp32, N each)
+// and, when E = 1, the EMA.
 int pi05_lora_save_state(pi05_engine* e, const char* path) {
   if (!e || !e->tr || !path) return PI05_ERR_ARG;
   cudaSetDevice(e->device);
@@ -910,9 +948,10 @@ int pi05_lora_save_state(pi05_engine* e, const char* path) {
     return PI05_ERR_ARG;
   }
   char hdr[256] = {0};
-  snprintf(hdr, sizeof(hdr), "pi05lora 1\nparams %ld\nstep %d\n", T->n_params, T->step);
+  snprintf(hdr, sizeof(hdr), "pi05lora 1\nparams %ld\nstep %d\nema %d\n", T->n_params, T->step, T->ema ? 1 : 0);
   fwrite(hdr, 1, sizeof(hdr), f);
-  for (float* src : {T->p, T->m, T->v}) {
+  for (float* src : {T->p, T->m, T->v, T->ema}) {
+    if (!src) continue;
     if (cudaMemcpy(buf.data(), src, T->n_params * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
       fclose(f);
       return PI05_ERR_CUDA;
@@ -935,14 +974,17 @@ int pi05_lora_load_state(pi05_engine* e, const char* path) {
   char hdr[256];
   long np = -1;
   int step = -1;
-  if (fread(hdr, 1, sizeof(hdr), f) != sizeof(hdr) || sscanf(hdr, "pi05lora 1\nparams %ld\nstep %d", &np, &step) != 2 ||
-      np != T->n_params) {
+  int ema = 0;
+  if (fread(hdr, 1, sizeof(hdr), f) != sizeof(hdr) ||
+      sscanf(hdr, "pi05lora 1\nparams %ld\nstep %d\nema %d", &np, &step, &ema) < 2 || np != T->n_params ||
+      (ema != 0) != (T->ema != nullptr)) {
     fclose(f);
     e->err = "pi05_lora_load_state: not a train state of this configuration";
     return PI05_ERR_ARG;
   }
   std::vector<float> buf((size_t)np);
-  for (float* dst : {T->p, T->m, T->v}) {
+  for (float* dst : {T->p, T->m, T->v, T->ema}) {
+    if (!dst) continue;
     if (fread(buf.data(), 4, buf.size(), f) != buf.size()) {
       fclose(f);
       e->err = "pi05_lora_load_state: short file";

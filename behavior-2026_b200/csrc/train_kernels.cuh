@@ -335,6 +335,12 @@ __global__ void scale_f32_kernel(float* x, long n, float s) {
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) x[i] *= s;
 }
 
+// ema = d * ema + (1 - d) * p after each update (openpi scripts/train.py)
+__global__ void ema_kernel(float* ema, const float* p, long n, float d) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    ema[i] = d * ema[i] + (1.0f - d) * p[i];
+}
+
 // ---------------------------------------------------------------- optimizer
 // sum of squares of the gradient, deterministic two-level reduction
 __global__ void sumsq_partial_kernel(const float* g, long n, float* partial) {

@@ -26,7 +26,7 @@ EXPORTS = [
     "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_resize_with_pad", "pi05_normalize", "pi05_discretize_state", "pi05_absolute_actions", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
     "pi05_linear_static_status", "pi05_verify", "pi05_set_act_config", "pi05_act",
     "pi05_nccl_unique_id", "pi05_lora_attach_nccl", "pi05_lora_world",
-    "pi05_read_weights_config",
+    "pi05_read_weights_config", "pi05_lora_schedule_lr", "pi05_lora_get_ema",
 ]
 
 
@@ -68,7 +68,23 @@ class ActConfig(ctypes.Structure):
 class LoraConfig(ctypes.Structure):
     _fields_ = [("rank", ctypes.c_int32), ("alpha", ctypes.c_float), ("lr", ctypes.c_float), ("beta1", ctypes.c_float),
                 ("beta2", ctypes.c_float), ("eps", ctypes.c_float), ("weight_decay", ctypes.c_float),
-                ("clip_norm", ctypes.c_float), ("micro_batch", ctypes.c_int32)]
+                ("clip_norm", ctypes.c_float), ("micro_batch", ctypes.c_int32), ("warmup_steps", ctypes.c_int32),
+                ("decay_steps", ctypes.c_int32), ("decay_lr", ctypes.c_float), ("ema_decay", ctypes.c_float)]
+
+    @classmethod
+    def reference_recipe(cls, micro_batch=8):
+        """the reference's fine-tuning recipe (π05_네이티브엔진.md:216): warmup 1000 -> cosine 2.5e-5 -> 2.5e-6 at
+        30000 steps, EMA 0.99"""
+        c = cls()
+        lib.pi05_lora_default_config(ctypes.byref(c))
+        c.micro_batch, c.lr, c.warmup_steps, c.decay_steps, c.decay_lr, c.ema_decay = micro_batch, 2.5e-5, 1000, \
+            30000, 2.5e-6, 0.99
+        return c
+
+
+def lora_schedule_lr(config, k):
+    """pi05_lora_schedule_lr: the learning rate of update k under `config` (a LoraConfig)"""
+    return lib.pi05_lora_schedule_lr(ctypes.byref(config), k)
 
 
 PROBE = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float), ctypes.c_int64, ctypes.c_void_p)
@@ -125,6 +141,9 @@ def _load():
     L.pi05_linear_static_status.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t]
     L.pi05_lora_default_config.argtypes = [P(LoraConfig)]
     L.pi05_lora_default_config.restype = None
+    L.pi05_lora_schedule_lr.argtypes = [P(LoraConfig), i32]
+    L.pi05_lora_schedule_lr.restype = ctypes.c_float
+    L.pi05_lora_get_ema.argtypes = [vp, vp]
     L.pi05_lora_init.argtypes = [vp, P(LoraConfig), u64]
     L.pi05_lora_num_params.argtypes = [vp]
     L.pi05_lora_num_params.restype = ctypes.c_long
@@ -373,6 +392,11 @@ class Engine:
     def lora_set_params(self, p):
         p = np.ascontiguousarray(p, np.float32)
         self._check(lib.pi05_lora_set_params(self._h, p.ctypes.data))
+
+    def lora_get_ema(self):
+        out = np.empty(self.lora_num_params, np.float32)
+        self._check(lib.pi05_lora_get_ema(self._h, out.ctypes.data))
+        return out
 
     def lora_get_grads(self):
         out = np.empty(self.lora_num_params, np.float32)

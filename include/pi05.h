@@ -143,8 +143,22 @@ typedef struct {
   float weight_decay;  /* 1e-10 */
   float clip_norm;     /* 1.0 (global norm) */
   int32_t micro_batch; /* samples per forward/backward pass; activations of all layers are kept */
+  /* learning-rate schedule (openpi training/optimizer.py CosineDecaySchedule, the reference's recipe,
+   * π05_네이티브엔진.md:216: warmup 1000, lr 2.5e-5, decay_steps 30000, decay_lr 2.5e-6): update k (k = 0, 1,
+   * ..) uses lr * ... rising linearly from lr / (warmup + 1) over warmup_steps, then a half cosine from lr
+   * to decay_lr at decay_steps; warmup_steps = decay_steps = 0 keeps lr constant (the default) */
+  int32_t warmup_steps;
+  int32_t decay_steps;
+  float decay_lr;
+  /* EMA of the adapters after every update, ema = d * ema + (1 - d) * params (openpi scripts/train.py,
+   * the reference's 0.99, π05_네이티브엔진.md:216); 0 = none (the default) */
+  float ema_decay;
 } pi05_lora_config;
 PI05_API void pi05_lora_default_config(pi05_lora_config* c);
+/* The learning rate of update `k` (0-based) under c's schedule; host only. */
+PI05_API float pi05_lora_schedule_lr(const pi05_lora_config* c, int k);
+/* The EMA adapters (fp32 flat buffer, the layout of pi05_lora_get_params); PI05_ERR_STATE without EMA. */
+PI05_API int pi05_lora_get_ema(pi05_engine* e, float* out);
 /* Adapters initialised N(0, 0.01) from `seed`; needs weights loaded and max_batch >= micro_batch. */
 PI05_API int pi05_lora_init(pi05_engine* e, const pi05_lora_config* c, uint64_t seed);
 PI05_API long pi05_lora_num_params(pi05_engine* e);
@@ -181,8 +195,8 @@ PI05_API int pi05_lora_get_grads(pi05_engine* e, float* out);
 PI05_API void* pi05_lora_grad_buffer(pi05_engine* e); /* device pointer to the fp32 gradients */
 /* zero the AdamW moments and the step count */
 PI05_API int pi05_lora_reset_optimizer(pi05_engine* e);
-/* checkpoint / resume of the train state: adapters, AdamW moments and step (fp32 flat buffers;
- * the reference saved params, EMA, Adam m/v and step, π05_네이티브엔진.md:281-282) */
+/* checkpoint / resume of the train state: adapters, AdamW moments, step and (when enabled) the EMA (fp32
+ * flat buffers; the reference saved params, EMA, Adam m/v and step, π05_네이티브엔진.md:281-282) */
 PI05_API int pi05_lora_save_state(pi05_engine* e, const char* path);
 PI05_API int pi05_lora_load_state(pi05_engine* e, const char* path);
 

@@ -59,3 +59,25 @@ def test_bf16_helpers_round_to_nearest_even(pn):
     back = pn.bf16_bits_to_f32(bits)
     # 1 + 2^-8 is a tie between 1 and 1+2^-7 -> even (1.0); 1.005859375 rounds up
     assert back.tolist() == [1.0, 1.0, 1.0078125, -0.10009765625, 45.25]
+
+
+def test_lora_schedule_matches_optax_warmup_cosine(pn):
+    """The reference recipe's schedule (openpi CosineDecaySchedule: optax warmup_cosine_decay_schedule with
+    init lr / (warmup + 1)) restated in numpy, float64 rounded to float32; the default is constant."""
+    import math
+
+    c = pn.LoraConfig.reference_recipe()
+    peak, end, w, d = float(np.float32(2.5e-5)), float(np.float32(2.5e-6)), 1000, 30000  # the struct holds float32
+
+    def ref(k):
+        if k < w:
+            init = peak / (w + 1)
+            return init + (peak - init) * k / w
+        t = min(k - w, d - w)
+        return end + (peak - end) * 0.5 * (1 + math.cos(math.pi * t / (d - w)))
+
+    for k in (0, 1, 500, 999, 1000, 1001, 15000, 29999, 30000, 40000):
+        assert pn.lora_schedule_lr(c, k) == np.float32(ref(k)), k
+    flat = pn.LoraConfig()
+    pn.lib.pi05_lora_default_config(ctypes.byref(flat))
+    assert pn.lora_schedule_lr(flat, 0) == pn.lora_schedule_lr(flat, 5000) == np.float32(1e-4)

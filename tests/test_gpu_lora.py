@@ -136,3 +136,36 @@ def test_lora_gradients_tcgen05_backward_match_mma_sync(lora_case, pn, monkeypat
             bad.append((n, d, e))
     assert not bad, bad
     assert rel_l2(g_tc, g_mma.astype(np.float64)) <= GRAD_REL_L2
+
+
+def test_lora_reference_recipe_schedule_and_ema(pn, oracle, lora_case, tmp_path):
+    """The reference's recipe (warmup 1000 -> cosine, EMA 0.99): the first update moves each adapter by
+    about the warmup's first rate lr / 1001 (AdamW's first step is ~lr * sign(g)); the EMA starts at the
+    initial adapters and follows ema = 0.99 ema + 0.01 p (fp32); a checkpoint resumes the EMA too."""
+    cfg = pn.Config.make(siglip_layers=1, gemma_layers=2, num_steps=10)
+    eng = pn.Engine(cfg, max_batch=2)
+    eng.init_random_weights(4)
+    rc = pn.LoraConfig.reference_recipe(micro_batch=2)
+    eng.lora_init(seed=5, micro_batch=2, lr=rc.lr, warmup_steps=rc.warmup_steps, decay_steps=rc.decay_steps,
+                  decay_lr=rc.decay_lr, ema_decay=rc.ema_decay)
+    batch = lora_case["batch"]
+    p0 = eng.lora_get_params()
+    np.testing.assert_array_equal(eng.lora_get_ema(), p0)
+    eng.lora_step(*batch)
+    p1 = eng.lora_get_params()
+    lr0 = pn.lora_schedule_lr(rc, 0)
+    d = np.abs(p1 - p0)
+    moved = d > 0
+    assert moved.mean() > 0.5 and 0.5 * lr0 < np.median(d[moved]) < 1.5 * lr0, (np.median(d[moved]), lr0)
+    ema1 = eng.lora_get_ema()
+    np.testing.assert_allclose(ema1, np.float32(0.99) * p0 + np.float32(0.01) * p1, rtol=1e-6, atol=1e-9)
+    path = str(tmp_path / "recipe.pi05lora")
+    eng.lora_save_state(path)
+    eng.lora_step(*batch)
+    p2, e2 = eng.lora_get_params(), eng.lora_get_ema()
+    eng.lora_load_state(path)
+    np.testing.assert_array_equal(eng.lora_get_ema(), ema1)
+    eng.lora_step(*batch)
+    np.testing.assert_array_equal(eng.lora_get_params(), p2)
+    np.testing.assert_array_equal(eng.lora_get_ema(), e2)
+    eng.close()

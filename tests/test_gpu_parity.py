@@ -221,7 +221,7 @@ def test_attention_engine_splits_match_torch(pn, torch_cuda, T, S, b):
 
 
 @pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma_sync"])
-@pytest.mark.parametrize("images", [1, 5])
+@pytest.mark.parametrize("images", [1, 5, 40])
 def test_siglip_attention_matches_torch(pn, torch_cuda, monkeypatch, tc, images):
     """SigLIP MHA (16 heads x 72 per 256-token image, q rounded after / 8.5) against fp32 torch."""
     torch = torch_cuda
