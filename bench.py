@@ -453,6 +453,30 @@ def run_sweep(args, local):
     return 0
 
 
+def run_sigattn(args, local):
+    """SigLIP attention by image count on both kernels (tcgen05 and mma.sync, PI05_ATTN_TC): the measurement
+    behind the engine's choice of kernel per image count.  Device time per launch over 20 launches."""
+    import torch
+    import pi05native as pn
+    for tc in ("1", "0"):
+        os.environ["PI05_ATTN_TC"] = tc  # read when the engine is created
+        eng = pn.Engine(pn.Config.make(siglip_layers=1, gemma_layers=1, num_steps=1), device=local, max_batch=1)
+        for images in (3, 6, 12, 24, 48, 96, 192):
+            qkv = torch.randn(images * 256, 3456, device="cuda").bfloat16()
+            out = torch.empty(images * 256, 1152, device="cuda", dtype=torch.bfloat16)
+            torch.cuda.synchronize()
+            for _ in range(3):
+                eng.op_siglip_attention(qkv, out)
+            total, _ = timed(eng, lambda: eng.op_siglip_attention(qkv, out), 20)
+            fl = 4.0 * images * 16 * 256 * 256 * 72
+            print(json.dumps({"op": "siglip_attention", "kernel": "tcgen05" if tc == "1" else "mma.sync",
+                              "images": images, "us": total / 20 * 1e3,
+                              "tflops": fl / (total / 20 / 1e3) / 1e12}), flush=True)
+        eng.close()
+    os.environ.pop("PI05_ATTN_TC", None)
+    return 0
+
+
 # ---------------------------------------------------------------- LoRA train step (config 4)
 LORA_TFLOP_PER_SAMPLE = None  # filled by lora_flops_per_sample()
 
@@ -595,7 +619,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="bs64", choices=["bs64", "bs1", "denoise", "sweep", "gemm", "lora"])
+    ap.add_argument("--workload", default="bs64", choices=["bs64", "bs1", "denoise", "sweep", "gemm", "lora", "sigattn"])
     ap.add_argument("--lora-batch", type=int, default=32, help="samples per GPU per LoRA step")
     ap.add_argument("--micro-batch", type=int, default=32,
                     help="samples per LoRA forward/backward pass (measured on B200: one 32-sample pass 86.0 "
@@ -618,6 +642,8 @@ def main():
             return run_sweep(args, local) if rank == 0 else 0
         if args.workload == "gemm":
             return run_gemm(args, local) if rank == 0 else 0
+        if args.workload == "sigattn":
+            return run_sigattn(args, local) if rank == 0 else 0
         if args.workload == "lora":
             return run_lora(args, world, rank, local)
         return run_ours(args, world, rank, local)
