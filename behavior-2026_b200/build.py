@@ -11,7 +11,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libpi05.so")
-SOURCES = ["engine.cu", "static_scratch.cu", "preprocess.cu"]
+SOURCES = ["engine.cu", "static_scratch.cu", "preprocess.cu", "tokenizer.cpp"]
 DEPS = SOURCES + ["common.cuh", "attention_bwd_tc.cuh", "gemm_tc.cuh", "attention.cuh", "kernels.cuh", "pi05_model.h", "train.cuh",
                   "train_kernels.cuh", "attention_bwd.cuh", "attention_tc.cuh", "denoise_mega.cuh", "attention_sig.cuh", "gemm_wide.cuh", "resize.cuh", "dp_nccl.cuh"]
 

@@ -26,7 +26,8 @@ EXPORTS = [
     "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_resize_with_pad", "pi05_normalize", "pi05_discretize_state", "pi05_absolute_actions", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
     "pi05_linear_static_status", "pi05_verify", "pi05_set_act_config", "pi05_act",
     "pi05_nccl_unique_id", "pi05_lora_attach_nccl", "pi05_lora_world",
-    "pi05_read_weights_config", "pi05_lora_schedule_lr", "pi05_lora_get_ema",
+    "pi05_read_weights_config", "pi05_lora_schedule_lr", "pi05_lora_get_ema", "pi05_tokenizer_load",
+    "pi05_tokenizer_free", "pi05_tokenizer_vocab_size", "pi05_tokenizer_encode", "pi05_tokenize_prompt",
 ]
 
 
@@ -162,6 +163,13 @@ def _load():
     L.pi05_set_act_config.argtypes = [vp, P(ActConfig)]
     L.pi05_nccl_unique_id.argtypes = [vp]
     L.pi05_read_weights_config.argtypes = [ctypes.c_char_p, cfg]
+    L.pi05_tokenizer_load.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]
+    L.pi05_tokenizer_load.restype = vp
+    L.pi05_tokenizer_free.argtypes = [vp]
+    L.pi05_tokenizer_free.restype = None
+    L.pi05_tokenizer_vocab_size.argtypes = [vp]
+    L.pi05_tokenizer_encode.argtypes = [vp, ctypes.c_char_p, i32, vp, i32]
+    L.pi05_tokenize_prompt.argtypes = [vp, ctypes.c_char_p, vp, i32, i32, vp, vp]
     L.pi05_lora_attach_nccl.argtypes = [vp, vp, i32, i32]
     L.pi05_lora_world.argtypes = [vp]
     L.pi05_act.argtypes = [vp, i32, vp, vp, vp, vp, vp]
@@ -491,6 +499,50 @@ class Engine:
 
     def reset_slot(self, slot):
         self._check(lib.pi05_reset_slot(self._h, slot))
+
+
+class Tokenizer:
+    """pi05_tokenizer: a SentencePiece BPE model file (identity normalization, byte fallback) and the
+    pi0.5 prompt layout"""
+
+    def __init__(self, model_path):
+        err = ctypes.create_string_buffer(512)
+        h = lib.pi05_tokenizer_load(model_path.encode(), err, len(err))
+        if not h:
+            raise Pi05Error(ERR_ARG, err.value.decode())
+        self._h = ctypes.c_void_p(h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib.pi05_tokenizer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def vocab_size(self):
+        return lib.pi05_tokenizer_vocab_size(self._h)
+
+    def encode(self, text, add_bos=False):
+        raw = text.encode()
+        n = lib.pi05_tokenizer_encode(self._h, raw, int(add_bos), None, 0)
+        if n < 0:
+            raise Pi05Error(n, "pi05_tokenizer_encode")
+        out = np.empty(max(n, 1), np.int32)
+        lib.pi05_tokenizer_encode(self._h, raw, int(add_bos), out.ctypes.data, n)
+        return out[:n].tolist()
+
+    def prompt(self, task, state=None, max_len=200):
+        """(ids int32 [max_len], mask bool [max_len]) of the pi0.5 prompt"""
+        ids = np.empty(max_len, np.int32)
+        mask = np.empty(max_len, np.uint8)
+        st = None if state is None else np.ascontiguousarray(state, np.float32)
+        n = lib.pi05_tokenize_prompt(self._h, task.encode(), None if st is None else st.ctypes.data,
+                                     0 if st is None else st.size, max_len, ids.ctypes.data, mask.ctypes.data)
+        if n < 0:
+            raise Pi05Error(n, "pi05_tokenize_prompt")
+        return ids, mask.astype(bool)
 
 
 def read_weights_config(path):

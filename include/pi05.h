@@ -304,6 +304,23 @@ PI05_API int pi05_normalize(float* x, int n, int dim, const float* a, const floa
 PI05_API int pi05_discretize_state(const float* x, int n, int dim, int bins, int32_t* out);
 PI05_API int pi05_absolute_actions(float* actions, int horizon, int dim, const float* state, const uint8_t* mask);
 
+/* Prompt tokenizer (the reference's C++ SentencePiece tokenizer, π05_네이티브엔진.md:83): a SentencePiece BPE
+ * model read from its .model file (identity normalization, byte fallback, user-defined symbols; Gemma's
+ * tokenizer is such a model; the file itself is not part of this build).  Host only, no GPU.
+ *   pi05_tokenizer_encode: ids of `text` (BOS first when add_bos); returns the number of ids (only the
+ *     first max_ids are written) or a negative error.
+ *   pi05_tokenize_prompt: the pi0.5 prompt of openpi's PaligemmaTokenizer: the task stripped, '_' and
+ *     newlines as spaces, "Task: <task>, State: <256-bin state bins>;\nAction: " with BOS, padded with 0 (mask
+ *     0) or cut to max_len (n_text); state_dim = 0 gives the pi0 layout (task, BOS, then "\n").  Returns the
+ *     number of real tokens. */
+typedef struct pi05_tokenizer pi05_tokenizer;
+PI05_API pi05_tokenizer* pi05_tokenizer_load(const char* model_path, char* err, size_t err_len);
+PI05_API void pi05_tokenizer_free(pi05_tokenizer* t);
+PI05_API int pi05_tokenizer_vocab_size(const pi05_tokenizer* t);
+PI05_API int pi05_tokenizer_encode(const pi05_tokenizer* t, const char* text, int add_bos, int32_t* ids, int max_ids);
+PI05_API int pi05_tokenize_prompt(const pi05_tokenizer* t, const char* task, const float* state, int state_dim,
+                                  int max_len, int32_t* ids, uint8_t* mask);
+
 #ifdef __cplusplus
 }
 #endif
