@@ -127,6 +127,7 @@ struct pi05_engine {
   std::vector<std::vector<float>> act_chunk;
   std::vector<int> act_next;
   std::vector<long> act_plans;
+  float* noise_chol = nullptr;  // [horizon*32][horizon*32] lower-triangular factor of the noise covariance
   // device staging of pi05_act_batch's camera frames: host frames, resize tap tables, frame jobs
   uint8_t* frame_stage = nullptr;
   size_t frame_stage_bytes = 0;
@@ -2468,8 +2469,15 @@ int pi05_act_batch(pi05_engine* e, int n, const int* slots, const pi05_frame* fr
         const uint64_t key = p5_key(e->act_seed, K_IN_NOISE, (uint32_t)sl);
         const float sc = p5_scale_for_std(1.0);
         for (size_t q = 0; q < nz; ++q) z[q] = p5_normal(key, (uint64_t)(e->act_plans[sl] * nz + q), sc);
-        if (cudaMemcpy(e->A.xt + k * nz, z.data(), nz * 4, cudaMemcpyHostToDevice) != cudaSuccess) return PI05_ERR_CUDA;
+        float* dst = (e->noise_chol ? e->A.noise : e->A.xt) + k * nz;
+        if (cudaMemcpy(dst, z.data(), nz * 4, cudaMemcpyHostToDevice) != cudaSuccess) return PI05_ERR_CUDA;
       }
+    }
+    if (!noise && e->noise_chol) {  // correlated noise L . eps for every re-planning slot
+      const long warps = (long)m * nz;
+      correlate_noise_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, e->stream>>>(e->noise_chol, e->A.noise,
+                                                                                        e->A.xt, m, (int)nz);
+      if (cudaGetLastError() != cudaSuccess) return PI05_ERR_CUDA;
     }
     if (!prefill_resident(e, m)) return fail_code(e);
     e->prefix_n = m;
@@ -2505,6 +2513,30 @@ int pi05_act_batch(pi05_engine* e, int n, const int* slots, const pi05_frame* fr
   }
   if (cudaMemcpy(out, rows.data(), rows.size() * 4, cudaMemcpyDefault) != cudaSuccess) return PI05_ERR_CUDA;
   return PI05_OK;
+}
+
+int pi05_set_noise_cholesky(pi05_engine* e, const float* L, int dim) {
+  if (!e) return PI05_ERR_ARG;
+  const int nz = e->cfg.horizon * P5_ACT_D;
+  if (!L) {
+    if (e->noise_chol) {
+      cudaSetDevice(e->device);
+      cudaStreamSynchronize(e->stream);
+      cudaFree(e->noise_chol);
+      e->allocs.erase(std::find(e->allocs.begin(), e->allocs.end(), (void*)e->noise_chol));
+      e->noise_chol = nullptr;
+    }
+    return PI05_OK;
+  }
+  if (dim != nz) {
+    set_err(e, "pi05_set_noise_cholesky: dim must be horizon * 32");
+    return PI05_ERR_ARG;
+  }
+  cudaSetDevice(e->device);
+  if (!e->noise_chol && !dalloc(e, (void**)&e->noise_chol, (size_t)nz * nz * 4)) return PI05_ERR_CUDA;
+  if (cudaMemcpyAsync(e->noise_chol, L, (size_t)nz * nz * 4, cudaMemcpyDefault, e->stream) != cudaSuccess)
+    return PI05_ERR_CUDA;
+  return pi05_sync(e);
 }
 
 int pi05_act(pi05_engine* e, int slot, const pi05_frame* frames, const int32_t* tokens, const float* state,

@@ -269,6 +269,23 @@ __global__ void action_out_euler_kernel(const bf16* h, const bf16* W, const bf16
   pdl_launch_dependents();
 }
 
+// ---------------------------------------------------------------- correlated noise
+// z[k][i] = fp32(sum_{j <= i} L[i][j] eps[k][j]) with a lower-triangular L [dim][dim]: one warp per output, the
+// lanes stride over j and accumulate in fp64 (a fixed-order reduction: reruns are bit-identical, and the fp64
+// sum rounds to the same fp32 as any other fp64 order except at rare ties)
+__global__ void correlate_noise_kernel(const float* L, const float* eps, float* z, int m, int dim) {
+  const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long)m * dim) return;
+  const int k = (int)(w / dim), i = (int)(w % dim);
+  const float* Li = L + (size_t)i * dim;
+  const float* ek = eps + (size_t)k * dim;
+  double acc = 0.0;
+  for (int j = lane; j <= i; j += 32) acc += (double)Li[j] * (double)ek[j];
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) z[(size_t)k * dim + i] = (float)acc;
+}
+
 // ---------------------------------------------------------------- time MLP (fp32, one warp per output)
 // y[s][o] = swish(sum_k x[s][k] W[o][k] + b[o]); optional bf16 copy (input of the bf16 modulation Dense)
 __global__ void linear_swish_f32_kernel(const float* x, const bf16* W, const bf16* b, float* y, bf16* ybf, int S,

@@ -28,6 +28,7 @@ EXPORTS = [
     "pi05_nccl_unique_id", "pi05_lora_attach_nccl", "pi05_lora_world",
     "pi05_read_weights_config", "pi05_lora_schedule_lr", "pi05_lora_get_ema", "pi05_tokenizer_load",
     "pi05_tokenizer_free", "pi05_tokenizer_vocab_size", "pi05_tokenizer_encode", "pi05_tokenize_prompt",
+    "pi05_set_noise_cholesky",
 ]
 
 
@@ -173,6 +174,7 @@ def _load():
     L.pi05_lora_attach_nccl.argtypes = [vp, vp, i32, i32]
     L.pi05_lora_world.argtypes = [vp]
     L.pi05_act.argtypes = [vp, i32, vp, vp, vp, vp, vp]
+    L.pi05_set_noise_cholesky.argtypes = [vp, vp, i32]
     L.pi05_lora_save_state.argtypes = [vp, ctypes.c_char_p]
     L.pi05_lora_load_state.argtypes = [vp, ctypes.c_char_p]
     return L
@@ -447,6 +449,15 @@ class Engine:
         c = ActConfig(act_dim, replan, *[None if k is None else k.ctypes.data for k in keep], noise_seed)
         self._check(lib.pi05_set_act_config(self._h, ctypes.byref(c)))
         self.act_dim = act_dim
+
+    def set_noise_cholesky(self, L=None):
+        """pi05_set_noise_cholesky: correlated re-plan noise L . eps (L lower-triangular [horizon*32]^2), None
+        for uncorrelated noise"""
+        if L is None:
+            self._check(lib.pi05_set_noise_cholesky(self._h, None, 0))
+            return
+        Lc = np.ascontiguousarray(L, np.float32)
+        self._check(lib.pi05_set_noise_cholesky(self._h, Lc.ctypes.data, Lc.shape[0]))
 
     @staticmethod
     def _frames(frames):

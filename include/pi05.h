@@ -282,6 +282,12 @@ PI05_API int pi05_set_act_config(pi05_engine* e, const pi05_act_config* c);
  * is bit-identical to stepping each slot alone with pi05_act. */
 PI05_API int pi05_act_batch(pi05_engine* e, int n, const int* slots, const pi05_frame* frames, const int32_t* tokens,
                             const float* state, const float* noise, float* out);
+/* Correlated noise for the re-plans whose noise the engine draws (pi05_act_batch with noise NULL): each
+ * slot's standard-normal draw eps over the flattened chunk (index t*32 + j) becomes L . eps, L the
+ * lower-triangular [dim][dim] factor of the covariance (dim = horizon * 32; the reference's PiBehavior
+ * model drew N(0, 0.5 I + 0.5 Sigma) with a Cholesky factor computed in f64 at export, π05_네이티브엔진.md:139).
+ * Accumulated in fp64 on the device.  L = NULL returns to uncorrelated noise. */
+PI05_API int pi05_set_noise_cholesky(pi05_engine* e, const float* L, int dim);
 /* pi05_act_batch for one slot (the reference's single-slot pi05_act). */
 PI05_API int pi05_act(pi05_engine* e, int slot, const pi05_frame* frames, const int32_t* tokens, const float* state,
                       const float* noise, float* out);

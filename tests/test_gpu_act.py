@@ -144,3 +144,31 @@ def test_batch_invariant_infer_equals_batch_of_one(pn, depth, n):
         one = eng.infer(im[i:i + 1], tk[i:i + 1], nz[i:i + 1])[0]
         np.testing.assert_array_equal(batch[i], one, err_msg=f"sample {i}")
     eng.close()
+
+
+def test_act_correlated_noise(pn):
+    """pi05_set_noise_cholesky: without caller noise a re-plan draws L . eps (the PiBehavior model's
+    N(0, 0.5 I + 0.5 Sigma) noise, fp64 accumulation on the device): the chunk equals pi05_infer's on the
+    float64 numpy product rounded to float32, bit for bit; clearing L restores plain noise."""
+    eng = pn.Engine(pn.Config.make(**SMALL), max_batch=2)
+    eng.init_random_weights(14)
+    eng.set_act_config(act_dim=32, replan=2, noise_seed=9)
+    dim = 50 * 32
+    rng = np.random.default_rng(15)
+    a = rng.normal(size=(dim, dim)) / np.sqrt(dim)
+    L = np.linalg.cholesky(0.5 * np.eye(dim) + 0.5 * (a @ a.T)).astype(np.float32)
+    eng.set_noise_cholesky(L)
+    im, tk, _ = inputs(pn, 16, [0, 1])
+    eps = np.stack([pn.synth_noise(9, s) for s in (0, 1)]).reshape(2, dim)
+    z = (L.astype(np.float64) @ eps.astype(np.float64).T).T.astype(np.float32).reshape(2, 50, 32)
+    ref = eng.infer(im, tk, z)
+    got = eng.act_batch([0, 1], frames224(im), tk)
+    np.testing.assert_array_equal(got, ref[:, 0, :])
+    eng.set_noise_cholesky(None)
+    eng.reset_slot(0)
+    eng.reset_slot(1)
+    # second plan of each slot: elements [1600, 3200) of its stream, uncorrelated
+    eps2 = np.stack([pn.synth_noise(9, s, horizon=100)[50:] for s in (0, 1)])
+    ref2 = eng.infer(im, tk, eps2)
+    np.testing.assert_array_equal(eng.act_batch([0, 1], frames224(im), tk), ref2[:, 0, :])
+    eng.close()
