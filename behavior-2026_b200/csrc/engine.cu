@@ -139,6 +139,7 @@ struct pi05_engine {
   // verify run (pi05_verify): named intermediate points of sample 0 are copied to the host and passed
   // to probe_fn after the kernels that produce them; null outside a verify run (and during capture)
   pi05_probe_fn probe_fn = nullptr;
+  pi05_plant_fn plant_fn = nullptr;  // teacher-forced verify run: the callback may overwrite the point
   void* probe_ctx = nullptr;
   // single-sample passes at batch position s0 (batch-invariant mode): the bodies offset the per-sample
   // inputs, KV cache and flow state by s0 and share the scratch activations of position 0
@@ -779,24 +780,40 @@ int rows_grid(long rows_warps) { return (int)((rows_warps * 32 + 255) / 256); }
 
 // Verify run: wait for the stream, copy a [rows][cols] bf16 (ld-strided) or fp32 block of sample 0 to
 // the host as fp32 and hand it to the probe callback.
+// In a teacher-forced run the callback may overwrite the values, which are then written back (rounded to
+// bf16 for bf16 points), so the kernels after this point start from them.
 bool emit_bf16(pi05_engine* e, const std::string& name, const bf16* dev, long rows, int cols, int ld) {
-  if (!e->probe_fn) return true;
+  if (!e->probe_fn && !e->plant_fn) return true;
   std::vector<uint16_t> h((size_t)rows * cols);
   CK(cudaMemcpy2DAsync(h.data(), (size_t)cols * 2, dev, (size_t)ld * 2, (size_t)cols * 2, rows,
                        cudaMemcpyDeviceToHost, e->stream));
   CK(cudaStreamSynchronize(e->stream));
   std::vector<float> f(h.size());
   for (size_t i = 0; i < h.size(); ++i) f[i] = p5_bf2f(h[i]);
-  e->probe_fn(name.c_str(), f.data(), (int64_t)f.size(), e->probe_ctx);
+  if (e->probe_fn) {
+    e->probe_fn(name.c_str(), f.data(), (int64_t)f.size(), e->probe_ctx);
+    return true;
+  }
+  e->plant_fn(name.c_str(), f.data(), (int64_t)f.size(), e->probe_ctx);
+  for (size_t i = 0; i < h.size(); ++i) h[i] = p5_f2bf(f[i]);
+  CK(cudaMemcpy2DAsync(const_cast<bf16*>(dev), (size_t)ld * 2, h.data(), (size_t)cols * 2, (size_t)cols * 2, rows,
+                       cudaMemcpyHostToDevice, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
   return true;
 }
 
 bool emit_f32(pi05_engine* e, const std::string& name, const float* dev, long n) {
-  if (!e->probe_fn) return true;
+  if (!e->probe_fn && !e->plant_fn) return true;
   std::vector<float> f((size_t)n);
   CK(cudaMemcpyAsync(f.data(), dev, (size_t)n * 4, cudaMemcpyDeviceToHost, e->stream));
   CK(cudaStreamSynchronize(e->stream));
-  e->probe_fn(name.c_str(), f.data(), (int64_t)n, e->probe_ctx);
+  if (e->probe_fn) {
+    e->probe_fn(name.c_str(), f.data(), (int64_t)n, e->probe_ctx);
+    return true;
+  }
+  e->plant_fn(name.c_str(), f.data(), (int64_t)n, e->probe_ctx);
+  CK(cudaMemcpyAsync(const_cast<float*>(dev), f.data(), (size_t)n * 4, cudaMemcpyHostToDevice, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
   return true;
 }
 
@@ -1021,7 +1038,8 @@ bool fused_rope_applies(pi05_engine* e, int n) {
 // adaRMSNorm folded into the few-token q/k/v and gate/up cluster GEMMs (one 64-token tile)
 bool fused_norm_applies(pi05_engine* e, int n) {
   const int T = n * e->cfg.horizon;
-  return e->fuse_norm && e->cluster_splitk && T <= 64 && P5_EXP_W % 32 == 0;
+  // a teacher-forced run replaces the residual stream after the kernels that emit its sums of squares
+  return e->fuse_norm && e->cluster_splitk && T <= 64 && P5_EXP_W % 32 == 0 && !e->plant_fn;
 }
 
 // Buffers and tensor-map table of the persistent denoise.  Runs outside stream capture.
@@ -1122,7 +1140,7 @@ bool run_denoise_mega(pi05_engine* e) {
 }
 
 bool run_denoise_body(pi05_engine* e, int n) {
-  if (mega_applies(e, n) && !e->probe_fn && e->s0 == 0) return run_denoise_mega(e);
+  if (mega_applies(e, n) && !e->probe_fn && !e->plant_fn && e->s0 == 0) return run_denoise_mega(e);
   const int H = e->cfg.horizon, T = n * H, D = P5_EXP_W, P = e->P;
   Acts& A = e->A;
   float* xt = A.xt + (size_t)e->s0 * H * P5_ACT_D;
@@ -1252,7 +1270,7 @@ bool run_denoise_body(pi05_engine* e, int n) {
     // the verify run also keeps the velocity v (A.actions is otherwise unused scratch of this size)
     if (!launch(e, action_out_euler_kernel, dim3(rows_grid((long)T * P5_ACT_D)), dim3(256), 0, true,
                 (const bf16*)A.eh, (const bf16*)e->aout_w, (const bf16*)e->aout_b, xt,
-                e->probe_fn ? A.actions : (float*)nullptr, T, D, dtb))
+                (e->probe_fn || e->plant_fn) ? A.actions : (float*)nullptr, T, D, dtb))
       return false;
     if (!emit_f32(e, sp + ".v", A.actions, (long)H * P5_ACT_D) || !emit_f32(e, sp + ".x", xt, (long)H * P5_ACT_D))
       return false;
@@ -2033,8 +2051,12 @@ int pi05_infer(pi05_engine* e, int n, const uint8_t* images, const int32_t* toke
   return pi05_denoise(e, n, noise, actions);
 }
 
-int pi05_verify(pi05_engine* e, const uint8_t* images, const int32_t* tokens, const float* noise, float* actions,
-                pi05_probe_fn fn, void* ctx) {
+}  // extern "C"
+
+namespace {
+
+int verify_run(pi05_engine* e, const uint8_t* images, const int32_t* tokens, const float* noise, float* actions,
+               pi05_probe_fn probe, pi05_plant_fn plant, void* ctx) {
   if (!e) return PI05_ERR_ARG;
   if (!images || (e->cfg.n_text > 0 && !tokens) || !noise) {
     e->err = "pi05_verify: bad arguments";
@@ -2050,17 +2072,34 @@ int pi05_verify(pi05_engine* e, const uint8_t* images, const int32_t* tokens, co
   if (e->cfg.n_text > 0 && !copy_in(e, e->A.tokens, tokens, (size_t)e->cfg.n_text * 4)) return PI05_ERR_CUDA;
   if (!copy_in(e, e->A.xt, noise, ab)) return PI05_ERR_CUDA;
   if (!qkv_interleave_prepare(e)) return fail_code(e);
-  e->probe_fn = fn;
+  e->probe_fn = probe;
+  e->plant_fn = plant;
   e->probe_ctx = ctx;
   bool ok = run_prefill_body(e, 1);
   if (ok) e->prefix_n = 1;
   ok = ok && run_denoise_body(e, 1);
   e->probe_fn = nullptr;
+  e->plant_fn = nullptr;
   e->probe_ctx = nullptr;
   if (!ok) return fail_code(e);
   if (actions && cudaMemcpyAsync(actions, e->A.xt, ab, cudaMemcpyDefault, e->stream) != cudaSuccess)
     return PI05_ERR_CUDA;
   return pi05_sync(e);
+}
+
+}  // namespace
+
+extern "C" {
+
+int pi05_verify(pi05_engine* e, const uint8_t* images, const int32_t* tokens, const float* noise, float* actions,
+                pi05_probe_fn fn, void* ctx) {
+  return verify_run(e, images, tokens, noise, actions, fn, nullptr, ctx);
+}
+
+int pi05_verify_planted(pi05_engine* e, const uint8_t* images, const int32_t* tokens, const float* noise,
+                        float* actions, pi05_plant_fn fn, void* ctx) {
+  if (!fn) return PI05_ERR_ARG;
+  return verify_run(e, images, tokens, noise, actions, nullptr, fn, ctx);
 }
 
 // kernels per call, as captured (for launch accounting in benchmarks)

@@ -28,7 +28,7 @@ EXPORTS = [
     "pi05_nccl_unique_id", "pi05_lora_attach_nccl", "pi05_lora_world",
     "pi05_read_weights_config", "pi05_lora_schedule_lr", "pi05_lora_get_ema", "pi05_tokenizer_load",
     "pi05_tokenizer_free", "pi05_tokenizer_vocab_size", "pi05_tokenizer_encode", "pi05_tokenize_prompt",
-    "pi05_set_noise_cholesky",
+    "pi05_set_noise_cholesky", "pi05_verify_planted",
 ]
 
 
@@ -90,6 +90,7 @@ def lora_schedule_lr(config, k):
 
 
 PROBE = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float), ctypes.c_int64, ctypes.c_void_p)
+PLANT = PROBE  # same C signature; the data of a teacher-forced run may be written
 
 
 def _load():
@@ -161,6 +162,7 @@ def _load():
     L.pi05_op_bench_linear.argtypes = [vp, i32, i32, i32, i32, i32, P(ctypes.c_float)]
     L.pi05_lora_reset_optimizer.argtypes = [vp]
     L.pi05_verify.argtypes = [vp, vp, vp, vp, vp, PROBE, vp]
+    L.pi05_verify_planted.argtypes = [vp, vp, vp, vp, vp, PLANT, vp]
     L.pi05_set_act_config.argtypes = [vp, P(ActConfig)]
     L.pi05_nccl_unique_id.argtypes = [vp]
     L.pi05_read_weights_config.argtypes = [ctypes.c_char_p, cfg]
@@ -326,6 +328,32 @@ class Engine:
         pn, kn = _ptr(noise, np.float32)
         self._check(lib.pi05_verify(self._h, pi, pt, pn, out.ctypes.data, cb, None))
         return out, points
+
+    def verify_planted(self, images, tokens, noise, plant, keep=None):
+        """Teacher-forced verify run (pi05_verify_planted): at every point named in `plant` ({name: array}) the
+        engine's own value is recorded and then replaced by the planted one, so the next layer starts from it.
+        Returns (actions, {name: the engine's value before planting, for planted points; the emitted value
+        for other points whose names start with one of `keep`})."""
+        seen = {}
+
+        def on(name, data, n, _ctx):
+            name = name.decode()
+            arr = np.ctypeslib.as_array(data, shape=(n,))
+            if name in plant:
+                seen[name] = arr.copy()
+                src = np.ascontiguousarray(plant[name], np.float32).reshape(-1)
+                assert src.size == n, (name, src.size, n)
+                arr[:] = src
+            elif keep is not None and any(name.startswith(k) for k in keep):
+                seen[name] = arr.copy()
+
+        cb = PLANT(on)
+        out = np.empty((self.config.horizon, 32), np.float32)
+        pi, ki = _ptr(images, np.uint8)
+        pt, kt = _ptr(tokens, np.int32)
+        pn_, kn = _ptr(noise, np.float32)
+        self._check(lib.pi05_verify_planted(self._h, pi, pt, pn_, out.ctypes.data, cb, None))
+        return out, seen
 
     # -- hot operators on device tensors (asynchronous on the engine stream)
     EPI = {"store": 0, "gelu": 1, "resid": 2, "gated": 3, "geglu": 4, "f32": 5}

@@ -110,6 +110,15 @@ PI05_API int pi05_infer(pi05_engine* e, int n, const uint8_t* images, const int3
 typedef void (*pi05_probe_fn)(const char* name, const float* data, int64_t n, void* ctx);
 PI05_API int pi05_verify(pi05_engine* e, const uint8_t* images, const int32_t* tokens, const float* noise,
                          float* actions, pi05_probe_fn fn, void* ctx);
+/* Teacher-forced verify run (the reference verifier's one-layer mode, π05_네이티브엔진.md:53-56): as
+ * pi05_verify, but `fn` may overwrite `data`; the values (rounded to bf16 for bf16 points) replace the
+ * engine's before the next kernel reads them, so planting a reference's layer outputs (img.l<N>.out,
+ * img.tokens, pre.l<N>.out, suf.s<S>.l<N>.out, suf.s<S>.x) makes every layer start from the reference's
+ * input and shows each layer's own error.  The adaRMSNorm of the denoise runs as a separate kernel in
+ * this mode (its fused form reads statistics made before the planting point). */
+typedef void (*pi05_plant_fn)(const char* name, float* data, int64_t n, void* ctx);
+PI05_API int pi05_verify_planted(pi05_engine* e, const uint8_t* images, const int32_t* tokens, const float* noise,
+                                 float* actions, pi05_plant_fn fn, void* ctx);
 
 /* Stream and synchronisation. */
 PI05_API void* pi05_stream(pi05_engine* e);  /* cudaStream_t of the engine */
