@@ -42,6 +42,7 @@ struct AttnArgs {
   float* lse;       // optional (splits == 1): log-sum-exp per row, [b * lse_b + row]
   long lse_b;
   int force_splits; // > 0: the tensor-core path uses this many key splits instead of choosing
+  const int* valid1; // optional (tensor-core path): batch item b attends to the first valid1[b] keys of segment 1
 };
 
 template <int HD, int NW = 4>

@@ -68,10 +68,13 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = z / a.splits, split = z % a.splits;
-  const int n1 = (a.len1 + C::KT - 1) / C::KT, n2 = (a.len2 + C::KT - 1) / C::KT;
+  // keys of segment 1 this batch item attends to (a padded prompt's tail is left out): the key tiles past
+  // them are skipped, so the item's tile list is [segment-1 tiles with keys | segment-2 tiles]
+  const int len1 = a.valid1 ? max(0, min(a.len1, a.valid1[b])) : a.len1;
+  const int n1 = (len1 + C::KT - 1) / C::KT, n2 = (a.len2 + C::KT - 1) / C::KT;
   const int tps = a.keys_per_split / C::KT;
   const int t0 = split * tps;
-  const int n = max(0, min(n1 + n2, t0 + tps) - t0);
+  const int n = max(0, min(n1 + n2, t0 + tps) - t0);  // 0: an empty split (partial m = -inf, l = 0, O = 0)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -102,7 +105,7 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
   auto tile_of = [&](int t, int& seg, int& row0, int& valid) {
     seg = t < n1 ? 0 : 1;
     row0 = (seg == 0 ? t : t - n1) * C::KT;
-    valid = min(C::KT, (seg == 0 ? a.len1 : a.len2) - row0);
+    valid = min(C::KT, (seg == 0 ? len1 : a.len2) - row0);
   };
 
   if (warp == 0) {
@@ -297,7 +300,9 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
     if (a.pdl) pdl_wait();
     const int rows_total = a.T * 8;
     const int row = rb * C::ROWS + r;
-    const bool store = __all_sync(0xffffffffu, done && alive && n > 0) && row < rows_total;
+    // an empty split stores its neutral partial (the merge gives it weight 0); otherwise n > 0
+    const bool empty = n == 0 && a.splits > 1;
+    const bool store = __all_sync(0xffffffffu, done && alive && (n > 0 || empty)) && row < rows_total;
     const int tok = row >> 3, hq = row & 7;
     const float inv = l_tot > 0.f ? 1.0f / l_tot : 0.f;
     const long base = (long)z * rows_total + row;
@@ -307,6 +312,10 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
       __syncwarp();
       tmem_ld32(t_o + (uint32_t)c, o);
       tmem_wait_ld();
+      if (empty) {  // no MMA wrote this accumulator
+#pragma unroll
+        for (int k = 0; k < 32; ++k) o[k] = 0u;
+      }
       const int col = g * (C::HD / 2) + c;
       if (!store) {
       } else if (a.splits == 1) {

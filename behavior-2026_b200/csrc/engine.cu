@@ -141,6 +141,9 @@ struct pi05_engine {
   pi05_probe_fn probe_fn = nullptr;
   pi05_plant_fn plant_fn = nullptr;  // teacher-forced verify run: the callback may overwrite the point
   void* probe_ctx = nullptr;
+  // prompt padding mask (cfg.text_pad_mask): per batch position, the number of prefix tokens before the
+  // prompt's trailing padding (ids 0) -- the keys attended to, and the first position of the action tokens
+  int* d_valid = nullptr;
   // single-sample passes at batch position s0 (batch-invariant mode): the bodies offset the per-sample
   // inputs, KV cache and flow state by s0 and share the scratch activations of position 0
   int s0 = 0;
@@ -337,6 +340,7 @@ struct Lin {
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
   int rope_pos_off = 0, rope_per_sample = 1, rope_ld_kv = 0;
+  const int* rope_base = nullptr;
   bf16* rope_k = nullptr;
   bf16* rope_v = nullptr;
   // fused adaRMSNorm of x (few-token cluster path; see GemmArgs nrm_*) and sum-of-squares partials out
@@ -596,6 +600,7 @@ bool linear(pi05_engine* e, const Lin& L) {
   ga.rope_cos = L.rope_cos;
   ga.rope_sin = L.rope_sin;
   ga.rope_pos_off = L.rope_pos_off;
+  ga.rope_base = L.rope_base;
   ga.rope_per_sample = L.rope_per_sample;
   ga.rope_ld_kv = L.rope_ld_kv;
   ga.rope_k = L.rope_k;
@@ -732,6 +737,7 @@ bool attention_tc(pi05_engine* e, const AttnArgs& a0, int batch) {
 
 bool attention(pi05_engine* e, const AttnArgs& a0, int batch, int hd) {
   if (hd == P5_HD && a0.G == 8 && a0.qdiv == 1.0f && e->attn_tc && a0.len1 > 0) return attention_tc(e, a0, batch);
+  if (a0.valid1) return set_err(e, "the prompt padding mask needs the tensor-core attention (PI05_ATTN_TC=1)");
   // SigLIP: one CTA per (128 queries, head, image) on tcgen05 up to 32 images; measured per call (CUDA events,
   // 20 launches): 3 images 9.7 vs 14.5 us, 24 images 51.4 vs 55.5 us, 48 images 111.7 vs 101.3 us, 192 images
   // 422.8 vs 378.2 us for the tcgen05 and the mma.sync kernel, so the larger batches take the mma.sync kernel
@@ -956,6 +962,7 @@ bool run_gemma(pi05_engine* e, int n) {
     at.G = P5_NH;
     at.qdiv = 1.0f;
     at.splits = 1;
+    at.valid1 = e->cfg.text_pad_mask ? e->d_valid + e->s0 : nullptr;
     if (!attention(e, at, n, P5_HD)) return false;
     Lin o{A.po, P5_QDIM, T, g.wo, P5_QDIM, D, P5_QDIM};
     o.epi = EPI_RESID;
@@ -986,6 +993,11 @@ bool run_gemma(pi05_engine* e, int n) {
 }
 
 bool run_prefill_body(pi05_engine* e, int n) {
+  if (e->cfg.text_pad_mask &&
+      !launch(e, text_valid_kernel, dim3((n + 127) / 128), dim3(128), 0, false,
+              (const int32_t*)e->A.tokens + (size_t)e->s0 * e->cfg.n_text, n, e->cfg.n_text,
+              e->cfg.n_cameras * P5_SIG_TOK, e->d_valid + e->s0))
+    return false;
   if (!run_siglip(e, n)) return false;
   if (e->cfg.n_text > 0 &&
       !launch(e, embed_text_kernel, dim3(e->cfg.n_text, n), dim3(256), 0, true,
@@ -1140,7 +1152,8 @@ bool run_denoise_mega(pi05_engine* e) {
 }
 
 bool run_denoise_body(pi05_engine* e, int n) {
-  if (mega_applies(e, n) && !e->probe_fn && !e->plant_fn && e->s0 == 0) return run_denoise_mega(e);
+  if (mega_applies(e, n) && !e->probe_fn && !e->plant_fn && e->s0 == 0 && !e->cfg.text_pad_mask)
+    return run_denoise_mega(e);
   const int H = e->cfg.horizon, T = n * H, D = P5_EXP_W, P = e->P;
   Acts& A = e->A;
   float* xt = A.xt + (size_t)e->s0 * H * P5_ACT_D;
@@ -1189,6 +1202,7 @@ bool run_denoise_body(pi05_engine* e, int n) {
         q.rope_sin = e->d_sin;
         q.rope_pos_off = P;
         q.rope_per_sample = H;
+        if (e->cfg.text_pad_mask) q.rope_base = e->d_valid + e->s0;  // action tokens follow the real prompt
         q.rope_ld_kv = P5_HD;
         q.rope_k = A.ek;
         q.rope_v = A.ev;
@@ -1198,6 +1212,8 @@ bool run_denoise_body(pi05_engine* e, int n) {
         q.out = A.eqkv;
         q.ld_out = P5_QKV;
         if (!linear(e, q)) return false;
+        if (e->cfg.text_pad_mask)
+          return set_err(e, "the prompt padding mask needs the fused RoPE projections (PI05_CLUSTER_SPLITK=1)");
         if (!launch(e, rope_qkv_kernel, dim3(T), dim3(256), 0, true, A.eqkv, T, H, P, A.ek, A.ev,
                     (const float*)e->d_cos, (const float*)e->d_sin, 256))
           return false;
@@ -1223,6 +1239,7 @@ bool run_denoise_body(pi05_engine* e, int n) {
       at.G = P5_NH;
       at.qdiv = 1.0f;
       at.splits = attn_splits;
+      at.valid1 = e->cfg.text_pad_mask ? e->d_valid + e->s0 : nullptr;
       if (!attention(e, at, n, P5_HD)) return false;
       Lin o{A.eo, P5_QDIM, T, x.wo, P5_QDIM, D, P5_QDIM};
       o.epi = EPI_GATED;
@@ -1360,6 +1377,13 @@ bool denoise_resident(pi05_engine* e, int n) {
     e->s0 = 0;
     if (!ok) return false;
   }
+  return true;
+}
+
+// A prefix cache installed directly (not by a prefill) has no padding: every key of it is attended to.
+bool set_valid_full(pi05_engine* e, int n) {
+  std::vector<int> v(n, e->P);
+  CK(cudaMemcpy(e->d_valid, v.data(), n * sizeof(int), cudaMemcpyHostToDevice));
   return true;
 }
 
@@ -1595,6 +1619,7 @@ bool create(pi05_engine* e) {
   if (!al((void**)&e->attn_ws_o, e->attn_ws_rows * P5_HD * 4) || !al((void**)&e->attn_ws_ml, e->attn_ws_rows * 2 * 4))
     return false;
   if (!al((void**)&e->d_status, 64)) return false;
+  if (!al((void**)&e->d_valid, (size_t)B * sizeof(int))) return false;
   if (!al((void**)&e->nrm_ss, (size_t)2 * (P5_EXP_W / 16) * 64 * 4)) return false;
   CK(cudaStreamSynchronize(e->stream));
   return true;
@@ -1610,6 +1635,7 @@ extern "C" {
 void pi05_default_config(pi05_config* c) {
   if (!c) return;
   c->batch_invariant = 0;
+  c->text_pad_mask = 0;
   c->siglip_layers = 27;
   c->gemma_layers = 18;
   c->expert_layers = 18;
@@ -1629,7 +1655,8 @@ pi05_engine* pi05_create(const pi05_config* c, int device, int max_batch, char* 
   if (c) cfg = *c;
   if (cfg.siglip_layers < 0 || cfg.gemma_layers < 1 || cfg.expert_layers != cfg.gemma_layers || cfg.num_steps < 1 ||
       cfg.n_cameras < 1 || cfg.n_text < 0 || cfg.horizon < 1 || cfg.horizon > 128 || max_batch < 1 ||
-      (cfg.batch_invariant != 0 && cfg.batch_invariant != 1) || max_batch > 32767)
+      (cfg.batch_invariant != 0 && cfg.batch_invariant != 1) || (cfg.text_pad_mask != 0 && cfg.text_pad_mask != 1) ||
+      max_batch > 32767)
     return fail("pi05_create: invalid configuration");
   pi05_engine* e = new pi05_engine();
   e->cfg = cfg;
@@ -1993,6 +2020,7 @@ int pi05_set_prefix_cache(pi05_engine* e, int n, const uint16_t* k, const uint16
         return PI05_ERR_CUDA;
     }
   if (!is_device_ptr(k) && cudaStreamSynchronize(e->stream) != cudaSuccess) return PI05_ERR_CUDA;
+  if (!set_valid_full(e, n)) return PI05_ERR_CUDA;
   e->prefix_n = n;
   return PI05_OK;
 }
@@ -2014,6 +2042,7 @@ int pi05_synth_prefix_cache(pi05_engine* e, int n, uint64_t seed) {
                                                           (long)(l * per));
     }
   }
+  if (!set_valid_full(e, n)) return PI05_ERR_CUDA;
   e->prefix_n = n;
   return cudaGetLastError() == cudaSuccess ? PI05_OK : PI05_ERR_CUDA;
 }

@@ -71,13 +71,15 @@ struct GemmArgs {
   // (2048 | 256 | 256); 2 interleaved gate/up rows (a = m % 2, r_a = m / 2).
   int lg_mode, lg_trans, lg_K;
   long lg_off[3];
-  // EPI_ROPE: token t sits at position rope_pos_off + t % rope_per_sample.  Head blocks 0..7 (q):
+  // EPI_ROPE: token t sits at position rope_pos_off + t % rope_per_sample (rope_base[t / rope_per_sample]
+  //   + t % rope_per_sample when rope_base is set).  Head blocks 0..7 (q):
   //   out[t][hb*256 + j], [.. + 128] = R(R(rope) / 16); block 8 (k): rope_k[t][j], [j+128] = R(rope);
   //   block 9 (v): rope_v[t][j], [j+128] = R(v).  rope(x1, x2) = (x1 cos - x2 sin, x2 cos + x1 sin),
   //   x1 = R(acc of dim j), x2 = R(acc of dim j+128), cos/sin tables [pos][128].
   const float* rope_cos;
   const float* rope_sin;
   int rope_pos_off, rope_per_sample, rope_ld_kv;
+  const int* rope_base;  // optional: sample s's first position is rope_base[s] instead of rope_pos_off
   bf16* rope_k;
   bf16* rope_v;
   // Fused adaRMSNorm of the few-token operand (swap cluster kernel, 64-token tiles): the B tiles hold the
@@ -158,7 +160,8 @@ __device__ __forceinline__ void epi_row32(const GemmArgs& a, float (&v)[32], int
           hi[p] = pack_bf2(v[4 * p + 1], v[4 * p + 3]);
         }
       } else {
-        const size_t ci = (size_t)(a.rope_pos_off + t % a.rope_per_sample) * 128 + j0;
+        const int p0 = a.rope_base ? a.rope_base[t / a.rope_per_sample] : a.rope_pos_off;
+        const size_t ci = (size_t)(p0 + t % a.rope_per_sample) * 128 + j0;
         float cs[16], sn[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -645,7 +648,8 @@ __device__ __forceinline__ void swap_epi_load(const GemmArgs& a, int f, int t0, 
   for (int q = 0; q < 4; ++q) {
     const int tc = min(t0 + q, a.N - 1);
     if (EPI == EPI_ROPE) {  // res, gate carry cos, sin of the token's position for this row pair
-      const size_t ci = (size_t)(a.rope_pos_off + tc % a.rope_per_sample) * 128 + ((fc & 255) >> 1);
+      const int p0 = a.rope_base ? a.rope_base[tc / a.rope_per_sample] : a.rope_pos_off;
+      const size_t ci = (size_t)(p0 + tc % a.rope_per_sample) * 128 + ((fc & 255) >> 1);
       o.res[q] = a.rope_cos[ci];
       o.gate[q] = a.rope_sin[ci];
     } else {

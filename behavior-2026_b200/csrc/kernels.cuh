@@ -269,6 +269,18 @@ __global__ void action_out_euler_kernel(const bf16* h, const bf16* W, const bf16
   pdl_launch_dependents();
 }
 
+// ---------------------------------------------------------------- prompt padding
+// valid[b] = image tokens + the prompt up to its last non-padding id (openpi pads prompts with id 0 and
+// masks the padding); a prompt of padding only keeps its first token
+__global__ void text_valid_kernel(const int32_t* tokens, int n, int n_text, int n_img_tokens, int* valid) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= n) return;
+  const int32_t* t = tokens + (size_t)b * n_text;
+  int len = n_text;
+  while (len > 1 && t[len - 1] == 0) --len;
+  valid[b] = n_img_tokens + len;
+}
+
 // ---------------------------------------------------------------- correlated noise
 // z[k][i] = fp32(sum_{j <= i} L[i][j] eps[k][j]) with a lower-triangular L [dim][dim]: one warp per output, the
 // lanes stride over j and accumulate in fp64 (a fixed-order reduction: reruns are bit-identical, and the fp64

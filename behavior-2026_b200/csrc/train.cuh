@@ -840,6 +840,10 @@ int pi05_lora_init(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
   pi05_lora_config cfg;
   pi05_lora_default_config(&cfg);
   if (c) cfg = *c;
+  if (e->cfg.text_pad_mask) {
+    e->err = "pi05_lora_init: the LoRA step trains on full prompts (text_pad_mask must be 0)";
+    return PI05_ERR_ARG;
+  }
   if (cfg.rank != 16 || cfg.alpha != 32.0f || cfg.micro_batch < 1) {
     e->err = "pi05_lora_init: this build implements rank 16, alpha 32";
     return PI05_ERR_ARG;

@@ -58,6 +58,12 @@ typedef struct {
    * 0 (default): batches run as one GEMM/attention problem each, for throughput; per-sample results
    * then differ from the batch-of-one results in the last bits (different tilings and sum orders). */
   int32_t batch_invariant;
+  /* 1: a prompt shorter than n_text is padded with id 0 (openpi's padding, pi05_tokenize_prompt's output)
+   * and masked as openpi masks it: no query attends to the padding, and the action tokens' RoPE positions
+   * follow the last real token; each sample's length is read from its tokens on the device.  0 (default):
+   * all n_text prompt positions are attended to (the benchmarks' full 200-token prompts).  Inference only
+   * (pi05_lora_init refuses it), and it needs the tensor-core attention and the fused RoPE projections. */
+  int32_t text_pad_mask;
 } pi05_config;
 
 PI05_API void pi05_default_config(pi05_config* c);

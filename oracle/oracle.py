@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(HERE, "libpi05_oracle.so")
 # generator stream ids (behavior-2026_b200/csrc/pi05_model.h)
 K_IN_IMAGE, K_IN_TOKENS, K_IN_NOISE, K_IN_KCACHE, K_IN_VCACHE, K_IN_ACTIONS, K_IN_TRAIN_NOISE = range(120, 127)
 FP32_ACTIVATIONS = 1
+TEXT_PAD_MASK = 2  # trailing prompt ids 0 are padding, masked as openpi masks it
 HD = 256
 GEM_W = 2048
 
@@ -60,6 +61,7 @@ def lib():
         L.p5o_denoise.argtypes = [cfg, ctypes.c_uint64, f32, f32, ctypes.c_int, f32, f32, ctypes.c_int, PROBE,
                                   ctypes.c_void_p]
         L.p5o_prefix_embed.argtypes = [cfg, ctypes.c_uint64, u8, i32, f32, ctypes.c_int]
+        L.p5o_valid_prefix.argtypes = [cfg, i32, ctypes.c_int]
         L.p5o_gen_images.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, u8]
         L.p5o_gen_tokens.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, i32]
         L.p5o_gen_normal.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_double,
@@ -194,6 +196,12 @@ def denoise(cfg, seed, kcache, vcache, noise, flags=0, probe=None):
     return out
 
 
+def valid_prefix(cfg, tokens, flags=0):
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    return lib().p5o_valid_prefix(ctypes.byref(cfg), _p(tokens, ctypes.c_int32), flags)
+
+
 def infer(cfg, seed, images, tokens, noise, flags=0, probe=None):
     k, v = prefill(cfg, seed, images, tokens, flags, probe)
-    return denoise(cfg, seed, k, v, noise, flags, probe)
+    s = valid_prefix(cfg, tokens, flags)  # with TEXT_PAD_MASK the padding's cache rows are left out
+    return denoise(cfg, seed, k[:, :s], v[:, :s], noise, flags, probe)

@@ -278,7 +278,9 @@ void siglip(const p5o_config* c, uint64_t seed, const uint8_t* images, float* ou
 }
 
 // ---------------------------------------------------------------- Gemma-2B prefix prefill
-void prefill(const p5o_config* c, uint64_t seed, Vf& x, int P, float* kc, float* vc, const Run& r) {
+// keys: every query attends to the first S of the P prefix tokens (S < P: a padded prompt's tail masked)
+void prefill(const p5o_config* c, uint64_t seed, Vf& x, int P, float* kc, float* vc, const Run& r, int S = -1) {
+  if (S < 0) S = P;
   const int D = P5_GEM_W, F = P5_GEM_MLP;
   Rope rp(P);
   Vf h((size_t)P * D), q((size_t)P * P5_QDIM), kk((size_t)P * P5_HD), vv((size_t)P * P5_HD), o((size_t)P * P5_QDIM),
@@ -300,7 +302,7 @@ void prefill(const p5o_config* c, uint64_t seed, Vf& x, int P, float* kc, float*
     r.point("pre.l" + std::to_string(l) + ".k", kk.data(), kk.size());
     r.point("pre.l" + std::to_string(l) + ".v", vv.data(), vv.size());
     if (l == c->gemma_layers - 1) break;  // the last layer's output feeds only the unused final norm
-    attention(r, P, P, P5_NH, P5_HD, q.data(), P5_QDIM, kk.data(), P5_HD, vv.data(), P5_HD, false, o.data(), P5_QDIM);
+    attention(r, P, S, P5_NH, P5_HD, q.data(), P5_QDIM, kk.data(), P5_HD, vv.data(), P5_HD, false, o.data(), P5_QDIM);
     linear(r, P, D, P5_QDIM, o.data(), wo.data(), nullptr, y.data());
     for (size_t i = 0; i < x.size(); ++i) x[i] = r.R(x[i] + y[i]);
     wq.clear(); wq.shrink_to_fit();
@@ -499,6 +501,14 @@ int p5o_prefix_embed(const p5o_config* c, uint64_t seed, const uint8_t* images, 
   return 0;
 }
 
+int p5o_valid_prefix(const p5o_config* c, const int32_t* tokens, int flags) {
+  const int P = P5_SIG_TOK * c->n_cameras + c->n_text;
+  if (!(flags & P5O_TEXT_PAD_MASK)) return P;
+  int len = c->n_text;  // openpi pads prompts with id 0 and masks the padding
+  while (len > 1 && tokens[len - 1] == 0) --len;
+  return P5_SIG_TOK * c->n_cameras + len;
+}
+
 int p5o_prefill(const p5o_config* c, uint64_t seed, const uint8_t* images, const int32_t* tokens, float* kcache,
                 float* vcache, int flags, p5o_probe_fn probe, void* ctx) {
   if (!check(c)) return -1;
@@ -508,7 +518,7 @@ int p5o_prefill(const p5o_config* c, uint64_t seed, const uint8_t* images, const
   siglip(c, seed, images, x.data(), r);
   embed_text(c, seed, tokens, x.data() + (size_t)P5_SIG_TOK * c->n_cameras * P5_GEM_W, r);
   r.point("txt.emb", x.data() + (size_t)P5_SIG_TOK * c->n_cameras * P5_GEM_W, (size_t)c->n_text * P5_GEM_W);
-  prefill(c, seed, x, P, kcache, vcache, r);
+  prefill(c, seed, x, P, kcache, vcache, r, p5o_valid_prefix(c, tokens, flags));
   return 0;
 }
 

@@ -27,7 +27,10 @@ typedef struct {
   int32_t n_cameras, n_text, horizon;
 } p5o_config;
 
-enum { P5O_FP32_ACTIVATIONS = 1 };
+/* P5O_TEXT_PAD_MASK: a prompt's trailing ids 0 are padding, masked as openpi masks it: p5o_prefill's
+ * queries attend to the first p5o_valid_prefix() keys only, and the denoise is then run on that many
+ * cache rows (its action tokens' positions follow them). */
+enum { P5O_FP32_ACTIVATIONS = 1, P5O_TEXT_PAD_MASK = 2 };
 
 /* Named intermediate points (names follow the reference verifier: img.tokens, pre.lN.k, suf.sN.v, ...). */
 typedef void (*p5o_probe_fn)(const char* name, const float* data, int64_t n, void* ctx);
@@ -45,6 +48,8 @@ void p5o_gen_param_at(uint64_t seed, int kind, int sub, int64_t first, int64_t n
 /* images: [n_cameras][224][224][3] uint8; out: [n_cameras*256][2048] */
 int p5o_siglip(const p5o_config* c, uint64_t seed, const uint8_t* images, float* img_tokens, int flags,
                p5o_probe_fn probe, void* ctx);
+/* prefix tokens attended to: P, or with P5O_TEXT_PAD_MASK the image tokens + the prompt before its padding */
+int p5o_valid_prefix(const p5o_config* c, const int32_t* tokens, int flags);
 /* full prefix: kcache/vcache [gemma_layers][P][256], P = 256*n_cameras + n_text */
 int p5o_prefill(const p5o_config* c, uint64_t seed, const uint8_t* images, const int32_t* tokens,
                 float* kcache, float* vcache, int flags, p5o_probe_fn probe, void* ctx);
