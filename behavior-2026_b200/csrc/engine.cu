@@ -118,6 +118,7 @@ struct pi05_engine {
   // few-token denoise: adaRMSNorm folded into the q/k/v and gate/up cluster GEMMs, fed by per-token
   // sum-of-squares partials from the producers of x (PI05_FUSE_NORM=0: separate rmsnorm launches)
   bool fuse_norm = true;
+  bool fuse_geglu_bwd = true;  // LoRA: GeGLU backward in the down projection's dX epilogue (PI05_FUSE_GEGLU_BWD=0: separate)
   // receding-horizon stepping (pi05_act_batch): per slot the last post-processed chunk [horizon][act_dim],
   // the next row to execute and the plans made (offset of the slot's noise stream)
   int act_dim = P5_ACT_D, act_replan = 16;
@@ -390,6 +391,8 @@ bool launch_gemm_bn(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb
     case EPI_GEGLU: return launch(e, gemm_tc_kernel<BN, EPI_GEGLU>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
     case EPI_ROPE: return launch(e, gemm_tc_kernel<BN, EPI_ROPE>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
     case EPI_F32: return launch(e, gemm_tc_kernel<BN, EPI_F32>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
+    case EPI_GEGLU_BWD:
+      return launch(e, gemm_tc_kernel<BN, EPI_GEGLU_BWD>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
     default: return launch(e, gemm_tc_kernel<BN, EPI_STORE>, grid, dim3(256), sm, ga.pdl != 0, ta, tb, ga);
   }
 }
@@ -482,6 +485,7 @@ bool set_gemm_smem(pi05_engine* e) {
   CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_GEGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_GEGLU_BWD>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
   return true;
 }
 
@@ -494,7 +498,9 @@ int wide_swap_split(pi05_engine* e, const Lin& L) {
                       L.epi == EPI_GEGLU || L.epi == EPI_F32 || L.epi == EPI_ROPE;
   // measured: it pays for long K only (SigLIP fc2 K=4304: 26.8 -> 22.0 µs; Gemma down K=16384: 78.3 -> 74.7 µs),
   // and loses for K <= 2048 (the 128x256 partial tiles' DSMEM reduce costs more than the shorter K loop saves)
-  if (!e->wide_swap || !e->cluster_splitk || L.T <= 128 || L.amn || !epi_ok || L.addend || L.out_t || kt < 64) return 0;
+  if (!e->wide_swap || !e->cluster_splitk || L.T <= 128 || L.amn || !epi_ok || L.addend || L.out_t || kt < 64 ||
+      L.epi == EPI_GEGLU_BWD)
+    return 0;
   const int t256 = ((L.T + 127) / 128) * ((L.F + 255) / 256);
   if (t256 >= e->num_sms / 2) return 0;
   const int tiles = ((L.F + 127) / 128) * ((L.T + 255) / 256);
@@ -640,9 +646,11 @@ bool linear(pi05_engine* e, const Lin& L) {
     }
   }
   if (L.epi == EPI_ROPE && swap) return set_err(e, "fused RoPE epilogue: few-token projection without a cluster split");
+  if (L.epi == EPI_GEGLU_BWD && (swap || L.F % 32 || BN < 64))
+    return set_err(e, "fused GeGLU backward: normal orientation and F % 32 == 0 only");
   if (fused_nrm) return set_err(e, "fused adaRMSNorm / sum-of-squares output: not a few-token cluster projection");
   if (!swap && BN == 256 && splits == 1 && !L.amn && e->gemm_wide && L.epi != EPI_STORE_T && L.epi != EPI_LORA_GRAD &&
-      kt >= 64) {
+      L.epi != EPI_GEGLU_BWD && kt >= 64) {
     // at least a full wave of 256x256 tiles and K >= 4096: the wider tile loads a third fewer bytes per
     // MAC, but its single accumulator set leaves the epilogue unoverlapped, which only a long K loop
     // amortises (measured: Gemma down 3.67 -> 3.20 ms, SigLIP fc2 550 -> 451 µs at bs64; K = 2048
@@ -1550,6 +1558,7 @@ bool create(pi05_engine* e) {
   if (const char* s = getenv("PI05_GEMM_WIDE")) e->gemm_wide = atoi(s) != 0;
   if (const char* s = getenv("PI05_MEGA")) e->mega = atoi(s) != 0;
   if (const char* s = getenv("PI05_FUSE_NORM")) e->fuse_norm = atoi(s) != 0;
+  if (const char* s = getenv("PI05_FUSE_GEGLU_BWD")) e->fuse_geglu_bwd = atoi(s) != 0;
   CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   cudaDriverEntryPointQueryResult q;
   void* fn = nullptr;

@@ -35,7 +35,20 @@ enum EpiKind : int {
   // reduce): the weight rows of each 256-wide head are interleaved (row 2j = dim j, row 2j+1 = dim
   // j+128), see GemmArgs rope_*
   EPI_ROPE = 8,
+  // GeGLU backward fused into the dX GEMM of the down projection (normal orientation): v = dact[t][f] and
+  // (g, u) = res[t][2f], res[t][2f+1] (the saved pre-activations): out[t][2f], [2f+1] = geglu_bwd_pair(g, u, R(v))
+  EPI_GEGLU_BWD = 9,
 };
+
+// GeGLU backward of one (gate, up) pair: act = R(gelu(g)) * u, so dg = da * u * gelu'(g) and du = da * R(gelu(g))
+// (gelu with the tanh approximation), packed as bf16 (dg, du).  Shared by geglu_bwd_kernel and the fused epilogue.
+__device__ __forceinline__ uint32_t geglu_bwd_pair(float g, float u, float da) {
+  const float c = 0.7978845608028654f, a = 0.044715f;
+  const float th = tanhf(c * (g + a * g * g * g));
+  const float grad = 0.5f * (1.0f + th) + 0.5f * g * (1.0f - th * th) * c * (1.0f + 3.0f * a * g * g);
+  const float gel = 0.5f * g * (1.0f + th);
+  return pack_bf2(da * u * grad, da * rbf(gel));
+}
 // v = acc * out_scale + bias[f] + addend[(t % add_mod)][f]
 
 struct GemmArgs {
@@ -215,6 +228,23 @@ __device__ __forceinline__ void epi_row32(const GemmArgs& a, float (&v)[32], int
       dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
       return;
     }
+    if (EPI == EPI_GEGLU_BWD) {
+      const uint4* g4 = reinterpret_cast<const uint4*>(a.res + (size_t)t * a.ld_res + 2 * f0);
+      uint4* dst = reinterpret_cast<uint4*>(a.out + (size_t)t * a.ld_out + 2 * f0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint4 gq = g4[q];
+        const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 p = unpack_bf2(gw[k]);
+          o[k] = geglu_bwd_pair(p.x, p.y, rbf(v[4 * q + k]));
+        }
+        dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      return;
+    }
     if (EPI == EPI_GELU) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(rbf(v[i]));
@@ -260,7 +290,7 @@ __device__ __forceinline__ void epi_row32(const GemmArgs& a, float (&v)[32], int
       a.out_f32[(size_t)t * a.ld_out_f32 + f] = x;
       continue;
     }
-    if (EPI == EPI_GEGLU) break;  // GeGLU widths are multiples of 32 (checked by the host)
+    if (EPI == EPI_GEGLU || EPI == EPI_GEGLU_BWD) break;  // widths are multiples of 32 (checked by the host)
     if (EPI == EPI_GELU) x = gelu_tanh(rbf(x));
     if (EPI == EPI_RESID) x = bf(a.res[(size_t)t * a.ld_res + f]) + rbf(x);
     if (EPI == EPI_GATED)

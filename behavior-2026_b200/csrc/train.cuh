@@ -617,14 +617,24 @@ bool micro_step(pi05_engine* e, int nb, const float* h_t) {
       if (!lora_v(e, t.dn, dy, R, T->vT) || !lora_wgrad(e, T, t.dn, dy, S.act, S.uT_dn, T->vT, R)) return false;
       Lin da{dy, t.dn.ldb(), R, t.dn.Wb, t.dn.ldb(), F, t.dn.ldb()};
       da.no_swap = true;
-      da.out = dact;
-      da.ld_out = F;
-      if (!linear(e, da)) return false;
-      static_assert(P5_GEM_MLP % 8 == 0 && P5_EXP_MLP % 8 == 0, "geglu_bwd_kernel takes 8 pairs per thread");
-      const long ng = (long)R * (F / 8);
-      if (!launch(e, geglu_bwd_kernel, dim3((ng + 255) / 256), dim3(256), 0, false, (const bf16*)S.gu,
-                  (const bf16*)dact, F, dgu, 2 * F + 32, R, F))
-        return false;
+      if (e->fuse_geglu_bwd) {
+        // dact never reaches memory: the epilogue turns each row's 32 dact values into the (dgate, dup) pairs
+        da.epi = EPI_GEGLU_BWD;
+        da.out = dgu;
+        da.ld_out = 2 * F + 32;
+        da.res = S.gu;
+        da.ld_res = 2 * F;
+        if (!linear(e, da)) return false;
+      } else {
+        da.out = dact;
+        da.ld_out = F;
+        if (!linear(e, da)) return false;
+        static_assert(P5_GEM_MLP % 8 == 0 && P5_EXP_MLP % 8 == 0, "geglu_bwd_kernel takes 8 pairs per thread");
+        const long ng = (long)R * (F / 8);
+        if (!launch(e, geglu_bwd_kernel, dim3((ng + 255) / 256), dim3(256), 0, false, (const bf16*)S.gu,
+                    (const bf16*)dact, F, dgu, 2 * F + 32, R, F))
+          return false;
+      }
       if (!lora_v(e, t.gu, dgu, R, T->vT) || !lora_wgrad(e, T, t.gu, dgu, S.h2, S.uT_gu, T->vT, R)) return false;
       if (!lora_dx(e, t.gu, dgu, R, dh)) return false;
       if (!rms_bwd(e, S.xmid, dh, D, prefix ? e->gem[l].rms2 : m2, rpg, gld, gx, R, D)) return false;

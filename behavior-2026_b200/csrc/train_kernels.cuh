@@ -236,15 +236,10 @@ __global__ void geglu_bwd_kernel(const bf16* gu, const bf16* dact, int ld_dact, 
   float da[8];
   unpack8(dv, da);
   uint32_t o[8];
-  const float c = 0.7978845608028654f, a = 0.044715f;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const float2 p = unpack_bf2(gw[k]);
-    const float g = p.x, u = p.y;
-    const float th = tanhf(c * (g + a * g * g * g));
-    const float grad = 0.5f * (1.0f + th) + 0.5f * g * (1.0f - th * th) * c * (1.0f + 3.0f * a * g * g);
-    const float gel = 0.5f * g * (1.0f + th);
-    o[k] = pack_bf2(da[k] * u * grad, da[k] * rbf(gel));
+    o[k] = geglu_bwd_pair(p.x, p.y, da[k]);
   }
   uint4* dst = reinterpret_cast<uint4*>(dgu + (long)t * ld_dgu + 2 * j0);
   dst[0] = make_uint4(o[0], o[1], o[2], o[3]);

@@ -169,3 +169,24 @@ def test_lora_reference_recipe_schedule_and_ema(pn, oracle, lora_case, tmp_path)
     np.testing.assert_array_equal(eng.lora_get_params(), p2)
     np.testing.assert_array_equal(eng.lora_get_ema(), e2)
     eng.close()
+
+
+def test_lora_fused_geglu_backward_equals_separate_kernel(lora_case, pn, monkeypatch):
+    """The GeGLU backward fused into the down projection's dX epilogue (dact never written) against the
+    separate geglu_bwd_kernel on the stored dact: the same rounding of dact and the same pair formula,
+    so the gradients are bit-identical."""
+    cfg = pn.Config.make(siglip_layers=1, gemma_layers=2, num_steps=10)
+    imgs, toks, acts, noise, t = lora_case["batch"]
+    out = {}
+    for fuse in ("1", "0"):
+        monkeypatch.setenv("PI05_FUSE_GEGLU_BWD", fuse)
+        eng = pn.Engine(cfg, max_batch=2)
+        eng.init_random_weights(4)
+        eng.lora_init(seed=5, micro_batch=2)
+        eng.lora_set_params(lora_case["p0"])
+        eng.lora_zero_grads()
+        out[fuse] = (eng.lora_accumulate(imgs, toks, acts, noise, t), eng.lora_get_grads())
+        eng.close()
+    assert out["1"][0] == out["0"][0]
+    np.testing.assert_array_equal(out["1"][1], out["0"][1])
+    np.testing.assert_array_equal(out["1"][1], lora_case["g_gpu"])
