@@ -40,9 +40,10 @@ def test_masked_prompt_matches_oracle(pn, oracle, depth):
         d, c = float(np.abs(act[i] - ref).max()), cos(act[i], ref)
         print(f"{depth} length {n}: max-abs {d:.3e} cos {c:.6f}")
         assert d <= 2e-2 and c >= 0.999, (n, d, c)
-        if n < 200:  # the mask changes the result: the unmasked network is far from it
+        if n < 200:  # the mask moves the result by more than twice the tolerance: an unmasked engine fails
             plain = oracle.infer(ocfg, 17, imgs[i], toks[i], noise[i])
-            assert np.abs(plain - ref).max() > 0.1
+            assert np.abs(plain - ref).max() > 2 * 2e-2
+            assert np.abs(act[i] - plain).max() > 2e-2
 
 
 def test_masked_prompt_batch_invariant(pn):
