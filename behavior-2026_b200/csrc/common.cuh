@@ -58,9 +58,25 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
   return m;
 }
+// 0.5 * (1 + tanh(u)) in its logistic form 1 / (1 + exp(-2u)): one exponential and one reciprocal, and no
+// cancellation for large negative u.  The exponent is clamped at 80 so that 1 + exp(-2u) stays finite
+// (exp(80) ~ 5.5e34); below u = -40 the value is below 2^-115 either way.
+__device__ __forceinline__ float half_one_plus_tanh(float u) {
+  const float e = __expf(fminf(-2.0f * u, 80.0f));
+  return __fdividef(1.0f, 1.0f + e);
+}
+
+// gelu with the tanh approximation: 0.5 x (1 + tanh(c (x + 0.044715 x^3))) = x * half_one_plus_tanh(...)
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float c = 0.7978845608028654f;
-  return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
+  return x * half_one_plus_tanh(c * (x + 0.044715f * x * x * x));
+}
+
+// d gelu / dx with s = 0.5 (1 + tanh(u)): 0.5 (1 + tanh) = s and 1 - tanh^2 = 4 s (1 - s), so
+// gelu'(x) = s + 2 x c s (1 - s) (1 + 3 * 0.044715 x^2)
+__device__ __forceinline__ float gelu_tanh_grad_s(float x, float s) {
+  const float c = 0.7978845608028654f, a = 0.044715f;
+  return s + 2.0f * x * c * s * (1.0f - s) * (1.0f + 3.0f * a * x * x);
 }
 
 __device__ __forceinline__ void record_error(int* status, int code) {
@@ -111,6 +127,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 }
 
 // ------------------------------------------------------------------ TMA
+// hint: bring [p, p + bytes) into L2 (16-byte aligned address, size a multiple of 16)
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }

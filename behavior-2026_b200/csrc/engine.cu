@@ -646,8 +646,9 @@ bool linear(pi05_engine* e, const Lin& L) {
     }
   }
   if (L.epi == EPI_ROPE && swap) return set_err(e, "fused RoPE epilogue: few-token projection without a cluster split");
-  if (L.epi == EPI_GEGLU_BWD && (swap || L.F % 32 || BN < 64))
-    return set_err(e, "fused GeGLU backward: normal orientation and F % 32 == 0 only");
+  if (L.epi == EPI_GEGLU_BWD && (swap || L.F % 32 || BN < 64 || L.ld_res % 8 || L.ld_out % 8 ||
+                                 ((uintptr_t)L.res | (uintptr_t)L.out) % 16))
+    return set_err(e, "fused GeGLU backward: normal orientation, F % 32 == 0, 16-byte aligned rows only");
   if (fused_nrm) return set_err(e, "fused adaRMSNorm / sum-of-squares output: not a few-token cluster projection");
   if (!swap && BN == 256 && splits == 1 && !L.amn && e->gemm_wide && L.epi != EPI_STORE_T && L.epi != EPI_LORA_GRAD &&
       L.epi != EPI_GEGLU_BWD && kt >= 64) {

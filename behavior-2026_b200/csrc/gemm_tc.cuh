@@ -43,11 +43,8 @@ enum EpiKind : int {
 // GeGLU backward of one (gate, up) pair: act = R(gelu(g)) * u, so dg = da * u * gelu'(g) and du = da * R(gelu(g))
 // (gelu with the tanh approximation), packed as bf16 (dg, du).  Shared by geglu_bwd_kernel and the fused epilogue.
 __device__ __forceinline__ uint32_t geglu_bwd_pair(float g, float u, float da) {
-  const float c = 0.7978845608028654f, a = 0.044715f;
-  const float th = tanhf(c * (g + a * g * g * g));
-  const float grad = 0.5f * (1.0f + th) + 0.5f * g * (1.0f - th * th) * c * (1.0f + 3.0f * a * g * g);
-  const float gel = 0.5f * g * (1.0f + th);
-  return pack_bf2(da * u * grad, da * rbf(gel));
+  const float s = half_one_plus_tanh(0.7978845608028654f * (g + 0.044715f * g * g * g));
+  return pack_bf2(da * u * gelu_tanh_grad_s(g, s), da * rbf(g * s));
 }
 // v = acc * out_scale + bias[f] + addend[(t % add_mod)][f]
 
@@ -231,9 +228,14 @@ __device__ __forceinline__ void epi_row32(const GemmArgs& a, float (&v)[32], int
     if (EPI == EPI_GEGLU_BWD) {
       const uint4* g4 = reinterpret_cast<const uint4*>(a.res + (size_t)t * a.ld_res + 2 * f0);
       uint4* dst = reinterpret_cast<uint4*>(a.out + (size_t)t * a.ld_out + 2 * f0);
+      // all eight loads before the first store: the compiler cannot tell res and out apart, so a store
+      // in between would hold each later load back by a full memory round trip
+      uint4 gl[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) gl[q] = g4[q];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const uint4 gq = g4[q];
+        const uint4 gq = gl[q];
         const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w};
         uint32_t o[4];
 #pragma unroll
@@ -529,6 +531,12 @@ __global__ void __launch_bounds__(256, 1)
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++j) {
       int tm, tn, split, kt0, nkt;
       decode(u, tm, tn, split, kt0, nkt);
+      if (EPI == EPI_GEGLU_BWD && args.splits == 1) {
+        // the tile's saved pre-activations head for L2 while its MMAs run
+        const int r = tm * C::BM + sub * 32 + lane, cb = tn * BN;
+        if (r < args.M && cb < args.N)
+          bulk_prefetch_l2(args.res + (size_t)r * args.ld_res + 2 * (size_t)cb, (uint32_t)min(BN, args.N - cb) * 4u);
+      }
       const int acc = j & 1;
       const uint32_t aph = (uint32_t)(j >> 1) & 1u;
       const bool ok = mbar_wait(&tfull_bar[acc], aph, args.status, P5_ERR_WAIT_ACCUM) && !flags[0] && nkt > 0;
@@ -536,7 +544,49 @@ __global__ void __launch_bounds__(256, 1)
       const uint32_t t_acc = tmem_base + lane_addr + (uint32_t)(acc * BN);
       const int row = tm * C::BM + sub * 32 + lane;
       const int col_base = tn * BN;
-      if (args.splits == 1) {
+      if (EPI == EPI_GEGLU_BWD && args.splits == 1) {
+        // software-pipelined: chunk c + 32's saved pre-activations (8 x 16 bytes per thread) are in flight
+        // while chunk c computes; rows past M read row M - 1 and store nothing
+        const int cmax = min(BN, args.N - col_base);
+        const uint4* gsrc =
+            reinterpret_cast<const uint4*>(args.res + (size_t)min(row, args.M - 1) * args.ld_res + 2 * (size_t)col_base);
+        uint4 gc[8], gn[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          gc[q] = ok ? gsrc[q] : make_uint4(0u, 0u, 0u, 0u);
+          gn[q] = gc[q];
+        }
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          const bool live = ok && c < cmax;
+          if (live && c + 32 < cmax) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) gn[q] = gsrc[(c + 32) / 4 + q];
+          }
+          uint32_t r[32];
+          tmem_ld32(t_acc + (uint32_t)c, r);
+          tmem_wait_ld();
+          if (live && row < args.M) {
+            uint4* dst = reinterpret_cast<uint4*>(args.out + (size_t)row * args.ld_out + 2 * (size_t)(col_base + c));
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint32_t gw[4] = {gc[q].x, gc[q].y, gc[q].z, gc[q].w};
+              uint32_t o[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float2 p = unpack_bf2(gw[k]);
+                o[k] = geglu_bwd_pair(p.x, p.y, rbf(__uint_as_float(r[4 * q + k])));
+              }
+              dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) gc[q] = gn[q];
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      } else if (args.splits == 1) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += C::CH) {
           uint32_t r[32];

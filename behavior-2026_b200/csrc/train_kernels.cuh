@@ -12,10 +12,7 @@
 namespace p5 {
 
 __device__ __forceinline__ float gelu_tanh_grad(float x) {
-  const float c = 0.7978845608028654f, a = 0.044715f;
-  const float inner = c * (x + a * x * x * x);
-  const float th = tanhf(inner);
-  return 0.5f * (1.0f + th) + 0.5f * x * (1.0f - th * th) * c * (1.0f + 3.0f * a * x * x);
+  return gelu_tanh_grad_s(x, half_one_plus_tanh(0.7978845608028654f * (x + 0.044715f * x * x * x)));
 }
 
 // ---------------------------------------------------------------- loss

@@ -108,6 +108,37 @@ def test_linear_epilogues_match_torch(pn, torch_cuda, epi, T):
     assert err <= 2e-2 * max(1.0, ref.abs().max().item()), (epi, err)
 
 
+def test_gelu_logistic_form_matches_tanh_gelu(pn, torch_cuda):
+    """The epilogues compute gelu's 0.5 (1 + tanh(u)) as 1 / (1 + exp(-2u)), u = c (x + 0.044715 x^3), on
+    bf16 pre-activations spread N(0, 3.2) into both tails.  Against the function evaluated in float64: equal
+    after bf16 rounding except at rounding boundaries (one bf16 ulp).  Against torch's CUDA fp32 gelu (tanh
+    form): within one bf16 ulp plus 1e-6, the cancellation error of 1 + tanh(u) in fp32 for x < -4."""
+    torch = torch_cuda
+    T, F, K = 968, 4096, 1024
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(F, K, device="cuda", generator=g) * 0.1).bfloat16()
+    eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), max_batch=1)
+    pre = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    eng.op_linear(x, w, pre, "store")
+    eng.op_linear(x, w, out, "gelu")
+    eng.sync()
+    eng.close()
+    assert pre.float().min().item() < -8 and pre.float().max().item() > 8
+    got = out.float()
+    xd = pre.double()
+    u = 0.7978845608028654 * (xd + 0.044715 * xd ** 3)
+    exact = (xd / (1.0 + torch.exp(-2.0 * u))).bfloat16().float()
+    one_ulp = torch.maximum(exact.abs(), got.abs()) * 2.0 ** -7
+    assert bool(((got - exact).abs() <= torch.clamp(one_ulp, min=1e-30)).all()), (got - exact).abs().max().item()
+    assert (got != exact).float().mean().item() < 0.02
+    ref32 = torch.nn.functional.gelu(pre.float(), approximate="tanh").bfloat16().float()
+    tol32 = torch.maximum(ref32.abs(), got.abs()) * 2.0 ** -7 + 1e-6
+    assert bool(((got - ref32).abs() <= tol32).all()), (got - ref32).abs().max().item()
+
+
 @pytest.mark.parametrize("T", [50, 64, 100])
 def test_linear_geglu_row_pairs_match_torch(pn, torch_cuda, T):
     """Few-token gate/up projection of the action expert (8192 interleaved rows): the cluster reduce
