@@ -20,6 +20,7 @@
 #include "attention_tc.cuh"
 #include "attention_sig.cuh"
 #include "gemm_wide.cuh"
+#include "gemm_pair.cuh"
 #include "denoise_mega.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
@@ -113,6 +114,8 @@ struct pi05_engine {
   struct Trainer* tr = nullptr;  // LoRA train state (train.cuh), created by pi05_lora_init
   bool cluster_splitk = true;    // few-token split-K GEMMs reduce inside a cluster (PI05_CLUSTER_SPLITK=0: tickets)
   bool gemm_wide = true;          // 256x256 tiles for large GEMMs (PI05_GEMM_WIDE=0: 128x256)
+  bool gemm_pair = true;          // CTA-pair 256x256 tiles (cta_group::2) for K < 4096 (PI05_GEMM_PAIR=0: one SM)
+  int pair_clusters = 0;          // CTA pairs of gemm_pair_kernel that fit on the GPU at once
   bool wide_swap = true;          // few M-tiles: weights-on-M cluster split-K (PI05_WIDE_SWAP=0: normal tiles)
   bool attn_tc = true;           // head_dim-256 MQA attention on tcgen05 (PI05_ATTN_TC=0: the mma.sync kernel)
   // few-token denoise: adaRMSNorm folded into the q/k/v and gate/up cluster GEMMs, fed by per-token
@@ -419,6 +422,53 @@ bool launch_cluster(pi05_engine* e, void (*kern)(KArgs...), dim3 grid, dim3 bloc
   return true;
 }
 
+// CTA-pair GEMM: one cluster of two CTAs per 256x256 tile, persistent over the tiles
+bool launch_gemm_pair(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga) {
+  const dim3 grid(2 * std::min(ga.tiles_m * ga.tiles_n, e->pair_clusters));
+  const size_t sm = (size_t)GemmPairCfg::SMEM;
+  const bool p = ga.pdl != 0;
+  switch (ga.epi) {
+    case EPI_GELU: return launch_cluster(e, gemm_pair_kernel<EPI_GELU>, grid, dim3(256), sm, 2, p, ta, tb, ga);
+    case EPI_RESID: return launch_cluster(e, gemm_pair_kernel<EPI_RESID>, grid, dim3(256), sm, 2, p, ta, tb, ga);
+    case EPI_GATED: return launch_cluster(e, gemm_pair_kernel<EPI_GATED>, grid, dim3(256), sm, 2, p, ta, tb, ga);
+    case EPI_GEGLU: return launch_cluster(e, gemm_pair_kernel<EPI_GEGLU>, grid, dim3(256), sm, 2, p, ta, tb, ga);
+    case EPI_ROPE: return launch_cluster(e, gemm_pair_kernel<EPI_ROPE>, grid, dim3(256), sm, 2, p, ta, tb, ga);
+    case EPI_F32: return launch_cluster(e, gemm_pair_kernel<EPI_F32>, grid, dim3(256), sm, 2, p, ta, tb, ga);
+    case EPI_GEGLU_BWD:
+      return launch_cluster(e, gemm_pair_kernel<EPI_GEGLU_BWD>, grid, dim3(256), sm, 2, p, ta, tb, ga);
+    default: return launch_cluster(e, gemm_pair_kernel<EPI_STORE>, grid, dim3(256), sm, 2, p, ta, tb, ga);
+  }
+}
+
+bool set_gemm_pair_smem(pi05_engine* e) {
+  const int sm = GemmPairCfg::SMEM;
+  CK(cudaFuncSetAttribute(gemm_pair_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_pair_kernel<EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_pair_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_pair_kernel<EPI_GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_pair_kernel<EPI_GEGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_pair_kernel<EPI_ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_pair_kernel<EPI_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  CK(cudaFuncSetAttribute(gemm_pair_kernel<EPI_GEGLU_BWD>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+  // the persistent grid holds as many pairs as can be resident at once (pairs need two SMs of one GPC)
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(2 * (e->num_sms / 2));
+  lc.blockDim = dim3(256);
+  lc.dynamicSmemBytes = sm;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  int n = 0;
+  CK(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<EPI_STORE>, &lc));
+  e->pair_clusters = std::min(n, e->num_sms / 2);
+  if (e->pair_clusters < 1) e->gemm_pair = false;
+  return true;
+}
+
 template <int BN>
 bool launch_swap_cluster(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga, int S) {
   const dim3 grid(ga.tiles_m * ga.tiles_n * S);
@@ -666,6 +716,17 @@ bool linear(pi05_engine* e, const Lin& L) {
       gw.group_m = std::max(1, std::min(wtm, (int)((48ull << 20) / (256ull * L.K * 2))));
       return launch_gemm_wide(e, ta, tb, gw);
     }
+  }
+  if (!swap && BN == 256 && splits == 1 && !L.amn && e->gemm_pair && L.epi != EPI_STORE_T &&
+      L.epi != EPI_LORA_GRAD) {
+    // one 256x256 tile per CTA pair: each SM stages half of A's and half of B's rows
+    GemmArgs gp = ga;
+    gp.tiles_m = (L.T + 255) / 256;
+    gp.tiles_n = (L.F + 255) / 256;
+    gp.group_m = std::max(1, std::min(gp.tiles_m, (int)((48ull << 20) / (256ull * L.K * 2))));
+    CUtensorMap tb2;
+    if (!make_tmap(e, &tb2, L.w, L.F, L.K, L.ldw, 128)) return false;
+    return launch_gemm_pair(e, ta, tb2, gp);
   }
   if (BN == 16) return launch_gemm_small<16>(e, ta, tb, ga, L.amn);
   if (BN == 32) return launch_gemm_small<32>(e, ta, tb, ga, L.amn);
@@ -1557,6 +1618,7 @@ bool create(pi05_engine* e) {
   if (const char* s = getenv("PI05_ATTN_TC")) e->attn_tc = atoi(s) != 0;
   if (const char* s = getenv("PI05_WIDE_SWAP")) e->wide_swap = atoi(s) != 0;
   if (const char* s = getenv("PI05_GEMM_WIDE")) e->gemm_wide = atoi(s) != 0;
+  if (const char* s = getenv("PI05_GEMM_PAIR")) e->gemm_pair = atoi(s) != 0;
   if (const char* s = getenv("PI05_MEGA")) e->mega = atoi(s) != 0;
   if (const char* s = getenv("PI05_FUSE_NORM")) e->fuse_norm = atoi(s) != 0;
   if (const char* s = getenv("PI05_FUSE_GEGLU_BWD")) e->fuse_geglu_bwd = atoi(s) != 0;
@@ -1570,7 +1632,7 @@ bool create(pi05_engine* e) {
   if (!set_gemm_smem<64>(e) || !set_gemm_smem<128>(e) || !set_gemm_smem<256>(e)) return false;
   if (!set_gemm_smem_small<16>(e) || !set_gemm_smem_small<32>(e) || !set_gemm_smem_small<48>(e)) return false;
   if (!set_swap_cluster_smem<64>(e) || !set_swap_cluster_smem<128>(e) || !set_swap_cluster_smem<256>(e)) return false;
-  if (!set_gemm_wide_smem(e)) return false;
+  if (!set_gemm_wide_smem(e) || !set_gemm_pair_smem(e)) return false;
 
   CK(cudaFuncSetAttribute(attn_kernel<P5_HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnCfg<P5_HD, 4>::SMEM));

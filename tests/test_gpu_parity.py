@@ -196,6 +196,51 @@ def test_linear_tile_shapes_epilogues(pn, torch_cuda, epi, shape):
     assert err <= 2e-2 * max(1.0, ref.abs().max().item()), (epi, err)
 
 
+@pytest.mark.parametrize("epi", ["store", "gelu", "gated", "geglu", "f32"])
+@pytest.mark.parametrize("shape", [(1000, 2336, 1024), (968, 8192, 2048), (4096, 2560, 1024)],
+                         ids=["ragged", "gemma_gate_up_bs1", "full_waves"])
+def test_pair_gemm_matches_one_sm_tiles(pn, torch_cuda, monkeypatch, epi, shape):
+    """The CTA-pair GEMM (cta_group::2, one 256x256 tile per pair of SMs, each staging half of A's and
+    half of B's rows) against the one-SM 128x256 tiles (PI05_GEMM_PAIR=0) on the same operands, with
+    ragged M and N (1000 x 2336: the last pair tile is part padding in both), and against fp32 torch.
+    Both accumulate every output over K in the same order."""
+    torch = torch_cuda
+    T, F, K = shape
+    g = torch.Generator(device="cuda").manual_seed(31)
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(F, K, device="cuda", generator=g) * 0.02).bfloat16()
+    res = torch.randn(T, F, device="cuda", generator=g).bfloat16()
+    gate = torch.randn(F, device="cuda", generator=g).bfloat16()
+    outs = []
+    for pair in ("1", "0"):
+        monkeypatch.setenv("PI05_GEMM_PAIR", pair)  # read when the engine is created
+        eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), max_batch=1)
+        if epi == "geglu":
+            out = torch.full((T, F // 2), 7.0, device="cuda", dtype=torch.bfloat16)
+        elif epi == "f32":
+            out = torch.full((T, F), 7.0, device="cuda", dtype=torch.float32)
+        else:
+            out = torch.full((T, F), 7.0, device="cuda", dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        eng.op_linear(x, w, out, epi, res=res if epi == "gated" else None, gate=gate if epi == "gated" else None)
+        eng.sync()
+        eng.close()
+        outs.append(out.float())
+    acc = x.float() @ w.float().t()
+    rb = lambda t: t.bfloat16().float()
+    ref = {"store": lambda: acc, "f32": lambda: acc,
+           "gelu": lambda: torch.nn.functional.gelu(rb(acc), approximate="tanh"),
+           "gated": lambda: res.float() + rb(rb(acc) * gate.float()),
+           "geglu": lambda: rb(torch.nn.functional.gelu(rb(acc[:, 0::2]), approximate="tanh")) * rb(acc[:, 1::2])}[epi]()
+    for o in outs:
+        err = (o - ref).abs().max().item()
+        assert err <= 2e-2 * max(1.0, ref.abs().max().item()), (epi, err)
+    # same K order: equal up to the rare bf16 rounding tie of a differently ordered sum
+    diff = (outs[0] - outs[1]).abs()
+    assert (diff > 0).float().mean().item() < 1e-3, (diff > 0).float().mean().item()
+    assert diff.max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+
+
 @pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("T,S,splits,qscale", [(50, 1018, 8, 0.1), (50, 1018, 1, 0.1), (968, 968, 1, 0.1),
                                                (100, 2048, 4, 0.1), (1, 1000, 3, 0.1), (33, 200, 1, 0.6),
