@@ -389,7 +389,7 @@ def run_ours(args, world, rank, local):
         fl = 2.0 * M * 32768 * 2048
         ach = fl / (ms / 1e3) / 1e12
         tr = profiled_traffic(f"gemma_gate_up_M{M}")
-        line["roofline"] = {"kernel": "gemm_tc_kernel<256> Gemma-2B gate/up + GeGLU epilogue",
+        line["roofline"] = {"kernel": "gemm_pair_kernel<EPI_GEGLU> Gemma-2B gate/up + GeGLU epilogue (CTA pairs, cta_group::2)",
                             "shape": [M, 32768, 2048], "bound": "tensor", "achieved": ach, "peak": tf_burst,
                             "unit": "TFLOP/s", "frac": ach / tf_burst, "peak_source": f"{peak_src} bf16 burst",
                             "ms_per_launch": ms, "algorithmic_flops": fl, "traffic": tr}
