@@ -428,15 +428,15 @@ bool launch_gemm_pair(pi05_engine* e, const CUtensorMap& ta, const CUtensorMap& 
   const size_t sm = (size_t)GemmPairCfg::SMEM;
   const bool p = ga.pdl != 0;
   switch (ga.epi) {
-    case EPI_GELU: return launch_cluster(e, gemm_pair_kernel<EPI_GELU>, grid, dim3(256), sm, 2, p, ta, tb, ga);
-    case EPI_RESID: return launch_cluster(e, gemm_pair_kernel<EPI_RESID>, grid, dim3(256), sm, 2, p, ta, tb, ga);
-    case EPI_GATED: return launch_cluster(e, gemm_pair_kernel<EPI_GATED>, grid, dim3(256), sm, 2, p, ta, tb, ga);
-    case EPI_GEGLU: return launch_cluster(e, gemm_pair_kernel<EPI_GEGLU>, grid, dim3(256), sm, 2, p, ta, tb, ga);
-    case EPI_ROPE: return launch_cluster(e, gemm_pair_kernel<EPI_ROPE>, grid, dim3(256), sm, 2, p, ta, tb, ga);
-    case EPI_F32: return launch_cluster(e, gemm_pair_kernel<EPI_F32>, grid, dim3(256), sm, 2, p, ta, tb, ga);
+    case EPI_GELU: return launch_cluster(e, gemm_pair_kernel<EPI_GELU>, grid, dim3(GemmPairCfg::THREADS), sm, 2, p, ta, tb, ga);
+    case EPI_RESID: return launch_cluster(e, gemm_pair_kernel<EPI_RESID>, grid, dim3(GemmPairCfg::THREADS), sm, 2, p, ta, tb, ga);
+    case EPI_GATED: return launch_cluster(e, gemm_pair_kernel<EPI_GATED>, grid, dim3(GemmPairCfg::THREADS), sm, 2, p, ta, tb, ga);
+    case EPI_GEGLU: return launch_cluster(e, gemm_pair_kernel<EPI_GEGLU>, grid, dim3(GemmPairCfg::THREADS), sm, 2, p, ta, tb, ga);
+    case EPI_ROPE: return launch_cluster(e, gemm_pair_kernel<EPI_ROPE>, grid, dim3(GemmPairCfg::THREADS), sm, 2, p, ta, tb, ga);
+    case EPI_F32: return launch_cluster(e, gemm_pair_kernel<EPI_F32>, grid, dim3(GemmPairCfg::THREADS), sm, 2, p, ta, tb, ga);
     case EPI_GEGLU_BWD:
-      return launch_cluster(e, gemm_pair_kernel<EPI_GEGLU_BWD>, grid, dim3(256), sm, 2, p, ta, tb, ga);
-    default: return launch_cluster(e, gemm_pair_kernel<EPI_STORE>, grid, dim3(256), sm, 2, p, ta, tb, ga);
+      return launch_cluster(e, gemm_pair_kernel<EPI_GEGLU_BWD>, grid, dim3(GemmPairCfg::THREADS), sm, 2, p, ta, tb, ga);
+    default: return launch_cluster(e, gemm_pair_kernel<EPI_STORE>, grid, dim3(GemmPairCfg::THREADS), sm, 2, p, ta, tb, ga);
   }
 }
 
@@ -453,7 +453,7 @@ bool set_gemm_pair_smem(pi05_engine* e) {
   // the persistent grid holds as many pairs as can be resident at once (pairs need two SMs of one GPC)
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(2 * (e->num_sms / 2));
-  lc.blockDim = dim3(256);
+  lc.blockDim = dim3(GemmPairCfg::THREADS);
   lc.dynamicSmemBytes = sm;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;

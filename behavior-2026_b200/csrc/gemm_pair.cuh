@@ -11,8 +11,9 @@
 //   warp 1  even CTA: MMA issuer.  Odd CTA: relay — once its own stage has landed it arrives on the
 //           even CTA's pair barrier for that stage, so the issuer knows both halves are in place
 //   warp 2  TMEM: 2 x 256 f32 columns (double-buffered accumulator), allocated as a pair
-//   warps 4-7 epilogue of the CTA's 128 rows (the same fused epilogues as gemm_tc_kernel); the
-//           accumulator is handed back to the issuer with 4 local + 4 remote arrivals
+//   warps 4-11 epilogue of the CTA's 128 rows (the same fused epilogues as gemm_tc_kernel): two warps
+//           per 32-lane TMEM quarter, one per 128-column half; the accumulator is handed back to the
+//           issuer with 8 local + 8 remote arrivals
 // The issuer's commits are multicast to both CTAs (stage released, accumulator complete).  The per-stage
 // waits are CTA-scope (acquire.cluster on every stage halved the throughput, measured) and the relay's
 // arrival is relaxed: it only forwards a completion the TMA already signalled.  Every wait is bounded;
@@ -34,10 +35,11 @@ struct GemmPairCfg {
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr int THREADS = 384;  // 4 role warps + 8 epilogue warps
 };
 
 template <int EPI>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(GemmPairCfg::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const GemmArgs args) {
   using C = GemmPairCfg;
@@ -50,7 +52,7 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* empty_bar = full_bar + C::STAGES;   // [STAGES] pair MMAs done with the stage (multicast commit)
   uint64_t* pair_bar = empty_bar + C::STAGES;   // [STAGES] even CTA: the odd CTA's stage landed (relay)
   uint64_t* tfull_bar = pair_bar + C::STAGES;   // [2] accumulator complete (multicast commit)
-  uint64_t* tempty_bar = tfull_bar + 2;         // [2] even CTA: accumulator drained by 8 epilogue warps
+  uint64_t* tempty_bar = tfull_bar + 2;         // [2] even CTA: accumulator drained by 16 epilogue warps
   uint64_t* done_bar = tempty_bar + 2;          // every pair MMA complete (multicast commit)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort, [2] skip
@@ -70,7 +72,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 8);
+      mbar_init(&tempty_bar[b], 16);
     }
     mbar_init(done_bar, 1);
     flags[0] = 0;
@@ -193,7 +195,8 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp >= 4) {
     // ---------------- epilogue: this CTA's 128 rows of the pair's tile
     if (args.pdl) pdl_wait();
-    const int sub = warp & 3;  // TMEM lanes [32*sub, 32*sub+32)
+    const int sub = warp & 3;              // TMEM lanes [32*sub, 32*sub+32)
+    const int c0 = ((warp - 4) >> 2) * (C::BN / 2);  // this warp's 128 columns
     const uint32_t lane_addr = (uint32_t)(sub * 32) << 16;
     const uint32_t tempty0 = map_peer(smem_u32(tempty_bar), 0);
     int j = 0;
@@ -209,7 +212,7 @@ __global__ void __launch_bounds__(256, 1)
       const int row = tm * 256 + (int)rank * 128 + sub * 32 + lane;
       const int col_base = tn * C::BN;
 #pragma unroll 1
-      for (int c = 0; c < C::BN; c += 32) {
+      for (int c = c0; c < c0 + C::BN / 2; c += 32) {
         uint32_t r[32];
         tmem_ld32(t_acc + (uint32_t)c, r);
         tmem_wait_ld();
