@@ -13,7 +13,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libpi05.so")
 SOURCES = ["engine.cu", "static_scratch.cu", "preprocess.cu", "tokenizer.cpp"]
 DEPS = SOURCES + ["common.cuh", "attention_bwd_tc.cuh", "gemm_tc.cuh", "attention.cuh", "kernels.cuh", "pi05_model.h", "train.cuh",
-                  "train_kernels.cuh", "attention_bwd.cuh", "attention_tc.cuh", "denoise_mega.cuh", "attention_sig.cuh", "gemm_wide.cuh", "gemm_pair.cuh", "resize.cuh", "dp_nccl.cuh"]
+                  "train_kernels.cuh", "attention_bwd.cuh", "attention_tc.cuh", "denoise_mega.cuh", "attention_sig.cuh", "gemm_wide.cuh", "gemm_pair.cuh", "attention_bwd_dq_pipe.cuh", "resize.cuh", "dp_nccl.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -118,6 +118,7 @@ struct pi05_engine {
   int pair_clusters = 0;          // CTA pairs of gemm_pair_kernel that fit on the GPU at once
   bool wide_swap = true;          // few M-tiles: weights-on-M cluster split-K (PI05_WIDE_SWAP=0: normal tiles)
   bool attn_tc = true;           // head_dim-256 MQA attention on tcgen05 (PI05_ATTN_TC=0: the mma.sync kernel)
+  bool attn_bwd_pipe = true;     // dQ backward with dS overlapped (PI05_ATTN_BWD_PIPE=0: the one-slot kernel)
   // few-token denoise: adaRMSNorm folded into the q/k/v and gate/up cluster GEMMs, fed by per-token
   // sum-of-squares partials from the producers of x (PI05_FUSE_NORM=0: separate rmsnorm launches)
   bool fuse_norm = true;
@@ -1616,6 +1617,7 @@ bool create(pi05_engine* e) {
   if (const char* s = getenv("PI05_PDL")) e->pdl = atoi(s) != 0;
   if (const char* s = getenv("PI05_CLUSTER_SPLITK")) e->cluster_splitk = atoi(s) != 0;
   if (const char* s = getenv("PI05_ATTN_TC")) e->attn_tc = atoi(s) != 0;
+  if (const char* s = getenv("PI05_ATTN_BWD_PIPE")) e->attn_bwd_pipe = atoi(s) != 0;
   if (const char* s = getenv("PI05_WIDE_SWAP")) e->wide_swap = atoi(s) != 0;
   if (const char* s = getenv("PI05_GEMM_WIDE")) e->gemm_wide = atoi(s) != 0;
   if (const char* s = getenv("PI05_GEMM_PAIR")) e->gemm_pair = atoi(s) != 0;

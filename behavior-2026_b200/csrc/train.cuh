@@ -15,6 +15,7 @@
 #pragma once
 #include "attention_bwd.cuh"
 #include "attention_bwd_tc.cuh"
+#include "attention_bwd_dq_pipe.cuh"
 #include "train_kernels.cuh"
 #include "dp_nccl.cuh"
 
@@ -138,6 +139,9 @@ bool attn_bwd_dq(pi05_engine* e, const AttnBwdArgs& a, int nb) {
   }
   if ((a.ld_dq * 2) % 16 || (a.dq_b * 2) % 16 || ((uintptr_t)a.dq & 15))
     return set_err(e, "attention backward: dq rows must be 16-byte aligned");
+  if (e->attn_bwd_pipe)
+    return launch(e, attn_bwd_dq_pipe_kernel, dim3((rows + AttnBwdPipeCfg::ROWS - 1) / AttnBwdPipeCfg::ROWS, 1, nb),
+                  dim3(384), (size_t)AttnBwdPipeCfg::SMEM, false, tq, tdo, tk1, tv1, tk2, tv2, a, e->d_status);
   return launch(e, attn_bwd_dq_tc_kernel, dim3((rows + C::ROWS - 1) / C::ROWS, 1, nb), dim3(384), (size_t)C::SMEM, false,
                 tq, tdo, tk1, tv1, tk2, tv2, a, e->d_status);
 }
@@ -321,6 +325,7 @@ bool lora_create(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
   if (!talloc(e, (void**)&T->dkv_ws, T->dkv_ws_rows * P5_HD * 4)) return false;
   CK(cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DQ));
   CK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdTcCfg::SMEM));
+  CK(cudaFuncSetAttribute(attn_bwd_dq_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdPipeCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_bwd_dkv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdKvCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_bwd_dkv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdKvCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_bwd_dkv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DKV));

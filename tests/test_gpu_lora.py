@@ -190,3 +190,25 @@ def test_lora_fused_geglu_backward_equals_separate_kernel(lora_case, pn, monkeyp
     assert out["1"][0] == out["0"][0]
     np.testing.assert_array_equal(out["1"][1], out["0"][1])
     np.testing.assert_array_equal(out["1"][1], lora_case["g_gpu"])
+
+
+def test_lora_pipelined_dq_backward_equals_one_slot_kernel(lora_case, pn, monkeypatch):
+    """The dQ backward with dS overlapped (S and dP of the next key tile issued ahead, two K slots, dS kept
+    in tensor memory as the A operand) against the one-slot kernel (dS through shared memory): the same
+    64-key tiles, the same bf16 rounding of dS and the same order of the dQ accumulation, so the gradients
+    are bit-identical, run after run."""
+    cfg = pn.Config.make(siglip_layers=1, gemma_layers=2, num_steps=10)
+    imgs, toks, acts, noise, t = lora_case["batch"]
+    out = {}
+    for pipe in ("1", "0", "1"):
+        monkeypatch.setenv("PI05_ATTN_BWD_PIPE", pipe)
+        eng = pn.Engine(cfg, max_batch=2)
+        eng.init_random_weights(4)
+        eng.lora_init(seed=5, micro_batch=2)
+        eng.lora_set_params(lora_case["p0"])
+        eng.lora_zero_grads()
+        out.setdefault(pipe, []).append((eng.lora_accumulate(imgs, toks, acts, noise, t), eng.lora_get_grads()))
+        eng.close()
+    for got in out["1"]:
+        assert got[0] == out["0"][0][0]
+        np.testing.assert_array_equal(got[1], out["0"][0][1])
