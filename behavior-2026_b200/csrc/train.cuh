@@ -192,10 +192,17 @@ bool attn_bwd_dkv(pi05_engine* e, Trainer* T, const AttnBwdArgs& a, int nb) {
   while (splits > 1 && (size_t)nb * kblocks * splits * C::KEYS > T->dkv_ws_rows) --splits;
   const dim3 grid(kblocks, splits, nb);
   for (int dk = 1; dk >= 0; --dk) {
-    const bool ok = dk ? launch(e, attn_bwd_dkv_tc_kernel<true>, grid, dim3(384), (size_t)C::SMEM, false, tk, tv, tqa,
-                                tdoa, tqb, tdob, a, T->dkv_ws, e->d_status)
-                       : launch(e, attn_bwd_dkv_tc_kernel<false>, grid, dim3(384), (size_t)C::SMEM, false, tk, tv, tqa,
-                                tdoa, tqb, tdob, a, T->dkv_ws, e->d_status);
+    const size_t sp = (size_t)AttnBwdKvPipeCfg::SMEM;
+    const bool ok =
+        e->attn_bwd_pipe
+            ? (dk ? launch(e, attn_bwd_dkv_pipe_kernel<true>, grid, dim3(384), sp, false, tk, tv, tqa, tdoa, tqb, tdob,
+                           a, T->dkv_ws, e->d_status)
+                  : launch(e, attn_bwd_dkv_pipe_kernel<false>, grid, dim3(384), sp, false, tk, tv, tqa, tdoa, tqb,
+                           tdob, a, T->dkv_ws, e->d_status))
+        : dk ? launch(e, attn_bwd_dkv_tc_kernel<true>, grid, dim3(384), (size_t)C::SMEM, false, tk, tv, tqa, tdoa, tqb,
+                      tdob, a, T->dkv_ws, e->d_status)
+             : launch(e, attn_bwd_dkv_tc_kernel<false>, grid, dim3(384), (size_t)C::SMEM, false, tk, tv, tqa, tdoa, tqb,
+                      tdob, a, T->dkv_ws, e->d_status);
     if (!ok) return false;
     if (splits > 1) {
       const long n = (long)nb * seg_len * 32;
@@ -326,6 +333,10 @@ bool lora_create(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
   CK(cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DQ));
   CK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdTcCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_bwd_dq_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdPipeCfg::SMEM));
+  CK(cudaFuncSetAttribute(attn_bwd_dkv_pipe_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          AttnBwdKvPipeCfg::SMEM));
+  CK(cudaFuncSetAttribute(attn_bwd_dkv_pipe_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          AttnBwdKvPipeCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_bwd_dkv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdKvCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_bwd_dkv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdKvCfg::SMEM));
   CK(cudaFuncSetAttribute(attn_bwd_dkv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ABW_SMEM_DKV));

@@ -192,11 +192,12 @@ def test_lora_fused_geglu_backward_equals_separate_kernel(lora_case, pn, monkeyp
     np.testing.assert_array_equal(out["1"][1], lora_case["g_gpu"])
 
 
-def test_lora_pipelined_dq_backward_equals_one_slot_kernel(lora_case, pn, monkeypatch):
-    """The dQ backward with dS overlapped (S and dP of the next key tile issued ahead, two K slots, dS kept
-    in tensor memory as the A operand) against the one-slot kernel (dS through shared memory): the same
-    64-key tiles, the same bf16 rounding of dS and the same order of the dQ accumulation, so the gradients
-    are bit-identical, run after run."""
+def test_lora_pipelined_attention_backward_equals_one_slot_kernels(lora_case, pn, monkeypatch):
+    """The attention backward with the dS step overlapped (dQ: S and dP of the next key tile issued ahead,
+    two K slots; dK / dV: S^T and dP^T of the next query tile ahead, two slots for the accumulate's operand;
+    dS kept in tensor memory as the A operand) against the one-slot kernels (dS through shared memory):
+    the same tiles, the same bf16 rounding of dS and the same accumulation order, so the gradients are
+    bit-identical, run after run."""
     cfg = pn.Config.make(siglip_layers=1, gemma_layers=2, num_steps=10)
     imgs, toks, acts, noise, t = lora_case["batch"]
     out = {}
