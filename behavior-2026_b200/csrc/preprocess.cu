@@ -145,4 +145,77 @@ int pi05_absolute_actions(float* actions, int horizon, int dim, const float* sta
   return PI05_OK;
 }
 
+// Cubic resampling of an executed action segment (the PiBehavior wrapper replays 26 actions in 20 steps,
+// π05_네이티브엔진.md:146; there scipy interp1d(kind="cubic")): per dimension, the not-a-knot cubic spline
+// through (i, in[i][j]), i = 0..n_in-1, evaluated at x_k = k (n_in - 1) / (n_out - 1).  The spline's second
+// derivatives M solve, with unit knot spacing, M[i-1] + 4 M[i] + M[i+1] = 6 (y[i-1] - 2 y[i] + y[i+1]) inside
+// and M[0] - 2 M[1] + M[2] = 0, M[n-3] - 2 M[n-2] + M[n-1] = 0 (a continuous third derivative at the
+// second and the second-to-last knot); the system is solved in double precision by Gaussian elimination
+// with partial pivoting.
+int pi05_interp_actions_cubic(const float* in, int n_in, int dim, float* out, int n_out) {
+  if (!in || !out || n_in < 4 || n_in > 4096 || dim < 1 || n_out < 2) return PI05_ERR_ARG;
+  const int n = n_in;
+  std::vector<double> A((size_t)n * n), M(n), y(n);
+  std::vector<int> piv(n);
+  for (int j = 0; j < dim; ++j) {
+    for (int i = 0; i < n; ++i) y[i] = in[(size_t)i * dim + j];
+    std::fill(A.begin(), A.end(), 0.0);
+    A[0] = 1.0, A[1] = -2.0, A[2] = 1.0, M[0] = 0.0;
+    for (int i = 1; i < n - 1; ++i) {
+      A[(size_t)i * n + i - 1] = 1.0, A[(size_t)i * n + i] = 4.0, A[(size_t)i * n + i + 1] = 1.0;
+      M[i] = 6.0 * (y[i - 1] - 2.0 * y[i] + y[i + 1]);
+    }
+    A[(size_t)(n - 1) * n + n - 3] = 1.0, A[(size_t)(n - 1) * n + n - 2] = -2.0, A[(size_t)(n - 1) * n + n - 1] = 1.0;
+    M[n - 1] = 0.0;
+    for (int c = 0; c < n; ++c) {  // forward elimination
+      int p = c;
+      for (int r = c + 1; r < n; ++r)
+        if (std::fabs(A[(size_t)r * n + c]) > std::fabs(A[(size_t)p * n + c])) p = r;
+      if (p != c) {
+        for (int k = 0; k < n; ++k) std::swap(A[(size_t)c * n + k], A[(size_t)p * n + k]);
+        std::swap(M[c], M[p]);
+      }
+      for (int r = c + 1; r < n; ++r) {
+        const double f = A[(size_t)r * n + c] / A[(size_t)c * n + c];
+        if (f == 0.0) continue;
+        for (int k = c; k < n; ++k) A[(size_t)r * n + k] -= f * A[(size_t)c * n + k];
+        M[r] -= f * M[c];
+      }
+    }
+    for (int c = n - 1; c >= 0; --c) {  // back substitution
+      double v = M[c];
+      for (int k = c + 1; k < n; ++k) v -= A[(size_t)c * n + k] * M[k];
+      M[c] = v / A[(size_t)c * n + c];
+    }
+    for (int k = 0; k < n_out; ++k) {
+      const double x = (double)k * (n - 1) / (n_out - 1);
+      const int i = std::min(n - 2, (int)x);
+      const double t = x - i;
+      const double b = y[i + 1] - y[i] - (2.0 * M[i] + M[i + 1]) / 6.0;
+      out[(size_t)k * dim + j] = (float)(y[i] + t * (b + t * (M[i] / 2.0 + t * (M[i + 1] - M[i]) / 6.0)));
+    }
+  }
+  return PI05_OK;
+}
+
+// Stage vote of the PiBehavior wrapper ("2 of the last 3", π05_네이티브엔진.md:146): `recent` holds the
+// last n stage predictions, oldest first; the stage predicted at least twice among the last three is the
+// new stage, otherwise `current` stays.  max_stage > 0 caps the result (the per-task stage count).
+int pi05_stage_vote(const int32_t* recent, int n, int current, int max_stage) {
+  if ((!recent && n > 0) || n < 0) return PI05_ERR_ARG;
+  int vote = current;
+  const int k = std::min(n, 3);
+  const int32_t* last = recent + (n - k);
+  for (int a = 0; a < k; ++a) {
+    int same = 0;
+    for (int b2 = 0; b2 < k; ++b2) same += last[b2] == last[a];
+    if (same >= 2) {
+      vote = last[a];
+      break;
+    }
+  }
+  if (max_stage > 0) vote = std::min(vote, max_stage - 1);
+  return std::max(vote, 0);
+}
+
 }  // extern "C"

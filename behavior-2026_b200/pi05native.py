@@ -23,7 +23,7 @@ EXPORTS = [
     "pi05_save_weights", "pi05_load_weights", "pi05_prefill", "pi05_set_prefix_cache", "pi05_get_prefix_cache",
     "pi05_denoise", "pi05_infer", "pi05_stream", "pi05_sync", "pi05_prefix_len", "pi05_graph_launches",
     "pi05_synth_images", "pi05_synth_tokens", "pi05_synth_noise", "pi05_synth_prefix_cache", "pi05_create_batch",
-    "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_resize_with_pad", "pi05_normalize", "pi05_discretize_state", "pi05_absolute_actions", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
+    "pi05_infer_batch", "pi05_set_stage", "pi05_act_batch", "pi05_reset_slot", "pi05_resize_with_pad", "pi05_normalize", "pi05_discretize_state", "pi05_absolute_actions", "pi05_interp_actions_cubic", "pi05_stage_vote", "pi05_op_linear", "pi05_op_attention", "pi05_op_siglip_attention", "pi05_linear_static",
     "pi05_linear_static_status", "pi05_verify", "pi05_set_act_config", "pi05_act",
     "pi05_nccl_unique_id", "pi05_lora_attach_nccl", "pi05_lora_world",
     "pi05_read_weights_config", "pi05_lora_schedule_lr", "pi05_lora_get_ema", "pi05_tokenizer_load",
@@ -138,6 +138,8 @@ def _load():
     L.pi05_normalize.argtypes = [vp, i32, i32, vp, vp, i32, i32]
     L.pi05_discretize_state.argtypes = [vp, i32, i32, i32, vp]
     L.pi05_absolute_actions.argtypes = [vp, i32, i32, vp, vp]
+    L.pi05_interp_actions_cubic.argtypes = [vp, i32, i32, vp, i32]
+    L.pi05_stage_vote.argtypes = [vp, i32, i32, i32]
     L.pi05_op_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp]
     L.pi05_op_attention.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32]
     L.pi05_op_siglip_attention.argtypes = [vp, i32, vp, vp]
@@ -669,6 +671,26 @@ def absolute_actions(actions, state, mask):
     if rc != 0:
         raise Pi05Error(rc, "pi05_absolute_actions")
     return y
+
+
+def interp_actions_cubic(actions, n_out):
+    """pi05_interp_actions_cubic: actions [n_in][dim] resampled to [n_out][dim] along a not-a-knot cubic spline."""
+    a = _f32(actions)
+    out = np.empty((n_out, a.shape[1]), np.float32)
+    rc = lib.pi05_interp_actions_cubic(a.ctypes.data_as(ctypes.c_void_p), a.shape[0], a.shape[1],
+                                       out.ctypes.data_as(ctypes.c_void_p), n_out)
+    if rc != 0:
+        raise Pi05Error(rc, "pi05_interp_actions_cubic")
+    return out
+
+
+def stage_vote(recent, current, max_stage=0):
+    """pi05_stage_vote: the stage predicted twice among the last three of `recent`, else `current`."""
+    r = np.ascontiguousarray(recent, dtype=np.int32)
+    rc = lib.pi05_stage_vote(r.ctypes.data_as(ctypes.c_void_p), len(r), int(current), int(max_stage))
+    if rc < 0:
+        raise Pi05Error(rc, "pi05_stage_vote")
+    return rc
 
 
 def linear_static(x, w, out, bias=None, stream=None):

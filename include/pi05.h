@@ -324,6 +324,13 @@ PI05_API int pi05_resize_with_pad(const uint8_t* src, int h, int w, int channels
 PI05_API int pi05_normalize(float* x, int n, int dim, const float* a, const float* b, int mode, int inverse);
 PI05_API int pi05_discretize_state(const float* x, int n, int dim, int bins, int32_t* out);
 PI05_API int pi05_absolute_actions(float* actions, int horizon, int dim, const float* state, const uint8_t* mask);
+/* PiBehavior wrapper helpers (π05_네이티브엔진.md:146), host memory, no engine needed:
+ *   pi05_interp_actions_cubic: out[n_out][dim] = the not-a-knot cubic spline through in[n_in][dim] at the
+ *     knots 0..n_in-1, sampled at k (n_in - 1) / (n_out - 1) (scipy interp1d kind="cubic"; n_in >= 4);
+ *   pi05_stage_vote: the stage predicted at least twice among the last three of recent[n] (oldest first),
+ *     else `current`; capped below max_stage when max_stage > 0.  Returns the stage (>= 0) or an error. */
+PI05_API int pi05_interp_actions_cubic(const float* in, int n_in, int dim, float* out, int n_out);
+PI05_API int pi05_stage_vote(const int32_t* recent, int n, int current, int max_stage);
 
 /* Prompt tokenizer (the reference's C++ SentencePiece tokenizer, π05_네이티브엔진.md:83): a SentencePiece BPE
  * model read from its .model file (identity normalization, byte fallback, user-defined symbols; Gemma's

@@ -102,3 +102,35 @@ def test_absolute_actions(pn):
     ref = acts.copy()
     ref[:, mask.astype(bool)] += state[mask.astype(bool)]
     np.testing.assert_array_equal(pn.absolute_actions(acts, state, mask), ref)
+
+
+@pytest.mark.parametrize("n_in,n_out,dim", [(26, 20, 23), (4, 9, 3), (30, 26, 32), (12, 12, 5)])
+def test_interp_actions_cubic_matches_scipy(pn, n_in, n_out, dim):
+    """pi05_interp_actions_cubic against scipy interp1d(kind="cubic") (the not-a-knot spline) over the
+    knots 0..n_in-1 sampled at n_out evenly spaced points of the same span; the engine solves in double
+    precision and rounds once to float32."""
+    interpolate = pytest.importorskip("scipy.interpolate")
+    rng = np.random.default_rng(n_in * 100 + n_out)
+    acts = np.cumsum(rng.normal(0, 0.1, (n_in, dim)), axis=0).astype(np.float32)
+    ref = interpolate.interp1d(np.arange(n_in, dtype=np.float64), acts.astype(np.float64), kind="cubic",
+                               axis=0)(np.linspace(0.0, n_in - 1.0, n_out))
+    got = pn.interp_actions_cubic(acts, n_out)
+    np.testing.assert_allclose(got, ref.astype(np.float32), rtol=0, atol=2e-6 * max(1.0, np.abs(ref).max()))
+    np.testing.assert_array_equal(got[0], acts[0])  # the ends are knots
+    np.testing.assert_allclose(got[-1], acts[-1], rtol=0, atol=1e-6)
+
+
+def test_interp_actions_cubic_rejects_short_segments(pn):
+    with pytest.raises(pn.Pi05Error):
+        pn.interp_actions_cubic(np.zeros((3, 2), np.float32), 5)
+
+
+def test_stage_vote(pn):
+    assert pn.stage_vote([], 2) == 2
+    assert pn.stage_vote([4], 2) == 2
+    assert pn.stage_vote([4, 4], 2) == 4
+    assert pn.stage_vote([1, 3, 3], 1) == 3
+    assert pn.stage_vote([3, 1, 3], 1) == 3
+    assert pn.stage_vote([5, 3, 1, 3], 1) == 3  # only the last three vote
+    assert pn.stage_vote([0, 1, 2], 1) == 1  # no majority: stays
+    assert pn.stage_vote([7, 7, 7], 0, max_stage=5) == 4  # capped below the task's stage count
