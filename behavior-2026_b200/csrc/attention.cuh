@@ -43,6 +43,7 @@ struct AttnArgs {
   long lse_b;
   int force_splits; // > 0: the tensor-core path uses this many key splits instead of choosing
   const int* valid1; // optional (tensor-core path): batch item b attends to the first valid1[b] keys of segment 1
+  int group1;        // > 0 (tensor-core path): query tokens t < group1 attend to segment-1 keys j < group1 only
 };
 
 template <int HD, int NW = 4>

@@ -193,6 +193,9 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
     const uint32_t t_lane = tmem_base + ((uint32_t)(sub * 32) << 16);
     const uint32_t t_o = t_lane + (uint32_t)(C::O_COL + g * (C::HD / 2));
     uint8_t* prow = sP + r * 128;
+    // two prefix attention groups: this row's query token sees segment-1 keys below group1 only
+    const int qtok = (rb * C::ROWS + r) / a.G;
+    const int glim = (a.group1 > 0 && qtok < a.group1) ? a.group1 : 0x7fffffff;
     float m_run = -INFINITY, l_run = 0.f;
     bool alive = true;
     for (int j = 0; j < n; ++j) {
@@ -214,6 +217,7 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
 
       int seg, row0, valid;
       tile_of(t0 + j, seg, row0, valid);
+      if (seg == 0) valid = min(valid, glim - row0);  // may be <= 0: every key of the tile masked for this row
       if (valid < C::KT) {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
@@ -239,7 +243,8 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
         m_run = mt;
         l_run *= alpha;
       }
-      const float msc = m_run * LOG2E;
+      // a row with no key yet (m_run = -inf: masked tiles at the start of a key split) gets p = 0
+      const float msc = m_run == -INFINITY ? 0.f : m_run * LOG2E;
       uint32_t pk[16];
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll

@@ -809,6 +809,7 @@ bool attention_tc(pi05_engine* e, const AttnArgs& a0, int batch) {
 bool attention(pi05_engine* e, const AttnArgs& a0, int batch, int hd) {
   if (hd == P5_HD && a0.G == 8 && a0.qdiv == 1.0f && e->attn_tc && a0.len1 > 0) return attention_tc(e, a0, batch);
   if (a0.valid1) return set_err(e, "the prompt padding mask needs the tensor-core attention (PI05_ATTN_TC=1)");
+  if (a0.group1 > 0) return set_err(e, "prefix attention groups need the tensor-core attention (PI05_ATTN_TC=1)");
   // SigLIP: one CTA per (128 queries, head, image) on tcgen05 up to 32 images; measured per call (CUDA events,
   // 20 launches): 3 images 9.7 vs 14.5 us, 24 images 51.4 vs 55.5 us, 48 images 111.7 vs 101.3 us, 192 images
   // 422.8 vs 378.2 us for the tcgen05 and the mma.sync kernel, so the larger batches take the mma.sync kernel
@@ -1034,6 +1035,7 @@ bool run_gemma(pi05_engine* e, int n) {
     at.qdiv = 1.0f;
     at.splits = 1;
     at.valid1 = e->cfg.text_pad_mask ? e->d_valid + e->s0 : nullptr;
+    at.group1 = e->cfg.prefix_group;
     if (!attention(e, at, n, P5_HD)) return false;
     Lin o{A.po, P5_QDIM, T, g.wo, P5_QDIM, D, P5_QDIM};
     o.epi = EPI_RESID;
@@ -1710,6 +1712,7 @@ void pi05_default_config(pi05_config* c) {
   if (!c) return;
   c->batch_invariant = 0;
   c->text_pad_mask = 0;
+  c->prefix_group = 0;
   c->siglip_layers = 27;
   c->gemma_layers = 18;
   c->expert_layers = 18;
@@ -1730,7 +1733,7 @@ pi05_engine* pi05_create(const pi05_config* c, int device, int max_batch, char* 
   if (cfg.siglip_layers < 0 || cfg.gemma_layers < 1 || cfg.expert_layers != cfg.gemma_layers || cfg.num_steps < 1 ||
       cfg.n_cameras < 1 || cfg.n_text < 0 || cfg.horizon < 1 || cfg.horizon > 128 || max_batch < 1 ||
       (cfg.batch_invariant != 0 && cfg.batch_invariant != 1) || (cfg.text_pad_mask != 0 && cfg.text_pad_mask != 1) ||
-      max_batch > 32767)
+      cfg.prefix_group < 0 || cfg.prefix_group > cfg.n_cameras * P5_SIG_TOK + cfg.n_text || max_batch > 32767)
     return fail("pi05_create: invalid configuration");
   pi05_engine* e = new pi05_engine();
   e->cfg = cfg;

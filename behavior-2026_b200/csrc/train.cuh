@@ -866,8 +866,9 @@ int pi05_lora_init(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
   pi05_lora_config cfg;
   pi05_lora_default_config(&cfg);
   if (c) cfg = *c;
-  if (e->cfg.text_pad_mask) {
-    e->err = "pi05_lora_init: the LoRA step trains on full prompts (text_pad_mask must be 0)";
+  if (e->cfg.text_pad_mask || e->cfg.prefix_group) {
+    e->err = "pi05_lora_init: the LoRA step trains on full prompts with one prefix attention group "
+             "(text_pad_mask and prefix_group must be 0)";
     return PI05_ERR_ARG;
   }
   if (cfg.rank != 16 || cfg.alpha != 32.0f || cfg.micro_batch < 1) {

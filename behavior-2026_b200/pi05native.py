@@ -41,13 +41,13 @@ class Pi05Error(RuntimeError):
 class Config(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in
                 ("siglip_layers", "gemma_layers", "expert_layers", "num_steps", "n_cameras", "n_text", "horizon",
-                 "batch_invariant", "text_pad_mask")]
+                 "batch_invariant", "text_pad_mask", "prefix_group")]
 
     @classmethod
     def make(cls, siglip_layers=27, gemma_layers=18, num_steps=10, n_cameras=3, n_text=200, horizon=50,
-             batch_invariant=0, text_pad_mask=0):
+             batch_invariant=0, text_pad_mask=0, prefix_group=0):
         return cls(siglip_layers, gemma_layers, gemma_layers, num_steps, n_cameras, n_text, horizon, batch_invariant,
-                   text_pad_mask)
+                   text_pad_mask, prefix_group)
 
     @property
     def prefix_len(self):

@@ -64,6 +64,11 @@ typedef struct {
    * all n_text prompt positions are attended to (the benchmarks' full 200-token prompts).  Inference only
    * (pi05_lora_init refuses it), and it needs the tensor-core attention and the fused RoPE projections. */
   int32_t text_pad_mask;
+  /* > 0: two attention groups in the prefix, as the PiBehavior variant's images + base task block
+   * (π05_네이티브엔진.md:138, "softmax kernel with a group-boundary argument"): prefix queries t < prefix_group
+   * attend to the prefix keys j < prefix_group only; the later prefix tokens and the action tokens attend
+   * to the whole prefix.  0 (default): one group.  Inference only, on the tensor-core attention. */
+  int32_t prefix_group;
 } pi05_config;
 
 PI05_API void pi05_default_config(pi05_config* c);

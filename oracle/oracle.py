@@ -18,6 +18,11 @@ LIB_PATH = os.path.join(HERE, "libpi05_oracle.so")
 K_IN_IMAGE, K_IN_TOKENS, K_IN_NOISE, K_IN_KCACHE, K_IN_VCACHE, K_IN_ACTIONS, K_IN_TRAIN_NOISE = range(120, 127)
 FP32_ACTIVATIONS = 1
 TEXT_PAD_MASK = 2  # trailing prompt ids 0 are padding, masked as openpi masks it
+
+
+def PREFIX_GROUP(g):
+    """flags: prefix queries t < g attend to keys j < g only (two attention groups in the prefix)"""
+    return int(g) << 16
 HD = 256
 GEM_W = 2048
 

@@ -181,8 +181,9 @@ void rope(const Run& r, float* x, int T, int nheads, int ld, int pos0, const flo
 // softmax(q k^T) v for `nh` query heads of width hd.  Query head h reads key/value head
 // (kv_per_head ? h : 0) (MHA vs MQA).  q already scaled.  logits and softmax in fp32,
 // probabilities rounded to the activation dtype before the value product (openpi gemma.Attention).
+// group > 0: queries t < group attend to the keys j < group only (two attention groups in the prefix).
 void attention(const Run& r, int T, int S, int nh, int hd, const float* q, int ldq, const float* k, int ldk,
-               const float* v, int ldv, bool kv_per_head, float* out, int ldo) {
+               const float* v, int ldv, bool kv_per_head, float* out, int ldo, int group = 0) {
   Vf logits((size_t)T * S), vt((size_t)hd * S), o((size_t)T * hd);
   for (int h = 0; h < nh; ++h) {
     const int kvh = kv_per_head ? h : 0;
@@ -190,14 +191,16 @@ void attention(const Run& r, int T, int S, int nh, int hd, const float* q, int l
 #pragma omp parallel for schedule(static)
     for (int t = 0; t < T; ++t) {
       float* l = logits.data() + (size_t)t * S;
+      const int lim = (group > 0 && t < group) ? std::min(S, group) : S;
       float m = -INFINITY;
-      for (int j = 0; j < S; ++j) m = std::max(m, l[j]);
+      for (int j = 0; j < lim; ++j) m = std::max(m, l[j]);
       float sum = 0.f;
-      for (int j = 0; j < S; ++j) {
+      for (int j = 0; j < lim; ++j) {
         l[j] = std::exp(l[j] - m);
         sum += l[j];
       }
-      for (int j = 0; j < S; ++j) l[j] = r.R(l[j] / sum);
+      for (int j = 0; j < lim; ++j) l[j] = r.R(l[j] / sum);
+      for (int j = lim; j < S; ++j) l[j] = 0.f;
     }
     transpose(v + kvh * hd, S, hd, ldv, vt.data());
     gemm_nt(T, hd, S, logits.data(), S, vt.data(), S, o.data(), hd);
@@ -302,7 +305,8 @@ void prefill(const p5o_config* c, uint64_t seed, Vf& x, int P, float* kc, float*
     r.point("pre.l" + std::to_string(l) + ".k", kk.data(), kk.size());
     r.point("pre.l" + std::to_string(l) + ".v", vv.data(), vv.size());
     if (l == c->gemma_layers - 1) break;  // the last layer's output feeds only the unused final norm
-    attention(r, P, S, P5_NH, P5_HD, q.data(), P5_QDIM, kk.data(), P5_HD, vv.data(), P5_HD, false, o.data(), P5_QDIM);
+    attention(r, P, S, P5_NH, P5_HD, q.data(), P5_QDIM, kk.data(), P5_HD, vv.data(), P5_HD, false, o.data(), P5_QDIM,
+              p5o_prefix_group(r.flags));
     linear(r, P, D, P5_QDIM, o.data(), wo.data(), nullptr, y.data());
     for (size_t i = 0; i < x.size(); ++i) x[i] = r.R(x[i] + y[i]);
     wq.clear(); wq.shrink_to_fit();

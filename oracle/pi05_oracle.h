@@ -31,6 +31,11 @@ typedef struct {
  * queries attend to the first p5o_valid_prefix() keys only, and the denoise is then run on that many
  * cache rows (its action tokens' positions follow them). */
 enum { P5O_FP32_ACTIVATIONS = 1, P5O_TEXT_PAD_MASK = 2 };
+/* Two attention groups in the prefix (the PiBehavior variant's image + base-task block): flags carrying
+ * P5O_PREFIX_GROUP(g) make prefix queries t < g attend to the keys j < g only; the others, and the action
+ * tokens, attend to the whole prefix. */
+#define P5O_PREFIX_GROUP(g) ((int)(g) << 16)
+static inline int p5o_prefix_group(int flags) { return (flags >> 16) & 0x7fff; }
 
 /* Named intermediate points (names follow the reference verifier: img.tokens, pre.lN.k, suf.sN.v, ...). */
 typedef void (*p5o_probe_fn)(const char* name, const float* data, int64_t n, void* ctx);

@@ -32,7 +32,7 @@ def test_default_config(pn):
     c = pn.Config()
     pn.lib.pi05_default_config(ctypes.byref(c))
     assert c.as_dict() == dict(siglip_layers=27, gemma_layers=18, expert_layers=18, num_steps=10, n_cameras=3,
-                               n_text=200, horizon=50, batch_invariant=0, text_pad_mask=0)
+                               n_text=200, horizon=50, batch_invariant=0, text_pad_mask=0, prefix_group=0)
     assert c.prefix_len == 968
 
 

@@ -80,3 +80,44 @@ def test_tokenized_prompt_through_act(pn, oracle, tmp_path):
     eng.close()
     ref = oracle.infer(oracle.Config.make(**SMALL), 22, img, ids, noise, flags=oracle.TEXT_PAD_MASK)
     assert np.abs(a[0] - ref[0]).max() <= 2e-2 and cos(a[0], ref[0]) >= 0.999
+
+
+@pytest.mark.parametrize("depth,group", [("small", 769), ("small", 500), ("small", 768), ("full", 769)])
+def test_prefix_groups_match_oracle(pn, oracle, depth, group):
+    """Two attention groups in the prefix (pi05_config.prefix_group, the PiBehavior variant's image + base
+    task block): prefix queries t < group attend to keys j < group only, on the tensor-core attention
+    (per-row key limits, key splits that start past the group boundary) against the oracle with the same
+    masking; 500 splits a 16-token query block, 768 ends on one.  Batch of two at reduced depth."""
+    kw = SMALL if depth == "small" else {}
+    n = 2 if depth == "small" else 1
+    eng = pn.Engine(pn.Config.make(**kw, prefix_group=group), max_batch=n)
+    eng.init_random_weights(27)
+    imgs = np.stack([pn.synth_images(28, i) for i in range(n)])
+    toks = np.stack([pn.synth_tokens(28, i) for i in range(n)])
+    noise = np.stack([pn.synth_noise(28, i) for i in range(n)])
+    act = eng.infer(imgs, toks, noise)
+    eng.close()
+    ocfg = oracle.Config.make(**kw)
+    for i in range(n):
+        ref = oracle.infer(ocfg, 27, imgs[i], toks[i], noise[i], flags=oracle.PREFIX_GROUP(group))
+        d, c = float(np.abs(act[i] - ref).max()), cos(act[i], ref)
+        print(f"{depth} group {group} sample {i}: max-abs {d:.3e} cos {c:.6f}")
+        assert d <= 2e-2 and c >= 0.999, (group, i, d, c)
+        if i == 0:
+            plain = oracle.infer(ocfg, 27, imgs[i], toks[i], noise[i])
+            # the engine is nearer the grouped oracle than the ungrouped one
+            assert np.abs(act[i] - ref).max() < np.abs(act[i] - plain).max()
+            if depth == "full":  # through 18 layers the groups move the chunk by more than twice the tolerance
+                assert np.abs(plain - ref).max() > 2 * 2e-2
+                assert np.abs(act[i] - plain).max() > 2e-2
+
+
+def test_prefix_groups_refused_where_unsupported(pn):
+    """The LoRA step trains one attention group; a group past the prefix is an invalid configuration."""
+    eng = pn.Engine(pn.Config.make(**SMALL, prefix_group=769), max_batch=1)
+    eng.init_random_weights(29)
+    with pytest.raises(pn.Pi05Error, match="prefix_group"):
+        eng.lora_init(seed=1, micro_batch=1)
+    eng.close()
+    with pytest.raises(pn.Pi05Error):
+        pn.Engine(pn.Config.make(**SMALL, prefix_group=969), max_batch=1)

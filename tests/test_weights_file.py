@@ -18,7 +18,7 @@ def test_pi05w_round_trip_bf16_and_f32(pn, tmp_path):
             want = t[k] if dt == "f32" else pn.bf16_bits_to_f32(pn.f32_to_bf16_bits(t[k])).reshape(t[k].shape)
             np.testing.assert_array_equal(t2[k], want)
         c = pn.read_weights_config(path)
-        assert c.as_dict() == dict(cfg, batch_invariant=0, text_pad_mask=0)
+        assert c.as_dict() == dict(cfg, batch_invariant=0, text_pad_mask=0, prefix_group=0)
 
 
 def test_reference_layout_conversion_shapes(pn):
