@@ -133,6 +133,14 @@ struct pi05_engine {
   std::vector<int> act_next;
   std::vector<long> act_plans;
   float* noise_chol = nullptr;  // [horizon*32][horizon*32] lower-triangular factor of the noise covariance
+  // soft inpainting (pi05_set_inpaint): the first inp_fixed action rows are held to known values after
+  // the steps that start above inp_tmin; inp_corr [U][K] = Sigma_UO Sigma_OO^-1, inp_known
+  // [max_batch][K], inp_on [max_batch] (0 = that batch position denoises freely), inp_eps the step-0
+  // noise of the batch (K = inp_fixed * 32, U = horizon * 32 - K)
+  int inp_fixed = 0;
+  float inp_tmin = 0.f;
+  float *inp_corr = nullptr, *inp_known = nullptr, *inp_eps = nullptr;
+  int* inp_on = nullptr;
   // device staging of pi05_act_batch's camera frames: host frames, resize tap tables, frame jobs
   uint8_t* frame_stage = nullptr;
   size_t frame_stage_bytes = 0;
@@ -1225,7 +1233,7 @@ bool run_denoise_mega(pi05_engine* e) {
 }
 
 bool run_denoise_body(pi05_engine* e, int n) {
-  if (mega_applies(e, n) && !e->probe_fn && !e->plant_fn && e->s0 == 0 && !e->cfg.text_pad_mask)
+  if (mega_applies(e, n) && !e->probe_fn && !e->plant_fn && e->s0 == 0 && !e->cfg.text_pad_mask && !e->inp_fixed)
     return run_denoise_mega(e);
   const int H = e->cfg.horizon, T = n * H, D = P5_EXP_W, P = e->P;
   Acts& A = e->A;
@@ -1235,6 +1243,20 @@ bool run_denoise_body(pi05_engine* e, int n) {
   const int MW = e->NM * 3 * D;  // modulation row width
   const float dtb = p5_dt_bf16(e->cfg.num_steps);
   const int attn_splits = n <= 4 ? 8 : 1;
+  // soft inpainting: the step-0 noise is kept, the flow time after step s is tsched[s + 1] (the same fp32
+  // accumulation as the time conditioning's schedule)
+  const int inp_k = e->inp_fixed * P5_ACT_D;
+  std::vector<float> tsched(e->cfg.num_steps + 1);
+  {
+    const float dt = (float)(-1.0 / (double)e->cfg.num_steps);
+    float t = 1.0f;
+    for (int s = 0; s <= e->cfg.num_steps; ++s) {
+      tsched[s] = t;
+      t = t + dt;
+    }
+  }
+  if (inp_k > 0)
+    CK(cudaMemcpyAsync(e->inp_eps, xt, (size_t)T * P5_ACT_D * 4, cudaMemcpyDeviceToDevice, e->stream));
   // fused adaRMSNorm: x's producers (action_in, O and down projections) write per-token sums of squares
   // over 16-feature groups; the q/k/v and gate/up projections read x and normalise it on chip
   const bool fnorm = fused_norm_applies(e, n);
@@ -1361,6 +1383,11 @@ bool run_denoise_body(pi05_engine* e, int n) {
     if (!launch(e, action_out_euler_kernel, dim3(rows_grid((long)T * P5_ACT_D)), dim3(256), 0, true,
                 (const bf16*)A.eh, (const bf16*)e->aout_w, (const bf16*)e->aout_b, xt,
                 (e->probe_fn || e->plant_fn) ? A.actions : (float*)nullptr, T, D, dtb))
+      return false;
+    if (inp_k > 0 && tsched[s] > e->inp_tmin &&
+        !launch(e, inpaint_kernel, dim3(n), dim3(1024), (size_t)inp_k * 4, false, xt, (const float*)e->inp_eps,
+                (const float*)e->inp_known, (const int*)e->inp_on, (const float*)e->inp_corr, e->s0, H, inp_k,
+                tsched[s + 1]))
       return false;
     if (!emit_f32(e, sp + ".v", A.actions, (long)H * P5_ACT_D) || !emit_f32(e, sp + ".x", xt, (long)H * P5_ACT_D))
       return false;
@@ -2680,6 +2707,59 @@ int pi05_set_noise_cholesky(pi05_engine* e, const float* L, int dim) {
   cudaSetDevice(e->device);
   if (!e->noise_chol && !dalloc(e, (void**)&e->noise_chol, (size_t)nz * nz * 4)) return PI05_ERR_CUDA;
   if (cudaMemcpyAsync(e->noise_chol, L, (size_t)nz * nz * 4, cudaMemcpyDefault, e->stream) != cudaSuccess)
+    return PI05_ERR_CUDA;
+  return pi05_sync(e);
+}
+
+int pi05_set_inpaint(pi05_engine* e, int fixed, float t_min, const float* corr) {
+  if (!e) return PI05_ERR_ARG;
+  const int H = e->cfg.horizon;
+  if (fixed < 0 || fixed >= H || fixed * P5_ACT_D * 4 > 48 * 1024 || (fixed > 0 && !corr) || !(t_min == t_min)) {
+    set_err(e, "pi05_set_inpaint: fixed must be in [0, horizon) and at most 384 rows, corr given when fixed > 0");
+    return PI05_ERR_ARG;
+  }
+  cudaSetDevice(e->device);
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess) return PI05_ERR_CUDA;
+  // the denoise graphs hold the inpainting launches (or their absence): capture them again
+  for (auto& kv : e->denoise_graphs) cudaGraphExecDestroy(kv.second);
+  e->denoise_graphs.clear();
+  e->denoise_launches.clear();
+  auto drop = [&](void* p) {
+    if (!p) return;
+    cudaFree(p);
+    e->allocs.erase(std::find(e->allocs.begin(), e->allocs.end(), p));
+  };
+  drop(e->inp_corr);
+  e->inp_corr = nullptr;
+  e->inp_fixed = 0;
+  if (fixed == 0) return PI05_OK;
+  const int K = fixed * P5_ACT_D, U = H * P5_ACT_D - K;
+  const size_t nz = (size_t)e->max_batch * H * P5_ACT_D;
+  if (!dalloc(e, (void**)&e->inp_corr, (size_t)U * K * 4)) return PI05_ERR_CUDA;
+  // the known rows and the per-position switches keep their size for the engine's life (K <= horizon*32)
+  if (!e->inp_known && !dalloc(e, (void**)&e->inp_known, nz * 4)) return PI05_ERR_CUDA;
+  if (!e->inp_eps && !dalloc(e, (void**)&e->inp_eps, nz * 4)) return PI05_ERR_CUDA;
+  if (!e->inp_on && !dalloc(e, (void**)&e->inp_on, (size_t)e->max_batch * sizeof(int))) return PI05_ERR_CUDA;
+  if (cudaMemsetAsync(e->inp_on, 0, (size_t)e->max_batch * sizeof(int), e->stream) != cudaSuccess ||
+      cudaMemcpyAsync(e->inp_corr, corr, (size_t)U * K * 4, cudaMemcpyDefault, e->stream) != cudaSuccess)
+    return PI05_ERR_CUDA;
+  e->inp_fixed = fixed;
+  e->inp_tmin = t_min;
+  return pi05_sync(e);
+}
+
+int pi05_set_inpaint_known(pi05_engine* e, int sample, const float* known) {
+  if (!e || sample < 0 || sample >= e->max_batch) return PI05_ERR_ARG;
+  if (!e->inp_fixed) {
+    set_err(e, "pi05_set_inpaint_known: inpainting is off (call pi05_set_inpaint first)");
+    return PI05_ERR_STATE;
+  }
+  cudaSetDevice(e->device);
+  const int K = e->inp_fixed * P5_ACT_D, on = known ? 1 : 0;
+  if (known && cudaMemcpyAsync(e->inp_known + (size_t)sample * K, known, (size_t)K * 4, cudaMemcpyDefault,
+                               e->stream) != cudaSuccess)
+    return PI05_ERR_CUDA;
+  if (cudaMemcpyAsync(e->inp_on + sample, &on, sizeof(int), cudaMemcpyHostToDevice, e->stream) != cudaSuccess)
     return PI05_ERR_CUDA;
   return pi05_sync(e);
 }

@@ -298,6 +298,38 @@ __global__ void correlate_noise_kernel(const float* L, const float* eps, float* 
   if (lane == 0) z[(size_t)k * dim + i] = (float)acc;
 }
 
+// ---------------------------------------------------------------- soft inpainting (one CTA per sample)
+// After an Euler step that lands at time t, for the samples whose known rows are on: the first K values
+// of the chunk (K = fixed rows x 32) are put back on the flow path of the known actions,
+// x_K <- t eps_K + (1 - t) a_K (eps the step-0 noise), and the rest follows the Gaussian conditional,
+// x_U += C (x_K,new - x_K,old), C = Sigma_UO Sigma_OO^-1 [U][K].  Unfused fp32 for the known rows, the
+// correction accumulated in fp64 (one warp per row of C) and rounded once.  Dynamic smem: K floats.
+__global__ void inpaint_kernel(float* xt, const float* eps, const float* known, const int* on, const float* C,
+                               int s0, int horizon, int K, float t) {
+  extern __shared__ float delta[];
+  const int b = blockIdx.x, sample = s0 + b;
+  if (!on[sample]) return;  // uniform for the CTA
+  const int n = horizon * P5_ACT_D, U = n - K;
+  float* x = xt + (size_t)b * n;
+  const float* e = eps + (size_t)b * n;
+  const float* a = known + (size_t)sample * K;
+  const float omt = __fsub_rn(1.0f, t);
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = __fadd_rn(__fmul_rn(t, e[k]), __fmul_rn(omt, a[k]));
+    delta[k] = __fsub_rn(v, x[k]);
+    x[k] = v;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int u = warp; u < U; u += nw) {
+    const float* cr = C + (size_t)u * K;
+    double acc = 0.0;
+    for (int k = lane; k < K; k += 32) acc += (double)cr[k] * (double)delta[k];
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) x[K + u] = __fadd_rn(x[K + u], (float)acc);
+  }
+}
+
 // ---------------------------------------------------------------- time MLP (fp32, one warp per output)
 // y[s][o] = swish(sum_k x[s][k] W[o][k] + b[o]); optional bf16 copy (input of the bf16 modulation Dense)
 __global__ void linear_swish_f32_kernel(const float* x, const bf16* W, const bf16* b, float* y, bf16* ybf, int S,

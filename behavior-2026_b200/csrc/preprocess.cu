@@ -146,7 +146,7 @@ int pi05_absolute_actions(float* actions, int horizon, int dim, const float* sta
 }
 
 // Cubic resampling of an executed action segment (the PiBehavior wrapper replays 26 actions in 20 steps,
-// π05_네이티브엔진.md:146; there scipy interp1d(kind="cubic")): per dimension, the not-a-knot cubic spline
+// π05_네이티브엔진.md:143 and :146; there scipy interp1d(kind="cubic")): per dimension, the not-a-knot cubic spline
 // through (i, in[i][j]), i = 0..n_in-1, evaluated at x_k = k (n_in - 1) / (n_out - 1).  The spline's second
 // derivatives M solve, with unit knot spacing, M[i-1] + 4 M[i] + M[i+1] = 6 (y[i-1] - 2 y[i] + y[i+1]) inside
 // and M[0] - 2 M[1] + M[2] = 0, M[n-3] - 2 M[n-2] + M[n-1] = 0 (a continuous third derivative at the
@@ -198,7 +198,7 @@ int pi05_interp_actions_cubic(const float* in, int n_in, int dim, float* out, in
   return PI05_OK;
 }
 
-// Stage vote of the PiBehavior wrapper ("2 of the last 3", π05_네이티브엔진.md:146): `recent` holds the
+// Stage vote of the PiBehavior wrapper ("2 of the last 3", π05_네이티브엔진.md:143): `recent` holds the
 // last n stage predictions, oldest first; the stage predicted at least twice among the last three is the
 // new stage, otherwise `current` stays.  max_stage > 0 caps the result (the per-task stage count).
 int pi05_stage_vote(const int32_t* recent, int n, int current, int max_stage) {

@@ -28,7 +28,7 @@ EXPORTS = [
     "pi05_nccl_unique_id", "pi05_lora_attach_nccl", "pi05_lora_world",
     "pi05_read_weights_config", "pi05_lora_schedule_lr", "pi05_lora_get_ema", "pi05_tokenizer_load",
     "pi05_tokenizer_free", "pi05_tokenizer_vocab_size", "pi05_tokenizer_encode", "pi05_tokenize_prompt",
-    "pi05_set_noise_cholesky", "pi05_verify_planted",
+    "pi05_set_noise_cholesky", "pi05_set_inpaint", "pi05_set_inpaint_known", "pi05_verify_planted",
 ]
 
 
@@ -180,6 +180,8 @@ def _load():
     L.pi05_lora_world.argtypes = [vp]
     L.pi05_act.argtypes = [vp, i32, vp, vp, vp, vp, vp]
     L.pi05_set_noise_cholesky.argtypes = [vp, vp, i32]
+    L.pi05_set_inpaint.argtypes = [vp, i32, ctypes.c_float, vp]
+    L.pi05_set_inpaint_known.argtypes = [vp, i32, vp]
     L.pi05_lora_save_state.argtypes = [vp, ctypes.c_char_p]
     L.pi05_lora_load_state.argtypes = [vp, ctypes.c_char_p]
     return L
@@ -489,6 +491,26 @@ class Engine:
             return
         Lc = np.ascontiguousarray(L, np.float32)
         self._check(lib.pi05_set_noise_cholesky(self._h, Lc.ctypes.data, Lc.shape[0]))
+
+    def set_inpaint(self, fixed=0, t_min=0.3, corr=None):
+        """pi05_set_inpaint: soft inpainting of the first `fixed` action rows after the steps that start above
+        t_min, the rest corrected by corr [(horizon - fixed) * 32][fixed * 32]; fixed = 0 switches it off"""
+        if not fixed:
+            self._check(lib.pi05_set_inpaint(self._h, 0, float(t_min), None))
+            return
+        c = np.ascontiguousarray(corr, np.float32)
+        H = self.config.horizon
+        if c.shape != ((H - fixed) * 32, fixed * 32):
+            raise ValueError(f"corr must be [{(H - fixed) * 32}][{fixed * 32}], got {c.shape}")
+        self._check(lib.pi05_set_inpaint(self._h, int(fixed), float(t_min), c.ctypes.data))
+
+    def set_inpaint_known(self, sample, known):
+        """pi05_set_inpaint_known: the known rows [fixed][32] of batch position `sample`, None = free"""
+        if known is None:
+            self._check(lib.pi05_set_inpaint_known(self._h, int(sample), None))
+            return
+        k = np.ascontiguousarray(known, np.float32)
+        self._check(lib.pi05_set_inpaint_known(self._h, int(sample), k.ctypes.data))
 
     @staticmethod
     def _frames(frames):

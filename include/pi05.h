@@ -305,9 +305,22 @@ PI05_API int pi05_act_batch(pi05_engine* e, int n, const int* slots, const pi05_
 /* Correlated noise for the re-plans whose noise the engine draws (pi05_act_batch with noise NULL): each
  * slot's standard-normal draw eps over the flattened chunk (index t*32 + j) becomes L . eps, L the
  * lower-triangular [dim][dim] factor of the covariance (dim = horizon * 32; the reference's PiBehavior
- * model drew N(0, 0.5 I + 0.5 Sigma) with a Cholesky factor computed in f64 at export, π05_네이티브엔진.md:139).
+ * model drew N(0, 0.5 I + 0.5 Sigma) with a Cholesky factor computed in f64 at export, π05_네이티브엔진.md:141).
  * Accumulated in fp64 on the device.  L = NULL returns to uncorrelated noise. */
 PI05_API int pi05_set_noise_cholesky(pi05_engine* e, const float* L, int dim);
+/* Soft inpainting of the denoise (the reference's PiBehavior model, π05_네이티브엔진.md:142: the first four
+ * actions of a chunk held to the ones already committed, only at flow times above 0.3, the rest corrected
+ * through Sigma_UO Sigma_OO^-1, an 832 x 128 matrix computed at export).  With K = fixed * 32 and
+ * U = horizon * 32 - K, after every Euler step that starts at a time t_s > t_min and lands at t, each batch
+ * position whose known rows are on gets
+ *   x[0:K] <- t eps[0:K] + (1 - t) known,   x[K:] += corr . (x[0:K],new - x[0:K],old)
+ * eps the position's step-0 noise, corr f32 [U][K] row-major (host or device).  fixed = 0 switches
+ * inpainting off; 1 <= fixed < horizon (and fixed <= 384).  Every position starts switched off.  A batch
+ * position is the sample's index in a pi05_denoise / pi05_infer / pi05_infer_batch call. */
+PI05_API int pi05_set_inpaint(pi05_engine* e, int fixed, float t_min, const float* corr);
+/* The known rows of batch position `sample`: known f32 [fixed][32] in the model's (normalised) action
+ * space, host or device; NULL switches the position back to free denoising. */
+PI05_API int pi05_set_inpaint_known(pi05_engine* e, int sample, const float* known);
 /* pi05_act_batch for one slot (the reference's single-slot pi05_act). */
 PI05_API int pi05_act(pi05_engine* e, int slot, const pi05_frame* frames, const int32_t* tokens, const float* state,
                       const float* noise, float* out);
@@ -329,7 +342,7 @@ PI05_API int pi05_resize_with_pad(const uint8_t* src, int h, int w, int channels
 PI05_API int pi05_normalize(float* x, int n, int dim, const float* a, const float* b, int mode, int inverse);
 PI05_API int pi05_discretize_state(const float* x, int n, int dim, int bins, int32_t* out);
 PI05_API int pi05_absolute_actions(float* actions, int horizon, int dim, const float* state, const uint8_t* mask);
-/* PiBehavior wrapper helpers (π05_네이티브엔진.md:146), host memory, no engine needed:
+/* PiBehavior wrapper helpers (π05_네이티브엔진.md:143, checked at :146), host memory, no engine needed:
  *   pi05_interp_actions_cubic: out[n_out][dim] = the not-a-knot cubic spline through in[n_in][dim] at the
  *     knots 0..n_in-1, sampled at k (n_in - 1) / (n_out - 1) (scipy interp1d kind="cubic"; n_in >= 4);
  *   pi05_stage_vote: the stage predicted at least twice among the last three of recent[n] (oldest first),

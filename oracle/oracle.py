@@ -65,6 +65,8 @@ def lib():
                                            ctypes.c_void_p]
         L.p5o_denoise.argtypes = [cfg, ctypes.c_uint64, f32, f32, ctypes.c_int, f32, f32, ctypes.c_int, PROBE,
                                   ctypes.c_void_p]
+        L.p5o_denoise_inpaint.argtypes = [cfg, ctypes.c_uint64, f32, f32, ctypes.c_int, f32, f32, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_float, f32, f32]
         L.p5o_prefix_embed.argtypes = [cfg, ctypes.c_uint64, u8, i32, f32, ctypes.c_int]
         L.p5o_valid_prefix.argtypes = [cfg, i32, ctypes.c_int]
         L.p5o_gen_images.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, u8]
@@ -189,12 +191,24 @@ def prefill_embedded(cfg, seed, emb, flags=0, probe=None):
     return k, v
 
 
-def denoise(cfg, seed, kcache, vcache, noise, flags=0, probe=None):
+def denoise(cfg, seed, kcache, vcache, noise, flags=0, probe=None, inpaint=None):
+    """inpaint = (known [fixed][32], corr [(horizon - fixed) * 32][fixed * 32], t_min): soft inpainting"""
     kcache = np.ascontiguousarray(kcache, np.float32)
     vcache = np.ascontiguousarray(vcache, np.float32)
     noise = np.ascontiguousarray(noise, np.float32)
     P = kcache.shape[1]
     out = np.empty_like(noise)
+    if inpaint is not None:
+        assert probe is None
+        known, corr, t_min = inpaint
+        known = np.ascontiguousarray(known, np.float32)
+        corr = np.ascontiguousarray(corr, np.float32)
+        rc = lib().p5o_denoise_inpaint(ctypes.byref(cfg), seed, _p(kcache, ctypes.c_float),
+                                       _p(vcache, ctypes.c_float), P, _p(noise, ctypes.c_float),
+                                       _p(out, ctypes.c_float), flags, known.shape[0], t_min,
+                                       _p(known, ctypes.c_float), _p(corr, ctypes.c_float))
+        assert rc == 0
+        return out
     rc = lib().p5o_denoise(ctypes.byref(cfg), seed, _p(kcache, ctypes.c_float), _p(vcache, ctypes.c_float), P,
                            _p(noise, ctypes.c_float), _p(out, ctypes.c_float), flags, *_probe_args(probe))
     assert rc == 0
@@ -206,7 +220,7 @@ def valid_prefix(cfg, tokens, flags=0):
     return lib().p5o_valid_prefix(ctypes.byref(cfg), _p(tokens, ctypes.c_int32), flags)
 
 
-def infer(cfg, seed, images, tokens, noise, flags=0, probe=None):
+def infer(cfg, seed, images, tokens, noise, flags=0, probe=None, inpaint=None):
     k, v = prefill(cfg, seed, images, tokens, flags, probe)
     s = valid_prefix(cfg, tokens, flags)  # with TEXT_PAD_MASK the padding's cache rows are left out
-    return denoise(cfg, seed, k[:, :s], v[:, :s], noise, flags, probe)
+    return denoise(cfg, seed, k[:, :s], v[:, :s], noise, flags, probe, inpaint)

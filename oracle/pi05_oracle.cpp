@@ -339,8 +339,36 @@ struct ExpertLayer {
   Vf wq, wk, wv, wo, wg, wu, wd;
 };
 
+// Soft inpainting of the PiBehavior model (π05_네이티브엔진.md:142): after an Euler step that starts above
+// t_min and lands at t, the first K chunk values go back on the flow path of the known actions and the
+// rest follow the Gaussian conditional through C = Sigma_UO Sigma_OO^-1.  fp32 without contraction for the
+// known values, the correction summed in fp64 and rounded once.
+struct Inpaint {
+  int K = 0;
+  float t_min = 0.f;
+  const float* known = nullptr;  // [K]
+  const float* corr = nullptr;   // [U][K]
+};
+
+void inpaint_step(const Inpaint& ip, const float* eps, float* x, int n, float t) {
+  const int K = ip.K, U = n - K;
+  const float omt = 1.0f - t;
+  std::vector<float> delta(K);
+  for (int k = 0; k < K; ++k) {
+    const float a = t * eps[k], b = omt * ip.known[k];
+    const float v = a + b;
+    delta[k] = v - x[k];
+    x[k] = v;
+  }
+  for (int u = 0; u < U; ++u) {
+    double acc = 0.0;
+    for (int k = 0; k < K; ++k) acc += (double)ip.corr[(size_t)u * K + k] * (double)delta[k];
+    x[K + u] = x[K + u] + (float)acc;
+  }
+}
+
 void denoise(const p5o_config* c, uint64_t seed, const float* kc, const float* vc, int P, const float* noise,
-             float* actions, const Run& r) {
+             float* actions, const Run& r, const Inpaint* ip = nullptr) {
   const int D = P5_EXP_W, F = P5_EXP_MLP, H = c->horizon, L = c->expert_layers, S = P + H;
   vector<ExpertLayer> W(L);
   for (int l = 0; l < L; ++l) {
@@ -436,6 +464,13 @@ void denoise(const p5o_config* c, uint64_t seed, const float* kc, const float* v
     linear(r, H, P5_ACT_D, D, h.data(), aout_w.data(), aout_b.data(), v.data());
     r.point(sp + ".v", v.data(), v.size());
     for (size_t i = 0; i < xt.size(); ++i) xt[i] = xt[i] + r.R(dtb * v[i]);
+    if (ip && ip->K > 0 && ts[s] > ip->t_min) {
+      // the time after step s, accumulated in fp32 as the schedule is
+      const float dt = (float)(-1.0 / (double)c->num_steps);
+      float t = 1.0f;
+      for (int q = 0; q <= s; ++q) t = t + dt;
+      inpaint_step(*ip, noise, xt.data(), (int)xt.size(), t);
+    }
     r.point(sp + ".x", xt.data(), xt.size());
   }
   std::memcpy(actions, xt.data(), xt.size() * 4);
@@ -531,6 +566,20 @@ int p5o_denoise(const p5o_config* c, uint64_t seed, const float* kcache, const f
   if (!check(c) || P < 1) return -1;
   Run r{flags, probe, ctx};
   denoise(c, seed, kcache, vcache, P, noise, actions, r);
+  return 0;
+}
+
+int p5o_denoise_inpaint(const p5o_config* c, uint64_t seed, const float* kcache, const float* vcache, int P,
+                        const float* noise, float* actions, int flags, int fixed, float t_min, const float* known,
+                        const float* corr) {
+  if (!check(c) || P < 1 || fixed < 0 || fixed >= c->horizon || (fixed > 0 && (!known || !corr))) return -1;
+  Run r{flags, nullptr, nullptr};
+  Inpaint ip;
+  ip.K = fixed * P5_ACT_D;
+  ip.t_min = t_min;
+  ip.known = known;
+  ip.corr = corr;
+  denoise(c, seed, kcache, vcache, P, noise, actions, r, &ip);
   return 0;
 }
 

@@ -67,6 +67,12 @@ int p5o_prefill_embedded(const p5o_config* c, uint64_t seed, const float* prefix
 /* denoise: noise [horizon][32] -> actions [horizon][32] */
 int p5o_denoise(const p5o_config* c, uint64_t seed, const float* kcache, const float* vcache, int P,
                 const float* noise, float* actions, int flags, p5o_probe_fn probe, void* ctx);
+/* denoise with soft inpainting: after each Euler step starting above t_min and landing at t, the first
+ * fixed*32 values x_K <- t noise_K + (1 - t) known, and x_U += corr . (x_K,new - x_K,old);
+ * known [fixed][32], corr [(horizon - fixed)*32][fixed*32] */
+int p5o_denoise_inpaint(const p5o_config* c, uint64_t seed, const float* kcache, const float* vcache, int P,
+                        const float* noise, float* actions, int flags, int fixed, float t_min, const float* known,
+                        const float* corr);
 
 #ifdef __cplusplus
 }

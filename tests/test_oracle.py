@@ -124,3 +124,24 @@ def test_text_embedding_matches_oracle(oracle):
     img, tok = oracle.gen_images(4, 0, 1), oracle.gen_tokens(4, 0, 24)
     emb = oracle.prefix_embed(cfg, 2, img, tok)[256:]
     np.testing.assert_array_equal(siglip_ref.text_embedding(2, tok), emb)
+
+
+def test_oracle_inpaint_step_restates_the_formula(oracle):
+    """Soft inpainting in the oracle, one Euler step (lands at t = 0): the first K values become the known
+    actions and the rest move by corr . (x_K,new - x_K,old) from the free step; with t_min >= 1 no step
+    qualifies and the result is the free denoise bit for bit."""
+    cfg = oracle.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1, n_cameras=1, n_text=16)
+    rng = np.random.default_rng(3)
+    kc = rng.standard_normal((1, 40, 256)).astype(np.float32)
+    vc = rng.standard_normal((1, 40, 256)).astype(np.float32)
+    noise = oracle.gen_noise(4, 0)
+    fixed, K = 4, 128
+    known = rng.uniform(-1, 1, (fixed, 32)).astype(np.float32)
+    corr = (rng.standard_normal((50 * 32 - K, K)) * 0.05).astype(np.float32)
+    free = oracle.denoise(cfg, 5, kc, vc, noise)
+    inp = oracle.denoise(cfg, 5, kc, vc, noise, inpaint=(known, corr, -1.0))
+    np.testing.assert_array_equal(inp.ravel()[:K], known.ravel())
+    delta = inp.ravel()[:K].astype(np.float32) - free.ravel()[:K].astype(np.float32)
+    want = free.ravel()[K:] + (corr.astype(np.float64) @ delta.astype(np.float64)).astype(np.float32)
+    np.testing.assert_allclose(inp.ravel()[K:], want, rtol=0, atol=1e-6)
+    np.testing.assert_array_equal(oracle.denoise(cfg, 5, kc, vc, noise, inpaint=(known, corr, 1.0)), free)
