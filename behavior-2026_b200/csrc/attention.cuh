@@ -44,6 +44,7 @@ struct AttnArgs {
   int force_splits; // > 0: the tensor-core path uses this many key splits instead of choosing
   const int* valid1; // optional (tensor-core path): batch item b attends to the first valid1[b] keys of segment 1
   int group1;        // > 0 (tensor-core path): query tokens t < group1 attend to segment-1 keys j < group1 only
+  int ws_half;       // 1 (tensor-core path): ws_o holds fp16 partials already divided by their own l
 };
 
 template <int HD, int NW = 4>
@@ -271,7 +272,8 @@ __global__ void __launch_bounds__(32 * NW) attn_kernel(const AttnArgs a) {
   if (a.pdl) pdl_launch_dependents();
 }
 
-// merge split-KV partials: out = sum_s O_s e^(m_s - M) / sum_s l_s e^(m_s - M); item = (b, row, pair)
+// merge split-KV partials: out = sum_s O_s e^(m_s - M) / sum_s l_s e^(m_s - M); item = (b, row, pair).
+// With ws_half the partials are O_s / l_s in fp16, weighted by l_s e^(m_s - M) instead.
 template <int HD>
 __device__ __forceinline__ void attn_combine_item(const AttnArgs& a, long idx) {
   const int rows_total = a.T * a.G;
@@ -280,7 +282,39 @@ __device__ __forceinline__ void attn_combine_item(const AttnArgs& a, long idx) {
   const int row = br % rows_total, b = br / rows_total;
   float M = -1e30f, L = 0.f, o0 = 0.f, o1 = 0.f;
   constexpr int SMAX = 16;
-  if (a.splits <= SMAX) {
+  if (a.ws_half && a.splits <= SMAX) {
+    const __half2* wh = reinterpret_cast<const __half2*>(a.ws_o);
+    float2 ml[SMAX];
+    __half2 ov[SMAX];
+#pragma unroll
+    for (int k = 0; k < SMAX; ++k) {
+      const long base = ((long)b * a.splits + min(k, a.splits - 1)) * rows_total + row;
+      ml[k] = *reinterpret_cast<const float2*>(a.ws_ml + base * 2);
+      ov[k] = wh[base * (HD / 2) + d2];
+    }
+#pragma unroll
+    for (int k = 0; k < SMAX; ++k) M = k < a.splits ? fmaxf(M, ml[k].x) : M;
+#pragma unroll
+    for (int k = 0; k < SMAX; ++k) {
+      if (k >= a.splits) break;
+      const float w = ml[k].y * __expf(ml[k].x - M);
+      const float2 p = __half22float2(ov[k]);
+      L += w;
+      o0 += p.x * w;
+      o1 += p.y * w;
+    }
+  } else if (a.ws_half) {
+    const __half2* wh = reinterpret_cast<const __half2*>(a.ws_o);
+    for (int s = 0; s < a.splits; ++s) M = fmaxf(M, a.ws_ml[(((long)b * a.splits + s) * rows_total + row) * 2]);
+    for (int s = 0; s < a.splits; ++s) {
+      const long base = ((long)b * a.splits + s) * rows_total + row;
+      const float w = a.ws_ml[base * 2 + 1] * __expf(a.ws_ml[base * 2] - M);
+      const float2 p = __half22float2(wh[base * (HD / 2) + d2]);
+      L += w;
+      o0 += p.x * w;
+      o1 += p.y * w;
+    }
+  } else if (a.splits <= SMAX) {
     // every split's loads in flight together: indices past the split count re-read the last split
     // (weight 0), so the loads carry no conditions; the sums still run in split order
     float2 ml[SMAX], ov[SMAX];

@@ -332,6 +332,15 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
                               pack_bf2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
                               pack_bf2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
                               pack_bf2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+      } else if (a.ws_half) {
+        // split partial O / l in fp16 (half the bytes to drain from this SM), staged like the bf16 rows
+        uint4* dst = reinterpret_cast<uint4*>(smem + r * C::STG_PITCH + col * 2);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_uint4(pack_h2_sat(__uint_as_float(o[8 * q]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                              pack_h2_sat(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                              pack_h2_sat(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                              pack_h2_sat(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
       } else {
         // split partial: staged in the (now idle) Q / K / V buffers, written out by row below
         uint4* dst = reinterpret_cast<uint4*>(smem + r * C::STG_PITCH + col * 4);
@@ -340,13 +349,16 @@ __device__ __forceinline__ void attn_tc_body(const AttnArgs& a, const CUtensorMa
       }
     }
     {
-      // one bulk copy per row (512 B of bf16 output, or the 1 KB fp32 split partial): a thread's own
+      // one bulk copy per row (512 B of bf16 output or fp16 split partial, or the 1 KB fp32 one): a thread's own
       // row is far from its lane neighbours', so direct stores would be 32 segments per warp instruction
       fence_proxy_async_smem();
       asm volatile("bar.sync 1, 256;" ::: "memory");  // both warpgroups' halves of every row are staged
       if (store && g == 0) {
         if (a.splits == 1)
           bulk_store_global(a.out + b * a.o_bstride + (long)tok * a.ldo + hq * C::HD, smem_u32(smem + r * C::STG_PITCH),
+                            C::HD * 2);
+        else if (a.ws_half)
+          bulk_store_global(reinterpret_cast<__half*>(a.ws_o) + base * C::HD, smem_u32(smem + r * C::STG_PITCH),
                             C::HD * 2);
         else
           bulk_store_global(a.ws_o + base * C::HD, smem_u32(smem + r * C::STG_PITCH), C::HD * 4);

@@ -7,6 +7,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -34,6 +35,11 @@ __device__ __forceinline__ bf16 tobf(float v) { return __float2bfloat16_rn(v); }
 __device__ __forceinline__ float rbf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
   __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+// two fp16 values, clamped to the finite fp16 range (+-65504) first
+__device__ __forceinline__ uint32_t pack_h2_sat(float lo, float hi) {
+  __half2 t = __floats2half2_rn(fminf(fmaxf(lo, -65504.f), 65504.f), fminf(fmaxf(hi, -65504.f), 65504.f));
   return *reinterpret_cast<uint32_t*>(&t);
 }
 __device__ __forceinline__ float2 unpack_bf2(uint32_t v) {

@@ -119,6 +119,9 @@ struct pi05_engine {
   bool wide_swap = true;          // few M-tiles: weights-on-M cluster split-K (PI05_WIDE_SWAP=0: normal tiles)
   bool attn_tc = true;           // head_dim-256 MQA attention on tcgen05 (PI05_ATTN_TC=0: the mma.sync kernel)
   bool attn_bwd_pipe = true;     // dQ backward with dS overlapped (PI05_ATTN_BWD_PIPE=0: the one-slot kernel)
+  // split-KV partials of the tensor-core attention as fp16 O / l, half the bytes of fp32 O
+  // (PI05_ATTN_WS_HALF=0: fp32)
+  bool attn_ws_half = true;
   // few-token denoise: adaRMSNorm folded into the q/k/v and gate/up cluster GEMMs, fed by per-token
   // sum-of-squares partials from the producers of x (PI05_FUSE_NORM=0: separate rmsnorm launches)
   bool fuse_norm = true;
@@ -782,6 +785,7 @@ bool attention_tc(pi05_engine* e, const AttnArgs& a0, int batch) {
   if (a.splits > 1) {
     a.ws_o = e->attn_ws_o;
     a.ws_ml = e->attn_ws_ml;
+    a.ws_half = e->attn_ws_half ? 1 : 0;
   }
   CUtensorMap tq, tk1, tv1, tk2, tv2;
   {
@@ -1647,6 +1651,7 @@ bool create(pi05_engine* e) {
   if (const char* s = getenv("PI05_CLUSTER_SPLITK")) e->cluster_splitk = atoi(s) != 0;
   if (const char* s = getenv("PI05_ATTN_TC")) e->attn_tc = atoi(s) != 0;
   if (const char* s = getenv("PI05_ATTN_BWD_PIPE")) e->attn_bwd_pipe = atoi(s) != 0;
+  if (const char* s = getenv("PI05_ATTN_WS_HALF")) e->attn_ws_half = atoi(s) != 0;
   if (const char* s = getenv("PI05_WIDE_SWAP")) e->wide_swap = atoi(s) != 0;
   if (const char* s = getenv("PI05_GEMM_WIDE")) e->gemm_wide = atoi(s) != 0;
   if (const char* s = getenv("PI05_GEMM_PAIR")) e->gemm_pair = atoi(s) != 0;

@@ -296,6 +296,42 @@ def test_attention_engine_splits_match_torch(pn, torch_cuda, T, S, b):
     assert err < 3e-2, err
 
 
+@pytest.mark.parametrize("T,S,b,vscale", [(50, 1018, 1, 1.0), (50, 1018, 2, 1.0), (1, 600, 3, 1.0),
+                                          (50, 1018, 1, 3000.0)])
+def test_attention_half_partials_match_fp32_partials(pn, torch_cuda, monkeypatch, T, S, b, vscale):
+    """Split-KV partials stored as fp16 O / l (the default) against fp32 O (PI05_ATTN_WS_HALF=0).  A
+    partial is a convex combination of V rows, so its fp16 rounding is at most 2^-11 max|V| in absolute
+    terms; after the merge that can move the final bf16 rounding by one ulp (and, where the splits' partials
+    cancel, a small output by a few of its own ulps).  Bound: one bf16 ulp + 2^-10 max|V|; both against
+    fp32 torch within the attention tests' tolerance; values of V up to ~10^4 stay inside the fp16 range."""
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(5 * T + S + b)
+    q = (torch.randn(b, T, 2560, device="cuda", generator=g) * 0.3).bfloat16()
+    k = torch.randn(b, S, 256, device="cuda", generator=g).bfloat16()
+    v = (torch.randn(b, S, 256, device="cuda", generator=g) * vscale).bfloat16()
+    outs = []
+    for half in ("1", "0"):
+        monkeypatch.setenv("PI05_ATTN_WS_HALF", half)
+        eng = pn.Engine(pn.Config.make(siglip_layers=0, gemma_layers=1, num_steps=1), max_batch=1)
+        out = torch.full((b, T, 2048), float("nan"), device="cuda", dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        eng.op_attention(q, k, v, out, 0)
+        eng.sync()
+        eng.close()
+        outs.append(out.float())
+    h, f = outs
+    assert torch.isfinite(h).all()
+    tol = 2.0 ** -7 * torch.maximum(h.abs(), f.abs()) + 2.0 ** -10 * v.float().abs().max()
+    assert ((h - f).abs() <= tol).all(), (h - f).abs().max().item()
+    qh = q[:, :, :2048].float().view(b, T, 8, 256)
+    p = torch.softmax(torch.einsum("bthd,bsd->bhts", qh, k.float()), -1)
+    ref = torch.einsum("bhts,bsd->bthd", p, v.float()).reshape(b, T, 2048)
+    for o in (h, f):
+        assert (o - ref).abs().max().item() < 3e-2 * max(1.0, vscale)
+    print(f"fp16 vs fp32 partials: max diff {(h - f).abs().max().item():.3e}, differing {(h != f).float().mean().item():.3f}; "
+          f"vs torch {(h - ref).abs().max().item():.3e} / {(f - ref).abs().max().item():.3e}")
+
+
 @pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("images", [1, 5, 40])
 def test_siglip_attention_matches_torch(pn, torch_cuda, monkeypatch, tc, images):
