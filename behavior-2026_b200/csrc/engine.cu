@@ -144,6 +144,12 @@ struct pi05_engine {
   float inp_tmin = 0.f;
   float *inp_corr = nullptr, *inp_known = nullptr, *inp_eps = nullptr;
   int* inp_on = nullptr;
+  // KV layer mixing (pi05_set_kv_mix): the expert's layer l attends to a linear combination of the prefix
+  // layers' K (and V); mix_w [2][L][L] and mix_b [2][L][256] (K then V, bf16 values in fp32), the mixed
+  // caches laid out as the prefix cache
+  bool kv_mix = false;
+  float *mix_w = nullptr, *mix_b = nullptr;
+  bf16 *kmix = nullptr, *vmix = nullptr;
   // device staging of pi05_act_batch's camera frames: host frames, resize tap tables, frame jobs
   uint8_t* frame_stage = nullptr;
   size_t frame_stage_bytes = 0;
@@ -1237,7 +1243,8 @@ bool run_denoise_mega(pi05_engine* e) {
 }
 
 bool run_denoise_body(pi05_engine* e, int n) {
-  if (mega_applies(e, n) && !e->probe_fn && !e->plant_fn && e->s0 == 0 && !e->cfg.text_pad_mask && !e->inp_fixed)
+  if (mega_applies(e, n) && !e->probe_fn && !e->plant_fn && e->s0 == 0 && !e->cfg.text_pad_mask && !e->inp_fixed &&
+      !e->kv_mix)
     return run_denoise_mega(e);
   const int H = e->cfg.horizon, T = n * H, D = P5_EXP_W, P = e->P;
   Acts& A = e->A;
@@ -1261,6 +1268,20 @@ bool run_denoise_body(pi05_engine* e, int n) {
   }
   if (inp_k > 0)
     CK(cudaMemcpyAsync(e->inp_eps, xt, (size_t)T * P5_ACT_D * 4, cudaMemcpyDeviceToDevice, e->stream));
+  // KV layer mixing: the mixed caches of this call's samples, once per denoise
+  const bf16* kc = e->kv_mix ? e->kmix : A.kcache;
+  const bf16* vc = e->kv_mix ? e->vmix : A.vcache;
+  if (e->kv_mix) {
+    const int L = e->cfg.gemma_layers;
+    const long items = (long)n * P * (P5_HD / 8);
+    const int LL = L * L;
+    if (!launch(e, kv_mix_kernel, dim3((unsigned)((items + 127) / 128)), dim3(128), 0, false, (const bf16*)A.kcache,
+                e->kmix, (const float*)e->mix_w, (const float*)e->mix_b, L, (long)cache_layer, (long)kv_s0, items) ||
+        !launch(e, kv_mix_kernel, dim3((unsigned)((items + 127) / 128)), dim3(128), 0, false, (const bf16*)A.vcache,
+                e->vmix, (const float*)(e->mix_w + LL), (const float*)(e->mix_b + (size_t)L * P5_HD), L,
+                (long)cache_layer, (long)kv_s0, items))
+      return false;
+  }
   // fused adaRMSNorm: x's producers (action_in, O and down projections) write per-token sums of squares
   // over 16-feature groups; the q/k/v and gate/up projections read x and normalise it on chip
   const bool fnorm = fused_norm_applies(e, n);
@@ -1324,8 +1345,8 @@ bool run_denoise_body(pi05_engine* e, int n) {
       at.out = A.eo;
       at.ldo = P5_QDIM;
       at.o_bstride = (long)H * P5_QDIM;
-      at.k1 = A.kcache + l * cache_layer + kv_s0;
-      at.v1 = A.vcache + l * cache_layer + kv_s0;
+      at.k1 = kc + l * cache_layer + kv_s0;
+      at.v1 = vc + l * cache_layer + kv_s0;
       at.ld1 = P5_HD;
       at.len1 = P;
       at.b1stride = (long)P * P5_HD;
@@ -2751,6 +2772,51 @@ int pi05_set_inpaint(pi05_engine* e, int fixed, float t_min, const float* corr) 
   e->inp_fixed = fixed;
   e->inp_tmin = t_min;
   return pi05_sync(e);
+}
+
+int pi05_set_kv_mix(pi05_engine* e, const float* wk, const float* bk, const float* wv, const float* bv) {
+  if (!e) return PI05_ERR_ARG;
+  const int L = e->cfg.gemma_layers;
+  if (wk && (!bk || !wv || !bv)) {
+    set_err(e, "pi05_set_kv_mix: wk, bk, wv and bv are given together");
+    return PI05_ERR_ARG;
+  }
+  if (wk && L > P5_KV_MIX_MAX_LAYERS) {
+    set_err(e, "pi05_set_kv_mix: at most 18 layers");
+    return PI05_ERR_ARG;
+  }
+  if (wk && e->tr) {
+    set_err(e, "pi05_set_kv_mix: the LoRA step trains without KV layer mixing");
+    return PI05_ERR_STATE;
+  }
+  cudaSetDevice(e->device);
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess) return PI05_ERR_CUDA;
+  // the denoise graphs hold the mixing launches (or their absence): capture them again
+  for (auto& kv : e->denoise_graphs) cudaGraphExecDestroy(kv.second);
+  e->denoise_graphs.clear();
+  e->denoise_launches.clear();
+  e->kv_mix = false;
+  if (!wk) return PI05_OK;
+  const size_t cache = (size_t)L * e->max_batch * e->P * P5_HD * 2;
+  if (!e->kmix && (!dalloc(e, (void**)&e->kmix, cache) || !dalloc(e, (void**)&e->vmix, cache))) return PI05_ERR_CUDA;
+  if (!e->mix_w && (!dalloc(e, (void**)&e->mix_w, (size_t)2 * L * L * 4) ||
+                    !dalloc(e, (void**)&e->mix_b, (size_t)2 * L * P5_HD * 4)))
+    return PI05_ERR_CUDA;
+  // the Dense weights of the mixing are bf16: round on the way in
+  std::vector<float> w((size_t)2 * L * L), b((size_t)2 * L * P5_HD);
+  for (int i = 0; i < L * L; ++i) {
+    w[i] = p5_round_bf(wk[i]);
+    w[L * L + i] = p5_round_bf(wv[i]);
+  }
+  for (int i = 0; i < L * P5_HD; ++i) {
+    b[i] = p5_round_bf(bk[i]);
+    b[(size_t)L * P5_HD + i] = p5_round_bf(bv[i]);
+  }
+  if (cudaMemcpy(e->mix_w, w.data(), w.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(e->mix_b, b.data(), b.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    return PI05_ERR_CUDA;
+  e->kv_mix = true;
+  return PI05_OK;
 }
 
 int pi05_set_inpaint_known(pi05_engine* e, int sample, const float* known) {

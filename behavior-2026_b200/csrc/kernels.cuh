@@ -330,6 +330,42 @@ __global__ void inpaint_kernel(float* xt, const float* eps, const float* known, 
   }
 }
 
+// ---------------------------------------------------------------- KV layer mixing (PiBehavior)
+// dst_l = bf16(bf16(sum_j w[l][j] src_j) + bias[l]) over the prefix cache's L layers, for the samples
+// [s0, s0 + n): one thread per 8 head dims of one (sample, position), holding that slice of every layer
+// in registers, so each cache element is read once and each mixed element written once.  w [L][L] and
+// bias [L][256] hold bf16 values; the sum runs over j in order in fp32 without contraction.
+constexpr int P5_KV_MIX_MAX_LAYERS = 18;
+__global__ void kv_mix_kernel(const bf16* src, bf16* dst, const float* w, const float* bias, int L, long layer_stride,
+                              long first, long items) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= items) return;
+  const long off = first + i * 8;  // element offset inside a layer
+  const int d0 = (int)(off % P5_HD);
+  uint4 x[P5_KV_MIX_MAX_LAYERS];
+#pragma unroll
+  for (int j = 0; j < P5_KV_MIX_MAX_LAYERS; ++j)
+    if (j < L) x[j] = *reinterpret_cast<const uint4*>(src + j * layer_stride + off);
+  for (int l = 0; l < L; ++l) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < P5_KV_MIX_MAX_LAYERS; ++j) {
+      if (j < L) {
+        const float wj = w[l * L + j];
+        float f[8];
+        unpack8(x[j], f);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], __fmul_rn(wj, f[q]));
+      }
+    }
+    const float* b = bias + (long)l * P5_HD + d0;
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o[q] = pack_bf2(rbf(acc[2 * q]) + b[2 * q], rbf(acc[2 * q + 1]) + b[2 * q + 1]);
+    *reinterpret_cast<uint4*>(dst + l * layer_stride + off) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // ---------------------------------------------------------------- time MLP (fp32, one warp per output)
 // y[s][o] = swish(sum_k x[s][k] W[o][k] + b[o]); optional bf16 copy (input of the bf16 modulation Dense)
 __global__ void linear_swish_f32_kernel(const float* x, const bf16* W, const bf16* b, float* y, bf16* ybf, int S,

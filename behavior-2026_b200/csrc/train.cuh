@@ -871,6 +871,10 @@ int pi05_lora_init(pi05_engine* e, const pi05_lora_config* c, uint64_t seed) {
              "(text_pad_mask and prefix_group must be 0)";
     return PI05_ERR_ARG;
   }
+  if (e->kv_mix) {
+    e->err = "pi05_lora_init: the LoRA step trains without KV layer mixing (pi05_set_kv_mix NULL first)";
+    return PI05_ERR_STATE;
+  }
   if (cfg.rank != 16 || cfg.alpha != 32.0f || cfg.micro_batch < 1) {
     e->err = "pi05_lora_init: this build implements rank 16, alpha 32";
     return PI05_ERR_ARG;

@@ -28,7 +28,7 @@ EXPORTS = [
     "pi05_nccl_unique_id", "pi05_lora_attach_nccl", "pi05_lora_world",
     "pi05_read_weights_config", "pi05_lora_schedule_lr", "pi05_lora_get_ema", "pi05_tokenizer_load",
     "pi05_tokenizer_free", "pi05_tokenizer_vocab_size", "pi05_tokenizer_encode", "pi05_tokenize_prompt",
-    "pi05_set_noise_cholesky", "pi05_set_inpaint", "pi05_set_inpaint_known", "pi05_verify_planted",
+    "pi05_set_noise_cholesky", "pi05_set_inpaint", "pi05_set_inpaint_known", "pi05_set_kv_mix", "pi05_verify_planted",
 ]
 
 
@@ -182,6 +182,7 @@ def _load():
     L.pi05_set_noise_cholesky.argtypes = [vp, vp, i32]
     L.pi05_set_inpaint.argtypes = [vp, i32, ctypes.c_float, vp]
     L.pi05_set_inpaint_known.argtypes = [vp, i32, vp]
+    L.pi05_set_kv_mix.argtypes = [vp, vp, vp, vp, vp]
     L.pi05_lora_save_state.argtypes = [vp, ctypes.c_char_p]
     L.pi05_lora_load_state.argtypes = [vp, ctypes.c_char_p]
     return L
@@ -503,6 +504,19 @@ class Engine:
         if c.shape != ((H - fixed) * 32, fixed * 32):
             raise ValueError(f"corr must be [{(H - fixed) * 32}][{fixed * 32}], got {c.shape}")
         self._check(lib.pi05_set_inpaint(self._h, int(fixed), float(t_min), c.ctypes.data))
+
+    def set_kv_mix(self, wk=None, bk=None, wv=None, bv=None):
+        """pi05_set_kv_mix: expert layer l attends to bf16(bf16(sum_j wk[l][j] K_j) + bk[l]) (V likewise);
+        wk, wv [L][L], bk, bv [L][256]; no arguments switch mixing off"""
+        if wk is None:
+            self._check(lib.pi05_set_kv_mix(self._h, None, None, None, None))
+            return
+        L = self.config.gemma_layers
+        arrs = [np.ascontiguousarray(a, np.float32) for a in (wk, bk, wv, bv)]
+        for a, shape in zip(arrs, ((L, L), (L, 256), (L, L), (L, 256))):
+            if a.shape != shape:
+                raise ValueError(f"expected {shape}, got {a.shape}")
+        self._check(lib.pi05_set_kv_mix(self._h, *[a.ctypes.data for a in arrs]))
 
     def set_inpaint_known(self, sample, known):
         """pi05_set_inpaint_known: the known rows [fixed][32] of batch position `sample`, None = free"""

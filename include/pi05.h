@@ -318,6 +318,15 @@ PI05_API int pi05_set_noise_cholesky(pi05_engine* e, const float* L, int dim);
  * inpainting off; 1 <= fixed < horizon (and fixed <= 384).  Every position starts switched off.  A batch
  * position is the sample's index in a pi05_denoise / pi05_infer / pi05_infer_batch call. */
 PI05_API int pi05_set_inpaint(pi05_engine* e, int fixed, float t_min, const float* corr);
+/* KV layer mixing of the denoise (the reference's PiBehavior model, π05_네이티브엔진.md:140: "each action
+ * expert layer sees a linear combination of the VLM's 18 layers' KV", computed as a bf16 einsum plus a bf16
+ * bias): with L = gemma_layers, expert layer l attends to
+ *   K~_l = bf16(bf16(sum_j wk[l][j] K_j) + bk[l]),   V~_l likewise with wv, bv
+ * over the prefix cache's layers j (the action tokens' own K/V are not mixed).  wk, wv f32 [L][L] and bk, bv
+ * f32 [L][256], host memory, rounded to bf16 on the way in; wk = NULL switches mixing off.  The mixed caches
+ * are formed at the start of every pi05_denoise / pi05_infer call (one extra copy of the prefix cache is
+ * allocated on first use); L <= 18; inference only (pi05_lora_init refuses it). */
+PI05_API int pi05_set_kv_mix(pi05_engine* e, const float* wk, const float* bk, const float* wv, const float* bv);
 /* The known rows of batch position `sample`: known f32 [fixed][32] in the model's (normalised) action
  * space, host or device; NULL switches the position back to free denoising. */
 PI05_API int pi05_set_inpaint_known(pi05_engine* e, int sample, const float* known);

@@ -191,8 +191,33 @@ def prefill_embedded(cfg, seed, emb, flags=0, probe=None):
     return k, v
 
 
-def denoise(cfg, seed, kcache, vcache, noise, flags=0, probe=None, inpaint=None):
-    """inpaint = (known [fixed][32], corr [(horizon - fixed) * 32][fixed * 32], t_min): soft inpainting"""
+def round_bf16(x):
+    """float32 -> the nearest bf16 value (round to nearest, ties to even), as float32"""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    return ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)).view(np.float32)
+
+
+def kv_mix(cache, w, b):
+    """KV layer mixing of the PiBehavior model (π05_네이티브엔진.md:140, a bf16 einsum over the prefix cache's
+    layers plus a bf16 bias): out[l] = bf16(bf16(sum_j w[l][j] cache[j]) + b[l]) with w, b rounded to bf16,
+    the sum in fp32 over j in order, each product and sum rounded (no contraction).  cache [L][P][256]."""
+    cache = np.ascontiguousarray(cache, np.float32)
+    w, b = round_bf16(np.asarray(w, np.float32)), round_bf16(np.asarray(b, np.float32))
+    out = np.empty_like(cache)
+    for l in range(cache.shape[0]):
+        acc = np.zeros(cache.shape[1:], np.float32)
+        for j in range(cache.shape[0]):
+            acc = acc + np.float32(w[l, j]) * cache[j]
+        out[l] = round_bf16(round_bf16(acc) + b[l][None, :])
+    return out
+
+
+def denoise(cfg, seed, kcache, vcache, noise, flags=0, probe=None, inpaint=None, mix=None):
+    """inpaint = (known [fixed][32], corr [(horizon - fixed) * 32][fixed * 32], t_min): soft inpainting;
+    mix = (wk, bk, wv, bv): the expert attends to the KV layer mixes of the prefix cache"""
+    if mix is not None:
+        wk, bk, wv, bv = mix
+        kcache, vcache = kv_mix(kcache, wk, bk), kv_mix(vcache, wv, bv)
     kcache = np.ascontiguousarray(kcache, np.float32)
     vcache = np.ascontiguousarray(vcache, np.float32)
     noise = np.ascontiguousarray(noise, np.float32)
@@ -220,7 +245,7 @@ def valid_prefix(cfg, tokens, flags=0):
     return lib().p5o_valid_prefix(ctypes.byref(cfg), _p(tokens, ctypes.c_int32), flags)
 
 
-def infer(cfg, seed, images, tokens, noise, flags=0, probe=None, inpaint=None):
+def infer(cfg, seed, images, tokens, noise, flags=0, probe=None, inpaint=None, mix=None):
     k, v = prefill(cfg, seed, images, tokens, flags, probe)
     s = valid_prefix(cfg, tokens, flags)  # with TEXT_PAD_MASK the padding's cache rows are left out
-    return denoise(cfg, seed, k[:, :s], v[:, :s], noise, flags, probe, inpaint)
+    return denoise(cfg, seed, k[:, :s], v[:, :s], noise, flags, probe, inpaint, mix)

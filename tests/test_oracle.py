@@ -145,3 +145,21 @@ def test_oracle_inpaint_step_restates_the_formula(oracle):
     want = free.ravel()[K:] + (corr.astype(np.float64) @ delta.astype(np.float64)).astype(np.float32)
     np.testing.assert_allclose(inp.ravel()[K:], want, rtol=0, atol=1e-6)
     np.testing.assert_array_equal(oracle.denoise(cfg, 5, kc, vc, noise, inpaint=(known, corr, 1.0)), free)
+
+
+def test_oracle_kv_mix(oracle):
+    """The oracle's KV layer mixing: bf16 rounding equals torch's, identity weights with zero bias give the
+    cache back, and a random mix is within two bf16 roundings of the float64 einsum."""
+    import torch
+
+    rng = np.random.default_rng(7)
+    x = (rng.standard_normal(100000) * 10.0 ** rng.integers(-3, 4, 100000)).astype(np.float32)
+    np.testing.assert_array_equal(oracle.round_bf16(x), torch.from_numpy(x).bfloat16().float().numpy())
+    cache = oracle.round_bf16(rng.standard_normal((4, 30, 256)).astype(np.float32))
+    np.testing.assert_array_equal(oracle.kv_mix(cache, np.eye(4), np.zeros((4, 256))), cache)
+    w = oracle.round_bf16(rng.normal(0, 0.5, (4, 4)).astype(np.float32))
+    b = oracle.round_bf16(rng.normal(0, 0.1, (4, 256)).astype(np.float32))
+    want = np.einsum("lj,jpd->lpd", w.astype(np.float64), cache.astype(np.float64)) + b[:, None, :]
+    got = oracle.kv_mix(cache, w, b)
+    scale = np.einsum("lj,jpd->lpd", np.abs(w).astype(np.float64), np.abs(cache).astype(np.float64)) + np.abs(b)[:, None]
+    assert (np.abs(got - want) <= 2 * 2.0 ** -8 * scale + 1e-30).all()
