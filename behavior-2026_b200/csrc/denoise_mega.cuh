@@ -64,6 +64,7 @@ struct MegaArgs {
   float* ws;      // GEMM partial tiles [unit][128][64]
   float* attn_o;  // attention split partials
   float* attn_ml;
+  int attn_half;  // attention split partials as fp16 O / l (as the per-kernel path stores them)
   unsigned* ctr;  // [0] grid barrier, then per-tile counters; zero at launch
   int* status;
   const bf16* mods;  // [steps][NM][3][1024] adaRMS scale, shift, gate
@@ -467,6 +468,7 @@ __global__ void __launch_bounds__(MegaCfg::THREADS, 1) denoise_mega_kernel(const
       at.keys_per_split = a.attn_tps * AttnTcCfg::KT;
       at.ws_o = a.attn_o;
       at.ws_ml = a.attn_ml;
+      at.ws_half = a.attn_half;
       if (cta >= c.attn_first) {
         const int u = cta - c.attn_first;
         const CUtensorMap* lm = a.maps + l * C::NMAPS_LAYER;

@@ -1205,6 +1205,7 @@ bool run_denoise_mega(pi05_engine* e) {
   m.ws = e->gemm_ws;
   m.attn_o = e->attn_ws_o;
   m.attn_ml = e->attn_ws_ml;
+  m.attn_half = e->attn_ws_half ? 1 : 0;
   m.ctr = e->mega_ctr;
   m.status = e->d_status;
   m.mods = e->mods;
