@@ -81,3 +81,12 @@ def test_lora_schedule_matches_optax_warmup_cosine(pn):
     flat = pn.LoraConfig()
     pn.lib.pi05_lora_default_config(ctypes.byref(flat))
     assert pn.lora_schedule_lr(flat, 0) == pn.lora_schedule_lr(flat, 5000) == np.float32(1e-4)
+
+
+def test_engine_setters_reject_a_null_engine_without_gpu(pn):
+    """The PiBehavior controls check their engine before touching the device."""
+    z = np.zeros(16, np.float32)
+    assert pn.lib.pi05_set_inpaint(None, 4, 0.3, z.ctypes.data) == -1
+    assert pn.lib.pi05_set_inpaint_known(None, 0, z.ctypes.data) == -1
+    assert pn.lib.pi05_set_kv_mix(None, z.ctypes.data, z.ctypes.data, z.ctypes.data, z.ctypes.data) == -1
+    assert pn.lib.pi05_set_noise_cholesky(None, z.ctypes.data, 4) == -1
