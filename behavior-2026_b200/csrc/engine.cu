@@ -110,6 +110,12 @@ struct pi05_engine {
   int prefix_n = 0;  // batch whose prefix cache is valid
   std::map<int, cudaGraphExec_t> denoise_graphs, prefill_graphs;
   std::map<int, long> denoise_launches, prefill_launches;
+  // pi05_prefill_embeds: the text part of the prefix from the caller's embeddings [max_batch][n_text][2048]
+  // instead of token ids, with its own prefill graphs
+  bf16* text_emb = nullptr;
+  bool text_from_emb = false;
+  std::map<int, cudaGraphExec_t> prefill_emb_graphs;
+  std::map<int, long> prefill_emb_launches;
   long launches = 0;  // kernels enqueued (counted at capture time)
   struct Trainer* tr = nullptr;  // LoRA train state (train.cuh), created by pi05_lora_init
   bool cluster_splitk = true;    // few-token split-K GEMMs reduce inside a cluster (PI05_CLUSTER_SPLITK=0: tickets)
@@ -1090,7 +1096,12 @@ bool run_prefill_body(pi05_engine* e, int n) {
               e->cfg.n_cameras * P5_SIG_TOK, e->d_valid + e->s0))
     return false;
   if (!run_siglip(e, n)) return false;
-  if (e->cfg.n_text > 0 &&
+  if (e->cfg.n_text > 0 && e->text_from_emb) {
+    if (!launch(e, copy_text_emb_kernel, dim3(e->cfg.n_text, n), dim3(256), 0, true,
+                (const bf16*)e->text_emb + (size_t)e->s0 * e->cfg.n_text * P5_GEM_W, e->A.px, e->cfg.n_text, e->P,
+                e->cfg.n_cameras * P5_SIG_TOK))
+      return false;
+  } else if (e->cfg.n_text > 0 &&
       !launch(e, embed_text_kernel, dim3(e->cfg.n_text, n), dim3(256), 0, true,
               (const int32_t*)e->A.tokens + (size_t)e->s0 * e->cfg.n_text,
               (const bf16*)e->embed, e->A.px, e->cfg.n_text, e->P, e->cfg.n_cameras * P5_SIG_TOK))
@@ -1481,10 +1492,12 @@ int fail_code(pi05_engine* e) {
 // result does not depend on the batch it came in.
 bool prefill_resident(pi05_engine* e, int n) {
   if (!qkv_interleave_prepare(e)) return false;
-  if (!e->cfg.batch_invariant) return run_graph(e, e->prefill_graphs, e->prefill_launches, n, run_prefill_body);
+  auto& graphs = e->text_from_emb ? e->prefill_emb_graphs : e->prefill_graphs;
+  auto& launches = e->text_from_emb ? e->prefill_emb_launches : e->prefill_launches;
+  if (!e->cfg.batch_invariant) return run_graph(e, graphs, launches, n, run_prefill_body);
   for (int b = 0; b < n; ++b) {
     e->s0 = b;
-    const bool ok = run_graph(e, e->prefill_graphs, e->prefill_launches, 1, run_prefill_body);
+    const bool ok = run_graph(e, graphs, launches, 1, run_prefill_body);
     e->s0 = 0;
     if (!ok) return false;
   }
@@ -1809,6 +1822,7 @@ void pi05_destroy(pi05_engine* e) {
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (auto& kv : e->denoise_graphs) cudaGraphExecDestroy(kv.second);
   for (auto& kv : e->prefill_graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : e->prefill_emb_graphs) cudaGraphExecDestroy(kv.second);
   if (e->tr) dp_release(e->tr->dp);
   delete e->tr;
   for (void* p : e->allocs) cudaFree(p);
@@ -2134,6 +2148,33 @@ int pi05_prefill(pi05_engine* e, int n, const uint8_t* images, const int32_t* to
   if (!copy_in(e, e->A.images, images, ib)) return PI05_ERR_CUDA;
   if (e->cfg.n_text > 0 && !copy_in(e, e->A.tokens, tokens, (size_t)n * e->cfg.n_text * 4)) return PI05_ERR_CUDA;
   if (!prefill_resident(e, n)) return fail_code(e);
+  e->prefix_n = n;
+  return PI05_OK;
+}
+
+int pi05_prefill_embeds(pi05_engine* e, int n, const uint8_t* images, const uint16_t* text_emb) {
+  if (!e || n < 1 || n > e->max_batch || !images || (e->cfg.n_text > 0 && !text_emb)) {
+    if (e) e->err = "pi05_prefill_embeds: bad arguments";
+    return PI05_ERR_ARG;
+  }
+  if (e->cfg.text_pad_mask) {
+    e->err = "pi05_prefill_embeds: the prompt padding mask reads token ids (text_pad_mask must be 0)";
+    return PI05_ERR_ARG;
+  }
+  if (!e->weights_ready) {
+    e->err = "pi05_prefill_embeds: weights not loaded";
+    return PI05_ERR_STATE;
+  }
+  cudaSetDevice(e->device);
+  const size_t tb = (size_t)e->cfg.n_text * P5_GEM_W * 2;  // one sample's text rows
+  if (tb > 0 && !e->text_emb && !dalloc(e, (void**)&e->text_emb, (size_t)e->max_batch * tb)) return PI05_ERR_CUDA;
+  const size_t ib = (size_t)n * e->cfg.n_cameras * P5_IMG * P5_IMG * 3;
+  if (!copy_in(e, e->A.images, images, ib)) return PI05_ERR_CUDA;
+  if (tb > 0 && !copy_in(e, e->text_emb, text_emb, (size_t)n * tb)) return PI05_ERR_CUDA;
+  e->text_from_emb = true;
+  const bool ok = prefill_resident(e, n);
+  e->text_from_emb = false;
+  if (!ok) return fail_code(e);
   e->prefix_n = n;
   return PI05_OK;
 }

@@ -199,6 +199,17 @@ __global__ void embed_text_kernel(const int32_t* tokens, const bf16* table, bf16
   pdl_launch_dependents();
 }
 
+// The text part of the prefix given as embeddings (pi05_prefill_embeds): rows [img_tokens, img_tokens +
+// n_text) of each sample's prefix copied from the caller's bf16 rows; grid (n_text, n), 256 threads x 8.
+__global__ void copy_text_emb_kernel(const bf16* emb, bf16* x, int n_text, int P, int img_tokens) {
+  const int b = blockIdx.y, i = blockIdx.x;
+  pdl_wait();
+  const uint4* src = reinterpret_cast<const uint4*>(emb + ((long)b * n_text + i) * P5_GEM_W);
+  uint4* dst = reinterpret_cast<uint4*>(x + ((long)b * P + img_tokens + i) * P5_GEM_W);
+  for (int d = threadIdx.x; d < P5_GEM_W / 8; d += blockDim.x) dst[d] = src[d];
+  pdl_launch_dependents();
+}
+
 // ---------------------------------------------------------------- action projections (fp32 math)
 // action_in_proj: y[t][o] = R(sum_k x[t][k] W[o][k] + b[o]), x fp32 [T][32] (nnx.Linear in fp32)
 // ss_out (optional): per-token partial sums of squares of the stored outputs, one per 16 output

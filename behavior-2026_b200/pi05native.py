@@ -28,7 +28,7 @@ EXPORTS = [
     "pi05_nccl_unique_id", "pi05_lora_attach_nccl", "pi05_lora_world",
     "pi05_read_weights_config", "pi05_lora_schedule_lr", "pi05_lora_get_ema", "pi05_tokenizer_load",
     "pi05_tokenizer_free", "pi05_tokenizer_vocab_size", "pi05_tokenizer_encode", "pi05_tokenize_prompt",
-    "pi05_set_noise_cholesky", "pi05_set_inpaint", "pi05_set_inpaint_known", "pi05_set_kv_mix", "pi05_verify_planted",
+    "pi05_set_noise_cholesky", "pi05_set_inpaint", "pi05_set_inpaint_known", "pi05_set_kv_mix", "pi05_prefill_embeds", "pi05_verify_planted",
 ]
 
 
@@ -183,6 +183,7 @@ def _load():
     L.pi05_set_inpaint.argtypes = [vp, i32, ctypes.c_float, vp]
     L.pi05_set_inpaint_known.argtypes = [vp, i32, vp]
     L.pi05_set_kv_mix.argtypes = [vp, vp, vp, vp, vp]
+    L.pi05_prefill_embeds.argtypes = [vp, i32, vp, vp]
     L.pi05_lora_save_state.argtypes = [vp, ctypes.c_char_p]
     L.pi05_lora_load_state.argtypes = [vp, ctypes.c_char_p]
     return L
@@ -266,6 +267,19 @@ class Engine:
         pi, ki = _ptr(images, np.uint8)
         pt, kt = _ptr(tokens, np.int32)
         self._check(lib.pi05_prefill(self._h, n, pi, pt))
+
+    def prefill_embeds(self, images, text_emb):
+        """pi05_prefill_embeds: the prefix from the images and the text part's embeddings ([n][n_text][2048],
+        bf16 bits as uint16, or float32 rounded to bf16 here)"""
+        n = images.shape[0]
+        emb = np.asarray(text_emb)
+        if emb.dtype != np.uint16:
+            emb = f32_to_bf16_bits(emb)
+        if emb.shape != (n, self.config.n_text, 2048):
+            raise ValueError(f"text_emb must be [{n}][{self.config.n_text}][2048], got {emb.shape}")
+        emb = np.ascontiguousarray(emb)
+        pi, ki = _ptr(images, np.uint8)
+        self._check(lib.pi05_prefill_embeds(self._h, n, pi, emb.ctypes.data))
 
     def set_prefix_cache(self, k_bits, v_bits):
         """k_bits/v_bits: uint16 (bf16 bit patterns) [n][layers][P][256]."""

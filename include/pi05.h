@@ -97,6 +97,13 @@ PI05_API int pi05_read_weights_config(const char* path, pi05_config* c);
 /* Prefix: SigLIP over the camera images, text embedding, Gemma-2B prefill; fills the per-sample
  * bf16 KV cache.  (Reference: the per-board prefix CUDA graph, π05_네이티브엔진.md:298.) */
 PI05_API int pi05_prefill(pi05_engine* e, int n, const uint8_t* images, const int32_t* tokens);
+/* pi05_prefill with the text part of the prefix given as embeddings instead of token ids: text_emb bf16
+ * (uint16 bits) [n][n_text][2048], the Gemma prefix's rows after the image tokens, already
+ * scaled as the model wants them (the token path's rows are embedding * sqrt(2048) rounded to bf16).  For
+ * callers whose prompt is not a sentence: the reference's PiBehavior model replaced it with learned task
+ * embeddings and stage tokens (π05_네이티브엔진.md:136-137), which the caller forms.  Host or device
+ * pointers; text_pad_mask must be 0 (it reads token ids). */
+PI05_API int pi05_prefill_embeds(pi05_engine* e, int n, const uint8_t* images, const uint16_t* text_emb);
 /* Install a prefix KV cache directly (the expert-only denoise workload). */
 PI05_API int pi05_set_prefix_cache(pi05_engine* e, int n, const uint16_t* k, const uint16_t* v);
 /* Read one layer of one sample's prefix cache (K and V, [P][256] bf16 bits each). */
