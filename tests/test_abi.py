@@ -90,3 +90,4 @@ def test_engine_setters_reject_a_null_engine_without_gpu(pn):
     assert pn.lib.pi05_set_inpaint_known(None, 0, z.ctypes.data) == -1
     assert pn.lib.pi05_set_kv_mix(None, z.ctypes.data, z.ctypes.data, z.ctypes.data, z.ctypes.data) == -1
     assert pn.lib.pi05_set_noise_cholesky(None, z.ctypes.data, 4) == -1
+    assert pn.lib.pi05_prefill_embeds(None, 1, z.ctypes.data, z.ctypes.data) == -1
